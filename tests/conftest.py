@@ -1,0 +1,30 @@
+import os
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a)")
+
+
+@pytest.fixture(scope="session")
+def golden_trees():
+    import numpy as np
+    return np.load(os.path.join(ROOT, "tests", "golden", "trees.npz"))
+
+
+@pytest.fixture(scope="session")
+def golden_misc():
+    import numpy as np
+    return np.load(os.path.join(ROOT, "tests", "golden", "misc.npz"))
+
+
+@pytest.fixture(scope="session")
+def golden_attention():
+    import numpy as np
+    return np.load(os.path.join(ROOT, "tests", "golden", "attention.npz"))
