@@ -1,0 +1,46 @@
+// Error reporting and device queries shared by the C-ABI entry points.
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace ddt {
+
+static thread_local char g_last_error[512] = "";
+
+int set_error(int status, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+    va_end(ap);
+    return status;
+}
+
+int check_launch(const char* what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_error(DDT_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+    return DDT_OK;
+}
+
+}  // namespace ddt
+
+extern "C" const char* ddt_last_error(void) { return ddt::g_last_error; }
+
+extern "C" int ddt_abi_version(void) { return 1; }
+
+extern "C" int ddt_sm_count(int device) {
+    static std::mutex mu;
+    static int cache[64] = {0};
+    if (device < 0 || device >= 64) return 0;
+    std::lock_guard<std::mutex> lock(mu);
+    if (cache[device] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) {
+            cudaGetLastError();
+            return 0;
+        }
+        cache[device] = n;
+    }
+    return cache[device];
+}

@@ -1,0 +1,833 @@
+// Kernel (1): DDTree tree build on sm_100a.
+//
+// Restates build_ddtree_tree (ddtree.py:114-196) as one launch:
+//   phase A  (rows x chunks CTAs)  per chunk of a draft row: max, sum of
+//            exp, and the chunk's top-k candidates by a block radix select on
+//            64-bit keys (value, then lower token id) - ddtree.py:136-138;
+//   phase B  (last CTA of a row)   merge the chunk candidates into the row's
+//            top-k, sort it, log-normaliser, lp = top - log_z  (ddtree.py:139);
+//   phase C  (last CTA overall)    the best-first expansion, restated exactly
+//            with one warp doing the frontier arg-min each step
+//            (ddtree.py:146-177), then parents / depths / tokens, the packed
+//            ancestor bitmask (ddtree.py:181-188) and the verify ids /
+//            positions (ddtree.py:233-242).
+// The hand-off between phases uses the "last block done" pattern (a fence
+// and an atomic counter); no CTA ever waits on another.
+
+#include <cstdio>
+
+#include "common.cuh"
+
+namespace ddt {
+namespace tree {
+
+constexpr int kThreads = 512;
+constexpr int kWarps = kThreads / 32;
+constexpr int kValsPerThread = 32;
+constexpr int kMaxChunk = kThreads * kValsPerThread;  // 16384 elements
+constexpr int kCandCap = 2048;
+constexpr int kMaxRows = 32;
+constexpr int kMaxBudget = 1024;
+constexpr int kMergeCap = 16384;  // chunks * topk keys held by the merging CTA
+
+struct SelectScratch {
+    uint32_t hist[256];
+    unsigned long long prefix;
+    int need;
+    int done;
+    int count;
+    int flag;
+};
+
+// Workspace layout (all offsets 256-byte aligned).
+struct WsLayout {
+    size_t row_cnt, done_cnt, part_m, part_s, part_keys, top_ids, top_lp, total;
+};
+
+__host__ __device__ inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+__host__ __device__ inline WsLayout ws_layout(int64_t rows, int64_t chunks, int64_t topk) {
+    WsLayout w;
+    size_t o = 0;
+    w.row_cnt = o;
+    o = align256(o + sizeof(uint32_t) * kMaxRows);
+    w.done_cnt = o;
+    o = align256(o + sizeof(uint32_t) * 4);
+    w.part_m = o;
+    o = align256(o + sizeof(float) * rows * chunks);
+    w.part_s = o;
+    o = align256(o + sizeof(double) * rows * chunks);
+    w.part_keys = o;
+    o = align256(o + sizeof(uint64_t) * rows * chunks * topk);
+    w.top_ids = o;
+    o = align256(o + sizeof(int64_t) * rows * topk);
+    w.top_lp = o;
+    o = align256(o + sizeof(float) * rows * topk);
+    w.total = o;
+    return w;
+}
+
+__host__ inline void choose_chunks(int64_t rows, int64_t vocab, int64_t topk, int sms, int64_t* chunks,
+                                   int64_t* chunk_len) {
+    int64_t c_min = ceil_div(vocab, kMaxChunk);
+    int64_t c_fill = rows > 0 ? (int64_t)sms / rows : 1;
+    int64_t c_small = ceil_div(vocab, 2048);
+    int64_t c = c_fill < c_small ? c_fill : c_small;
+    if (c < c_min) c = c_min;
+    if (c < 1) c = 1;
+    while (c > c_min && c * topk > kMergeCap) --c;
+    int64_t len = ceil_div(vocab, c);
+    len = (len + 7) & ~int64_t(7);
+    *chunk_len = len;
+    *chunks = ceil_div(vocab, len);
+}
+
+// ---------------------------------------------------------------------------
+// block-wide helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float block_max(float v, float* red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(DDT_FULL_MASK, v, o));
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+        v = lane < kWarps ? red[lane] : -INFINITY;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(DDT_FULL_MASK, v, o));
+        if (lane == 0) red[0] = v;
+    }
+    __syncthreads();
+    return red[0];
+}
+
+__device__ __forceinline__ double block_sum_d(double v, double* red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(DDT_FULL_MASK, v, o);
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+        v = lane < kWarps ? red[lane] : 0.0;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(DDT_FULL_MASK, v, o);
+        if (lane == 0) red[0] = v;
+    }
+    __syncthreads();
+    return red[0];
+}
+
+// Warp 0 picks the 8-bit bin that holds the need-th largest key.
+__device__ __forceinline__ void pick_bin(SelectScratch* s, int shift) {
+    const int lane = threadIdx.x & 31;
+    // lane l owns bins 255-8l ... 248-8l (descending)
+    uint32_t c[8];
+    uint32_t tot = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        c[j] = s->hist[255 - (lane * 8 + j)];
+        tot += c[j];
+    }
+    uint32_t incl = tot;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        uint32_t t = __shfl_up_sync(DDT_FULL_MASK, incl, o);
+        if (lane >= o) incl += t;
+    }
+    uint32_t before = incl - tot;
+    const uint32_t need = (uint32_t)s->need;
+    bool mine = before < need && need <= incl;
+    if (mine) {
+        uint32_t acc = before;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            if (acc < need && need <= acc + c[j]) {
+                const uint32_t bin = 255 - (lane * 8 + j);
+                s->prefix |= (unsigned long long)bin << shift;
+                s->need = (int)(need - acc);
+                s->done = (c[j] == need - acc) ? 1 : 0;
+            }
+            acc += c[j];
+        }
+    }
+}
+
+// K-th largest of n distinct 64-bit keys held in shared or global memory.
+// Returns T with "key >= T" selecting exactly K keys.  All threads call it.
+__device__ unsigned long long block_kth_largest(const unsigned long long* keys, int n, int K, SelectScratch* s) {
+    if (threadIdx.x == 0) {
+        s->prefix = 0ull;
+        s->need = K;
+        s->done = 0;
+    }
+    unsigned long long mask = 0ull;
+    for (int shift = 56; shift >= 0; shift -= 8) {
+        for (int i = threadIdx.x; i < 256; i += kThreads) s->hist[i] = 0;
+        __syncthreads();
+        const unsigned long long prefix = s->prefix;
+        for (int i = threadIdx.x; i < n; i += kThreads) {
+            const unsigned long long k = keys[i];
+            if ((k & mask) == prefix) atomicAdd(&s->hist[(k >> shift) & 255u], 1u);
+        }
+        __syncthreads();
+        if (threadIdx.x < 32) pick_bin(s, shift);
+        __syncthreads();
+        mask |= 0xffull << shift;
+        if (s->done) break;
+    }
+    const unsigned long long t = s->prefix;
+    __syncthreads();
+    return t;
+}
+
+// Same, over keys produced by key_at(j), j < kValsPerThread, per thread (0 = empty).
+template <typename KeyAt>
+__device__ unsigned long long block_kth_largest_regs(KeyAt key_at, int K, SelectScratch* s) {
+    if (threadIdx.x == 0) {
+        s->prefix = 0ull;
+        s->need = K;
+        s->done = 0;
+    }
+    unsigned long long mask = 0ull;
+    for (int shift = 56; shift >= 0; shift -= 8) {
+        for (int i = threadIdx.x; i < 256; i += kThreads) s->hist[i] = 0;
+        __syncthreads();
+        const unsigned long long prefix = s->prefix;
+#pragma unroll
+        for (int j = 0; j < kValsPerThread; ++j) {
+            const unsigned long long k = key_at(j);
+            if (k != 0ull && (k & mask) == prefix) atomicAdd(&s->hist[(k >> shift) & 255u], 1u);
+        }
+        __syncthreads();
+        if (threadIdx.x < 32) pick_bin(s, shift);
+        __syncthreads();
+        mask |= 0xffull << shift;
+        if (s->done) break;
+    }
+    const unsigned long long t = s->prefix;
+    __syncthreads();
+    return t;
+}
+
+// Descending bitonic sort of P (power of two) keys in shared memory.
+__device__ void bitonic_sort_desc(unsigned long long* a, int P) {
+    for (int k = 2; k <= P; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = threadIdx.x; i < P; i += kThreads) {
+                const int ixj = i ^ j;
+                if (ixj > i) {
+                    const bool desc = (i & k) == 0;
+                    const unsigned long long x = a[i], y = a[ixj];
+                    if (desc ? (x < y) : (x > y)) {
+                        a[i] = y;
+                        a[ixj] = x;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+
+__device__ __forceinline__ unsigned long long make_key(float v, int64_t idx) {
+    return ((unsigned long long)ord_f32(v) << 32) | (unsigned long long)(0xffffffffu - (uint32_t)idx);
+}
+__device__ __forceinline__ int64_t key_index(unsigned long long k) {
+    return (int64_t)(0xffffffffu - (uint32_t)(k & 0xffffffffull));
+}
+__device__ __forceinline__ float key_value(unsigned long long k) { return unord_f32((uint32_t)(k >> 32)); }
+
+// ---------------------------------------------------------------------------
+// phase C: best-first expansion (ddtree.py:146-189)
+// ---------------------------------------------------------------------------
+struct ExpandSmem {
+    float* lp;           // [rows * topk]
+    double* f_logw;      // frontier: path score
+    int32_t* f_parent;   //           parent node index
+    int32_t* f_dr;       //           depth << 16 | rank
+    int32_t* n_parent;   // node i: parent        (i in [0, budget])
+    int32_t* n_dr;       //         depth << 16 | rank
+    int32_t* scalars;    // [4]
+};
+
+__host__ __device__ inline size_t expand_smem_bytes(int64_t rows, int64_t topk, int64_t budget) {
+    size_t o = 0;
+    o += align256(sizeof(float) * rows * topk);
+    o += align256(sizeof(double) * (budget + 1));
+    o += align256(sizeof(int32_t) * (budget + 1)) * 4;
+    o += 256;
+    return o;
+}
+
+__device__ inline ExpandSmem carve_expand(unsigned char* base, int64_t rows, int64_t topk, int64_t budget) {
+    ExpandSmem e;
+    size_t o = 0;
+    e.lp = reinterpret_cast<float*>(base + o);
+    o += align256(sizeof(float) * rows * topk);
+    e.f_logw = reinterpret_cast<double*>(base + o);
+    o += align256(sizeof(double) * (budget + 1));
+    e.f_parent = reinterpret_cast<int32_t*>(base + o);
+    o += align256(sizeof(int32_t) * (budget + 1));
+    e.f_dr = reinterpret_cast<int32_t*>(base + o);
+    o += align256(sizeof(int32_t) * (budget + 1));
+    e.n_parent = reinterpret_cast<int32_t*>(base + o);
+    o += align256(sizeof(int32_t) * (budget + 1));
+    e.n_dr = reinterpret_cast<int32_t*>(base + o);
+    o += align256(sizeof(int32_t) * (budget + 1));
+    e.scalars = reinterpret_cast<int32_t*>(base + o);
+    return e;
+}
+
+// Ranks tuple of a frontier slot (ddtree.py:148): ranks of its parent's path, then its own rank.
+__device__ int slot_path(const ExpandSmem& e, int slot, int* out) {
+    const int dr = e.f_dr[slot];
+    const int depth = dr >> 16;
+    out[depth - 1] = dr & 0xffff;
+    int node = e.f_parent[slot];
+    for (int k = depth - 2; k >= 0; --k) {
+        out[k] = e.n_dr[node] & 0xffff;
+        node = e.n_parent[node];
+    }
+    return depth;
+}
+
+// Python tuple order of the ranks tuples of two slots.
+__device__ bool slot_tuple_less(const ExpandSmem& e, int a, int b) {
+    int pa[kMaxRows], pb[kMaxRows];
+    const int na = slot_path(e, a, pa), nb = slot_path(e, b, pb);
+    const int n = na < nb ? na : nb;
+    for (int k = 0; k < n; ++k)
+        if (pa[k] != pb[k]) return pa[k] < pb[k];
+    return na < nb;
+}
+
+// Runs on all threads of one CTA.  lp / ids: [rows, topk] in global memory.
+__device__ void expand_tree(const float* lp_g, const int64_t* ids_g, int rows, int topk, int budget,
+                            const int64_t* root_token, int64_t start, const ddt_tree_outputs out, ExpandSmem e) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int i = tid; i < rows * topk; i += kThreads) e.lp[i] = __ldcg(lp_g + i);
+    __syncthreads();
+
+    if (warp == 0) {
+        int fsize = 1;
+        if (lane == 0) {
+            e.f_logw[0] = (double)e.lp[0];
+            e.f_parent[0] = 0;
+            e.f_dr[0] = (1 << 16) | 0;
+            e.n_parent[0] = -1;
+            e.n_dr[0] = 0;
+        }
+        __syncwarp();
+        int count = 0;
+        while (count < budget && fsize > 0) {
+            // lane-local minimum of (-logw, ranks tuple)
+            unsigned long long best_u = ~0ull;
+            int best_s = -1;
+            for (int s = lane; s < fsize; s += 32) {
+                const unsigned long long u = ord_f64(-e.f_logw[s]);
+                if (u < best_u || (u == best_u && best_s >= 0 && slot_tuple_less(e, s, best_s))) {
+                    best_u = u;
+                    best_s = s;
+                }
+            }
+            const uint32_t hi = __reduce_min_sync(DDT_FULL_MASK, (uint32_t)(best_u >> 32));
+            const uint32_t lo =
+                __reduce_min_sync(DDT_FULL_MASK, ((uint32_t)(best_u >> 32) == hi) ? (uint32_t)best_u : 0xffffffffu);
+            const unsigned long long umin = ((unsigned long long)hi << 32) | lo;
+            const uint32_t tied = __ballot_sync(DDT_FULL_MASK, best_s >= 0 && best_u == umin);
+            int w;
+            if (__popc(tied) == 1) {
+                w = __shfl_sync(DDT_FULL_MASK, best_s, __ffs(tied) - 1);
+            } else {
+                // exact float64 tie across lanes: decide by the ranks tuples
+                int pick = -1;
+                if (lane == 0) {
+                    for (int s = 0; s < fsize; ++s) {
+                        if (ord_f64(-e.f_logw[s]) != umin) continue;
+                        if (pick < 0 || slot_tuple_less(e, s, pick)) pick = s;
+                    }
+                }
+                w = __shfl_sync(DDT_FULL_MASK, pick, 0);
+            }
+            if (lane == 0) {
+                const double logw = e.f_logw[w];
+                const int parent = e.f_parent[w];
+                const int dr = e.f_dr[w];
+                const int depth = dr >> 16, rank = dr & 0xffff;
+                const int cur = count + 1;
+                e.n_parent[cur] = parent;
+                e.n_dr[cur] = dr;
+                const bool sib = rank + 1 < topk;
+                const bool child = depth < rows;
+                int nf = fsize;
+                if (sib) {
+                    const double a = (double)e.lp[(depth - 1) * topk + rank];
+                    const double b = (double)e.lp[(depth - 1) * topk + rank + 1];
+                    const double s = __dadd_rn(__dadd_rn(logw, -a), b);
+                    e.f_logw[w] = s;
+                    e.f_parent[w] = parent;
+                    e.f_dr[w] = (depth << 16) | (rank + 1);
+                }
+                if (child) {
+                    const double c = __dadd_rn(logw, (double)e.lp[depth * topk]);
+                    const int slot = sib ? nf++ : w;
+                    e.f_logw[slot] = c;
+                    e.f_parent[slot] = cur;
+                    e.f_dr[slot] = (depth + 1) << 16;
+                }
+                if (!sib && !child) {
+                    nf -= 1;
+                    if (w != nf) {
+                        e.f_logw[w] = e.f_logw[nf];
+                        e.f_parent[w] = e.f_parent[nf];
+                        e.f_dr[w] = e.f_dr[nf];
+                    }
+                }
+                e.scalars[0] = nf;
+            }
+            __syncwarp();
+            fsize = *(volatile int32_t*)&e.scalars[0];
+            count += 1;
+        }
+        if (lane == 0) e.scalars[1] = count;
+    }
+    __syncthreads();
+    const int n = e.scalars[1];
+    int max_depth = 0;
+    for (int i = 1 + tid; i <= n; i += kThreads) {
+        const int dr = e.n_dr[i];
+        const int depth = dr >> 16, rank = dr & 0xffff;
+        const int64_t tok = __ldcg(ids_g + (int64_t)(depth - 1) * topk + rank);
+        out.node_token_ids[i - 1] = tok;
+        out.node_depths[i - 1] = depth;
+        if (out.verify_ids) out.verify_ids[i] = tok;
+        if (out.verify_pos) out.verify_pos[i] = start + depth;
+        max_depth = max(max_depth, depth);
+    }
+    for (int i = tid; i <= n; i += kThreads) out.parents[i] = e.n_parent[i];
+    if (tid == 0) {
+        if (out.verify_ids) out.verify_ids[0] = root_token ? *root_token : 0;
+        if (out.verify_pos) out.verify_pos[0] = start;
+    }
+    if (out.visibility) {
+        const int W = (int)out.vis_words;
+        for (int i = tid; i <= n; i += kThreads) {
+            int anc[kMaxRows + 1];
+            int na = 0;
+            for (int a = i; a >= 0; a = e.n_parent[a]) anc[na++] = a;
+            uint32_t* row = out.visibility + (int64_t)i * W;
+            for (int wd = 0; wd < W; ++wd) {
+                uint32_t bits = 0;
+                for (int k = 0; k < na; ++k)
+                    if ((anc[k] >> 5) == wd) bits |= 1u << (anc[k] & 31);
+                row[wd] = bits;
+            }
+        }
+    }
+    // max depth (warp reduce then smem)
+    for (int o = 16; o > 0; o >>= 1) max_depth = max(max_depth, __shfl_xor_sync(DDT_FULL_MASK, max_depth, o));
+    __syncthreads();
+    if (lane == 0) atomicMax(&e.scalars[2], max_depth);
+    __syncthreads();
+    if (tid == 0 && out.info) {
+        out.info[0] = n;
+        out.info[1] = e.scalars[2];
+        out.info[3] = topk;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// phases A + B (+ C on the last CTA)
+// ---------------------------------------------------------------------------
+template <typename T, bool kVec>
+__global__ void __launch_bounds__(kThreads, 1)
+tree_build_kernel(const T* __restrict__ logits, int rows, int64_t vocab, int64_t row_stride, int topk, int chunks,
+                  int64_t chunk_len, int budget, const int64_t* root_token, int64_t start, ddt_tree_outputs out,
+                  unsigned char* ws) {
+    extern __shared__ __align__(256) unsigned char smem[];
+    __shared__ SelectScratch sel;
+    __shared__ double red_d[kWarps];
+    __shared__ float red_f[kWarps];
+    __shared__ int s_flag;
+
+    const WsLayout L = ws_layout(rows, chunks, topk);
+    uint32_t* row_cnt = reinterpret_cast<uint32_t*>(ws + L.row_cnt);
+    uint32_t* done_cnt = reinterpret_cast<uint32_t*>(ws + L.done_cnt);
+    float* part_m = reinterpret_cast<float*>(ws + L.part_m);
+    double* part_s = reinterpret_cast<double*>(ws + L.part_s);
+    unsigned long long* part_keys = reinterpret_cast<unsigned long long*>(ws + L.part_keys);
+    int64_t* top_ids = reinterpret_cast<int64_t*>(ws + L.top_ids);
+    float* top_lp = reinterpret_cast<float*>(ws + L.top_lp);
+
+    const int tid = threadIdx.x;
+    const int d = blockIdx.y, c = blockIdx.x;
+    const T* rowp = logits + (int64_t)d * row_stride;
+    const int64_t c0 = (int64_t)c * chunk_len;
+    const int64_t c1 = min(c0 + chunk_len, vocab);
+
+    // ---- load the chunk into registers --------------------------------
+    constexpr int kEpv = 16 / sizeof(T);  // elements per 16-byte vector
+    float vals[kValsPerThread];
+    uint32_t valid = 0;
+#pragma unroll
+    for (int j = 0; j < kValsPerThread / kEpv; ++j) {
+        const int64_t base = c0 + ((int64_t)j * kThreads + tid) * kEpv;
+        if (kVec && base + kEpv <= c1) {
+            const uint4 raw = __ldcs(reinterpret_cast<const uint4*>(rowp + base));
+            const T* pv = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+            for (int e = 0; e < kEpv; ++e) {
+                vals[j * kEpv + e] = to_f32<T>(pv[e]);
+                valid |= 1u << (j * kEpv + e);
+            }
+        } else {
+#pragma unroll
+            for (int e = 0; e < kEpv; ++e) {
+                const int64_t idx = base + e;
+                if (idx < c1) {
+                    vals[j * kEpv + e] = to_f32<T>(rowp[idx]);
+                    valid |= 1u << (j * kEpv + e);
+                } else {
+                    vals[j * kEpv + e] = -INFINITY;
+                }
+            }
+        }
+    }
+    auto elem_index = [&](int j) -> int64_t {
+        return c0 + ((int64_t)(j / kEpv) * kThreads + tid) * kEpv + (j % kEpv);
+    };
+
+    // ---- max and sum of exp (logsumexp pieces, ddtree.py:138) ----------
+    float m = -INFINITY;
+    bool nan_seen = false;
+#pragma unroll
+    for (int j = 0; j < kValsPerThread; ++j) {
+        if (valid >> j & 1u) {
+            const float v = vals[j];
+            nan_seen |= (v != v);
+            m = fmaxf(m, v);
+        }
+    }
+    if (tid == 0) s_flag = 0;
+    __syncthreads();
+    if (nan_seen) s_flag = 1;
+    m = block_max(m, red_f);
+    float sum_t = 0.f;
+    if (m != -INFINITY && m == m) {
+#pragma unroll
+        for (int j = 0; j < kValsPerThread; ++j)
+            if (valid >> j & 1u) sum_t += expf(vals[j] - m);
+    }
+    const double sum_c = block_sum_d((double)sum_t, red_d);
+
+    // ---- chunk top-k candidates ----------------------------------------
+    const int n_valid = (int)(c1 - c0);
+    const int kc = min(topk, n_valid);
+    uint32_t ov[kValsPerThread];
+    unsigned long long tmax = 0ull;
+#pragma unroll
+    for (int j = 0; j < kValsPerThread; ++j) ov[j] = ord_f32(vals[j]);
+    auto key_at = [&](int j) -> unsigned long long {
+        return (valid >> j & 1u) ? (((unsigned long long)ov[j] << 32) |
+                                    (unsigned long long)(0xffffffffu - (uint32_t)elem_index(j)))
+                                 : 0ull;
+    };
+#pragma unroll
+    for (int j = 0; j < kValsPerThread; ++j) {
+        const unsigned long long k = key_at(j);
+        tmax = k > tmax ? k : tmax;
+    }
+    unsigned long long* maxkeys = reinterpret_cast<unsigned long long*>(smem);
+    unsigned long long* cand = maxkeys + kThreads;
+    unsigned long long* dst = part_keys + ((int64_t)d * chunks + c) * topk;
+    maxkeys[tid] = tmax;
+    if (tid == 0) sel.count = 0;
+    __syncthreads();
+    unsigned long long t0 = 0ull;
+    if (n_valid > kCandCap && kc <= kThreads) t0 = block_kth_largest(maxkeys, kThreads, kc, &sel);
+    // gather keys >= t0 (warp-aggregated slots)
+#pragma unroll
+    for (int j = 0; j < kValsPerThread; ++j) {
+        const unsigned long long kj = key_at(j);
+        const bool take = kj != 0ull && kj >= t0;
+        const uint32_t b = __ballot_sync(DDT_FULL_MASK, take);
+        if (b) {
+            int base = 0;
+            const int lane = tid & 31;
+            if (lane == __ffs(b) - 1) base = atomicAdd(&sel.count, __popc(b));
+            base = __shfl_sync(DDT_FULL_MASK, base, __ffs(b) - 1);
+            if (take) {
+                const int pos = base + __popc(b & ((1u << lane) - 1u));
+                if (pos < kCandCap) cand[pos] = kj;
+            }
+        }
+    }
+    __syncthreads();
+    const int ncand = sel.count;
+    __syncthreads();
+    if (tid == 0) sel.count = 0;
+    if (ncand <= kCandCap) {
+        const unsigned long long t1 = block_kth_largest(cand, ncand, kc, &sel);
+        for (int i = tid; i < ncand; i += kThreads) {
+            const unsigned long long k = cand[i];
+            if (k >= t1) {
+                const int pos = atomicAdd(&sel.count, 1);
+                if (pos < topk) dst[pos] = k;
+            }
+        }
+    } else {
+        const unsigned long long t1 = block_kth_largest_regs(key_at, kc, &sel);
+#pragma unroll
+        for (int j = 0; j < kValsPerThread; ++j) {
+            const unsigned long long kj = key_at(j);
+            if (kj != 0ull && kj >= t1) {
+                const int pos = atomicAdd(&sel.count, 1);
+                if (pos < topk) dst[pos] = kj;
+            }
+        }
+    }
+    for (int i = kc + tid; i < topk; i += kThreads) dst[i] = 0ull;
+    if (tid == 0) {
+        part_m[d * chunks + c] = s_flag ? __int_as_float(0x7fc00000) : m;
+        part_s[d * chunks + c] = sum_c;
+    }
+
+    // ---- hand-off to the row merge ---------------------------------------
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_flag = (atomicAdd(&row_cnt[d], 1u) == (uint32_t)(chunks - 1)) ? 1 : 0;
+    __syncthreads();
+    if (!s_flag) return;
+    __threadfence();
+
+    // ---- phase B: merge the row ------------------------------------------
+    {
+        const int n = chunks * topk;
+        unsigned long long* mk = reinterpret_cast<unsigned long long*>(smem);
+        int P = 1;
+        while (P < topk) P <<= 1;
+        unsigned long long* sk = mk + n;
+        const unsigned long long* src = part_keys + (int64_t)d * chunks * topk;
+        for (int i = tid; i < n; i += kThreads) mk[i] = __ldcg(src + i);
+        for (int i = tid; i < P; i += kThreads) sk[i] = 0ull;
+        if (tid == 0) sel.count = 0;
+        __syncthreads();
+        const unsigned long long t = block_kth_largest(mk, n, topk, &sel);
+        for (int i = tid; i < n; i += kThreads) {
+            const unsigned long long k = mk[i];
+            if (k != 0ull && k >= t) {
+                const int pos = atomicAdd(&sel.count, 1);
+                if (pos < topk) sk[pos] = k;
+            }
+        }
+        __syncthreads();
+        bitonic_sort_desc(sk, P);
+        __shared__ float s_logz;
+        if (tid == 0) {
+            float M = -INFINITY;
+            bool nan_row = false;
+            for (int q = 0; q < chunks; ++q) {
+                const float mq = __ldcg(part_m + d * chunks + q);
+                nan_row |= (mq != mq);
+                M = fmaxf(M, mq);
+            }
+            float lz;
+            if (nan_row) {
+                lz = __int_as_float(0x7fc00000);
+            } else if (isinf(M)) {
+                lz = M;
+            } else {
+                double S = 0.0;
+                for (int q = 0; q < chunks; ++q) {
+                    const float mq = __ldcg(part_m + d * chunks + q);
+                    const double sq = __ldcg(part_s + d * chunks + q);
+                    if (mq != -INFINITY) S += sq * exp((double)mq - (double)M);
+                }
+                lz = (float)((double)M + log(S));
+            }
+            s_logz = lz;
+            if (!isfinite(lz)) atomicOr(&done_cnt[1], DDT_INFO_NONFINITE);
+        }
+        __syncthreads();
+        const float lz = s_logz;
+        bool bad = false;
+        for (int i = tid; i < topk; i += kThreads) {
+            const unsigned long long k = sk[i];
+            const float v = key_value(k);
+            const float lp = __fsub_rn(v, lz);
+            bad |= !isfinite(lp);
+            const int64_t id = key_index(k);
+            top_ids[(int64_t)d * topk + i] = id;
+            top_lp[(int64_t)d * topk + i] = lp;
+            if (out.top_ids) out.top_ids[(int64_t)d * topk + i] = id;
+            if (out.top_lp) out.top_lp[(int64_t)d * topk + i] = lp;
+        }
+        if (bad) atomicOr(&done_cnt[1], DDT_INFO_NONFINITE);
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        row_cnt[d] = 0u;
+        s_flag = (atomicAdd(&done_cnt[0], 1u) == (uint32_t)(rows - 1)) ? 1 : 0;
+    }
+    __syncthreads();
+    if (!s_flag) return;
+    __threadfence();
+
+    // ---- phase C: expansion on the last CTA --------------------------------
+    ExpandSmem e = carve_expand(smem, rows, topk, budget);
+    if (tid == 0) {
+        e.scalars[2] = 0;
+    }
+    __syncthreads();
+    expand_tree(top_lp, top_ids, rows, topk, budget, root_token, start, out, e);
+    if (tid == 0) {
+        if (out.info) out.info[2] = (int32_t)atomicExch(&done_cnt[1], 0u);
+        done_cnt[0] = 0u;
+    }
+}
+
+// Expansion alone from given (lp, ids).
+__global__ void __launch_bounds__(kThreads, 1)
+tree_expand_kernel(const float* lp, const int64_t* ids, int rows, int topk, int budget, const int64_t* root_token,
+                   int64_t start, ddt_tree_outputs out) {
+    extern __shared__ __align__(256) unsigned char smem[];
+    ExpandSmem e = carve_expand(smem, rows, topk, budget);
+    if (threadIdx.x == 0) e.scalars[2] = 0;
+    __syncthreads();
+    expand_tree(lp, ids, rows, topk, budget, root_token, start, out, e);
+    if (threadIdx.x == 0 && out.info) out.info[2] = 0;
+}
+
+// Root-only tree (budget <= 0 or no draft rows, ddtree.py:120-130).
+__global__ void tree_root_only_kernel(const int64_t* root_token, int64_t start, ddt_tree_outputs out) {
+    out.parents[0] = -1;
+    if (out.visibility) {
+        out.visibility[0] = 1u;
+        for (int w = 1; w < out.vis_words; ++w) out.visibility[w] = 0u;
+    }
+    if (out.verify_ids) out.verify_ids[0] = root_token ? *root_token : 0;
+    if (out.verify_pos) out.verify_pos[0] = start;
+    if (out.info) {
+        out.info[0] = 0;
+        out.info[1] = 0;
+        out.info[2] = 0;
+        out.info[3] = 0;
+    }
+}
+
+}  // namespace tree
+}  // namespace ddt
+
+using namespace ddt;
+using namespace ddt::tree;
+
+static size_t phase_smem(int64_t rows, int64_t chunks, int64_t topk, int64_t budget) {
+    size_t a = sizeof(uint64_t) * (kThreads + kCandCap);
+    int64_t P = 1;
+    while (P < topk) P <<= 1;
+    size_t b = sizeof(uint64_t) * (chunks * topk + P);
+    size_t c = expand_smem_bytes(rows, topk, budget);
+    size_t m = a > b ? a : b;
+    return m > c ? m : c;
+}
+
+static int validate_outputs(const ddt_tree_outputs* out, int64_t budget) {
+    if (!out) return set_error(DDT_EINVAL, "tree outputs struct is null");
+    if (budget > 0 && (!out->node_token_ids || !out->node_depths))
+        return set_error(DDT_EINVAL, "node_token_ids / node_depths are required");
+    if (!out->parents) return set_error(DDT_EINVAL, "parents is required");
+    if (out->visibility && out->vis_words < ceil_div(budget + 1, 32))
+        return set_error(DDT_EINVAL, "vis_words %lld < ceil((budget+1)/32)", (long long)out->vis_words);
+    return DDT_OK;
+}
+
+extern "C" size_t ddt_tree_build_workspace_size(int64_t rows, int64_t vocab, int64_t budget) {
+    if (rows <= 0 || vocab <= 0 || budget <= 0) return 256;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int sms = ddt_sm_count(dev);
+    const int64_t topk = budget < vocab ? budget : vocab;
+    int64_t chunks, len;
+    choose_chunks(rows, vocab, topk, sms > 0 ? sms : 148, &chunks, &len);
+    // sized for the largest chunk count any device could pick
+    int64_t chunks_max, len2;
+    choose_chunks(rows, vocab, topk, 1024, &chunks_max, &len2);
+    if (chunks_max < chunks) chunks_max = chunks;
+    return ws_layout(rows, chunks_max, topk).total;
+}
+
+extern "C" int ddt_tree_build(const void* logits, int dtype, int64_t rows, int64_t vocab, int64_t row_stride,
+                              int64_t budget, const int64_t* root_token, int64_t start, const ddt_tree_outputs* out,
+                              void* workspace, size_t workspace_bytes, ddt_stream_t stream) {
+    int rc = validate_outputs(out, budget);
+    if (rc) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (budget <= 0 || rows == 0) {
+        tree_root_only_kernel<<<1, 1, 0, st>>>(root_token, start, *out);
+        return check_launch("tree_root_only_kernel");
+    }
+    if (!logits) return set_error(DDT_EINVAL, "logits is null");
+    if (rows < 0 || rows > kMaxRows) return set_error(DDT_EUNSUPPORTED, "rows=%lld outside [0, %d]", (long long)rows, kMaxRows);
+    if (vocab <= 0 || vocab >= (int64_t)1 << 31) return set_error(DDT_EINVAL, "vocab=%lld", (long long)vocab);
+    if (budget > kMaxBudget) return set_error(DDT_EUNSUPPORTED, "budget=%lld > %d", (long long)budget, kMaxBudget);
+    if (row_stride < vocab) return set_error(DDT_EINVAL, "row_stride < vocab");
+    if (dtype != DDT_F32 && dtype != DDT_BF16 && dtype != DDT_F16) return set_error(DDT_EINVAL, "dtype %d", dtype);
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int sms = ddt_sm_count(dev);
+    const int64_t topk = budget < vocab ? budget : vocab;
+    int64_t chunks, chunk_len;
+    choose_chunks(rows, vocab, topk, sms, &chunks, &chunk_len);
+    const WsLayout L = ws_layout(rows, chunks, topk);
+    if (!workspace || workspace_bytes < L.total)
+        return set_error(DDT_EWORKSPACE, "tree build workspace needs %zu bytes, got %zu", L.total, workspace_bytes);
+    if (reinterpret_cast<uintptr_t>(workspace) % 256) return set_error(DDT_EINVAL, "workspace must be 256-byte aligned");
+    const size_t smem = phase_smem(rows, chunks, topk, budget);
+    if (smem > 227 * 1024) return set_error(DDT_EUNSUPPORTED, "tree build needs %zu bytes of shared memory", smem);
+    const size_t esz = dtype == DDT_F32 ? 4 : 2;
+    const bool vec = (reinterpret_cast<uintptr_t>(logits) % 16 == 0) && ((row_stride * esz) % 16 == 0);
+    dim3 grid((unsigned)chunks, (unsigned)rows);
+    unsigned char* ws = static_cast<unsigned char*>(workspace);
+#define DDT_LAUNCH_TB(T, V)                                                                                        \
+    do {                                                                                                           \
+        auto k = tree_build_kernel<T, V>;                                                                          \
+        if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)        \
+            return check_launch("cudaFuncSetAttribute(tree_build_kernel)");                                        \
+        k<<<grid, kThreads, smem, st>>>(static_cast<const T*>(logits), (int)rows, vocab, row_stride, (int)topk,    \
+                                        (int)chunks, chunk_len, (int)budget, root_token, start, *out, ws);        \
+    } while (0)
+    if (dtype == DDT_F32) {
+        if (vec) DDT_LAUNCH_TB(float, true); else DDT_LAUNCH_TB(float, false);
+    } else if (dtype == DDT_BF16) {
+        if (vec) DDT_LAUNCH_TB(__nv_bfloat16, true); else DDT_LAUNCH_TB(__nv_bfloat16, false);
+    } else {
+        if (vec) DDT_LAUNCH_TB(__half, true); else DDT_LAUNCH_TB(__half, false);
+    }
+#undef DDT_LAUNCH_TB
+    return check_launch("tree_build_kernel");
+}
+
+extern "C" int ddt_tree_from_log_probs(const float* lp, const int64_t* ids, int64_t rows, int64_t topk,
+                                       int64_t budget, const int64_t* root_token, int64_t start,
+                                       const ddt_tree_outputs* out, ddt_stream_t stream) {
+    int rc = validate_outputs(out, budget);
+    if (rc) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (budget <= 0 || rows == 0) {
+        tree_root_only_kernel<<<1, 1, 0, st>>>(root_token, start, *out);
+        return check_launch("tree_root_only_kernel");
+    }
+    if (!lp || !ids) return set_error(DDT_EINVAL, "lp / ids are null");
+    if (rows < 0 || rows > kMaxRows) return set_error(DDT_EUNSUPPORTED, "rows=%lld outside [0, %d]", (long long)rows, kMaxRows);
+    if (topk <= 0 || topk > 0xffff) return set_error(DDT_EINVAL, "topk=%lld", (long long)topk);
+    if (budget > kMaxBudget) return set_error(DDT_EUNSUPPORTED, "budget=%lld > %d", (long long)budget, kMaxBudget);
+    const size_t smem = expand_smem_bytes(rows, topk, budget);
+    if (smem > 227 * 1024) return set_error(DDT_EUNSUPPORTED, "expansion needs %zu bytes of shared memory", smem);
+    if (cudaFuncSetAttribute(tree_expand_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+        return check_launch("cudaFuncSetAttribute(tree_expand_kernel)");
+    tree_expand_kernel<<<1, kThreads, smem, st>>>(lp, ids, (int)rows, (int)topk, (int)budget, root_token, start, *out);
+    return check_launch("tree_expand_kernel");
+}

@@ -1,0 +1,313 @@
+"""Torch-facing wrappers of the C-ABI entry points (device tensors in, device
+tensors out, launched on the current CUDA stream)."""
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from ._lib import AttentionArgs, TreeOutputs, WORKSPACES, check, dtype_code, ptr, require_cuda, stream_of
+
+
+def vis_words_for(n_rows: int) -> int:
+    return max(1, (int(n_rows) + 31) // 32)
+
+
+@dataclass
+class DeviceTree:
+    """Outputs of the tree-build kernel, resident on the device.
+
+    node i (1-based) of the tree is row i of the verify batch; row 0 is the
+    root.  ``visibility`` holds one row of packed ancestor bits per verify
+    row (int32 words carrying uint32 bit patterns)."""
+
+    budget: int
+    rows: int
+    topk: int
+    top_ids: torch.Tensor
+    top_lp: torch.Tensor
+    node_token_ids: torch.Tensor
+    node_depths: torch.Tensor
+    parents: torch.Tensor
+    visibility: torch.Tensor
+    verify_ids: torch.Tensor
+    verify_pos: torch.Tensor
+    info: torch.Tensor
+
+    @classmethod
+    def allocate(cls, rows: int, vocab: int, budget: int, device: torch.device) -> "DeviceTree":
+        b = max(int(budget), 0)
+        k = min(b, int(vocab)) if b > 0 else 0
+        W = vis_words_for(b + 1)
+        i64 = dict(dtype=torch.int64, device=device)
+        return cls(
+            budget=b, rows=int(rows), topk=k,
+            top_ids=torch.empty((rows, max(k, 1)), **i64),
+            top_lp=torch.empty((rows, max(k, 1)), dtype=torch.float32, device=device),
+            node_token_ids=torch.empty((max(b, 1),), **i64),
+            node_depths=torch.empty((max(b, 1),), **i64),
+            parents=torch.empty((b + 1,), dtype=torch.int32, device=device),
+            visibility=torch.zeros((b + 1, W), dtype=torch.int32, device=device),
+            verify_ids=torch.empty((b + 1,), **i64),
+            verify_pos=torch.empty((b + 1,), **i64),
+            info=torch.zeros((4,), dtype=torch.int32, device=device),
+        )
+
+    def c_outputs(self) -> TreeOutputs:
+        return TreeOutputs(
+            top_ids=ptr(self.top_ids), top_lp=ptr(self.top_lp), node_token_ids=ptr(self.node_token_ids),
+            node_depths=ptr(self.node_depths), parents=ptr(self.parents), visibility=ptr(self.visibility),
+            vis_words=self.visibility.shape[1], verify_ids=ptr(self.verify_ids), verify_pos=ptr(self.verify_pos),
+            info=ptr(self.info))
+
+
+def tree_build(draft_logits: torch.Tensor, budget: int, root_token: torch.Tensor | None = None, start: int = 0,
+               out: DeviceTree | None = None) -> DeviceTree:
+    """Kernel (1) on ``draft_logits`` [rows, vocab] (fp32 / bf16 / fp16)."""
+    require_cuda(draft_logits, "draft_logits")
+    if draft_logits.dim() != 2:
+        raise ValueError("draft_logits must be [rows, vocab]")
+    if draft_logits.stride(1) != 1:
+        draft_logits = draft_logits.contiguous()
+    rows, vocab = draft_logits.shape
+    dev = draft_logits.device
+    if out is None:
+        out = DeviceTree.allocate(rows, vocab, budget, dev)
+    lib = _lib.load()
+    ws_bytes = lib.ddt_tree_build_workspace_size(rows, vocab, max(int(budget), 0))
+    ws = WORKSPACES.get("tree_build", dev, ws_bytes)
+    if root_token is not None:
+        require_cuda(root_token, "root_token")
+        if root_token.dtype != torch.int64:
+            raise TypeError("root_token must be int64")
+    o = out.c_outputs()
+    rc = lib.ddt_tree_build(ptr(draft_logits), dtype_code(draft_logits.dtype), rows, vocab, draft_logits.stride(0),
+                            int(budget), ptr(root_token), int(start), ctypes.byref(o), ptr(ws), ws.numel(),
+                            stream_of(dev))
+    check(rc, "ddt_tree_build")
+    return out
+
+
+def tree_from_log_probs(lp: torch.Tensor, ids: torch.Tensor, budget: int, root_token: torch.Tensor | None = None,
+                        start: int = 0) -> DeviceTree:
+    """Best-first expansion alone from given [rows, topk] log-probs and ids."""
+    require_cuda(lp, "lp")
+    require_cuda(ids, "ids")
+    lp = lp.to(torch.float32).contiguous()
+    ids = ids.to(torch.int64).contiguous()
+    rows, topk = lp.shape
+    out = DeviceTree.allocate(rows, topk, budget, lp.device)
+    o = out.c_outputs()
+    rc = _lib.load().ddt_tree_from_log_probs(ptr(lp), ptr(ids), rows, topk, int(budget), ptr(root_token), int(start),
+                                             ctypes.byref(o), stream_of(lp.device))
+    check(rc, "ddt_tree_from_log_probs")
+    return out
+
+
+def tree_mask_fill(mask2d: torch.Tensor, past_length: int, n_rows: int, visibility: torch.Tensor,
+                   prev_start: int, prev_len: int) -> None:
+    """Write the additive-mask rows of a tree into ``mask2d`` [rows_cap, cols]."""
+    require_cuda(mask2d, "mask")
+    if mask2d.stride(1) != 1:
+        raise ValueError("mask rows must be contiguous")
+    min_value = torch.finfo(mask2d.dtype).min
+    rc = _lib.load().ddt_tree_mask_fill(ptr(mask2d), dtype_code(mask2d.dtype), mask2d.stride(0), mask2d.shape[0],
+                                        int(past_length), int(n_rows), ptr(visibility), visibility.shape[1],
+                                        int(prev_start), int(prev_len), float(min_value),
+                                        stream_of(mask2d.device))
+    check(rc, "ddt_tree_mask_fill")
+
+
+def mask_to_bits(mask2d: torch.Tensor, col_offset: int, n_rows: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Pack the [n_rows, n_rows] tree block of a dense mask at ``col_offset``."""
+    require_cuda(mask2d, "mask")
+    if mask2d.stride(1) != 1:
+        mask2d = mask2d.contiguous()
+    W = vis_words_for(n_rows)
+    if out is None:
+        out = torch.empty((n_rows, W), dtype=torch.int32, device=mask2d.device)
+    rc = _lib.load().ddt_mask_to_bits(ptr(mask2d), dtype_code(mask2d.dtype), mask2d.stride(0), int(col_offset),
+                                      int(n_rows), ptr(out), W, stream_of(mask2d.device))
+    check(rc, "ddt_mask_to_bits")
+    return out
+
+
+def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, past_length: int, visibility: torch.Tensor,
+                   scale: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Kernel (2): one layer of tree-masked attention.
+
+    q [n_tokens, hq, 128], k / v [hkv, kv_rows, 128] (bf16, last dim
+    contiguous, any other strides), visibility [n_tokens, W] int32.
+    Returns out [n_tokens, hq, 128] bf16."""
+    for t, n in ((q, "q"), (k, "k"), (v, "v"), (visibility, "visibility")):
+        require_cuda(t, n)
+    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
+        raise TypeError("q, k, v must be bf16")
+    if q.stride(-1) != 1 or k.stride(-1) != 1 or v.stride(-1) != 1:
+        raise ValueError("head_dim must be the contiguous dimension")
+    if k.stride() != v.stride() or k.shape != v.shape:
+        raise ValueError("k and v must share shape and strides")
+    n_tokens, hq, d = q.shape
+    hkv, kv_rows, _ = k.shape
+    if out is None:
+        out = torch.empty((n_tokens, hq, d), dtype=torch.bfloat16, device=q.device)
+    visibility = visibility.contiguous()
+    lib = _lib.load()
+    dev = q.device
+    ws_bytes = lib.ddt_tree_attention_workspace_size(n_tokens, hq, hkv, int(past_length),
+                                                     dev.index if dev.index is not None else 0)
+    ws = WORKSPACES.get("attention", dev, ws_bytes)
+    a = AttentionArgs(
+        q=ptr(q), q_stride_tok=q.stride(0), q_stride_head=q.stride(1), k=ptr(k), v=ptr(v),
+        kv_stride_head=k.stride(0), kv_stride_row=k.stride(1), kv_rows=kv_rows, out=ptr(out),
+        o_stride_tok=out.stride(0), o_stride_head=out.stride(1), n_tokens=n_tokens, hq=hq, hkv=hkv, head_dim=d,
+        past_length=int(past_length), visibility=ptr(visibility), vis_words=visibility.shape[1], scale=float(scale))
+    check(lib.ddt_tree_attention(ctypes.byref(a), ptr(ws), ws.numel(), stream_of(dev)), "ddt_tree_attention")
+    return out
+
+
+def attention_status(device: torch.device) -> int:
+    """Device-side status word of the attention kernel (0 = no bounded wait ran out)."""
+    ws = WORKSPACES.get("attention", device, 256)
+    return int(ws[:4].view(torch.int32).item())
+
+
+def tree_accept(logits: torch.Tensor, parents: torch.Tensor, node_token_ids: torch.Tensor,
+                n_nodes_dev: torch.Tensor | None = None, max_accept: int | None = None,
+                accepted: torch.Tensor | None = None, accept_info: torch.Tensor | None = None,
+                posterior: torch.Tensor | None = None):
+    """Kernel (3a): argmax of every verify row + walk down the tree.
+
+    Returns (accepted [max_accept] int64, accept_info [2] int64 = {count,
+    next_token}, posterior [n_rows] int64)."""
+    require_cuda(logits, "logits")
+    if logits.dim() == 3:
+        logits = logits[0]
+    if logits.stride(1) != 1:
+        logits = logits.contiguous()
+    n_rows, vocab = logits.shape
+    dev = logits.device
+    if max_accept is None:
+        max_accept = n_rows
+    if accepted is None:
+        accepted = torch.zeros((max_accept,), dtype=torch.int64, device=dev)
+    if accept_info is None:
+        accept_info = torch.zeros((2,), dtype=torch.int64, device=dev)
+    if posterior is None:
+        posterior = torch.empty((n_rows,), dtype=torch.int64, device=dev)
+    lib = _lib.load()
+    ws = WORKSPACES.get("accept", dev, lib.ddt_tree_accept_workspace_size(n_rows, vocab))
+    rc = lib.ddt_tree_accept(ptr(logits), dtype_code(logits.dtype), n_rows, vocab, logits.stride(0), ptr(parents),
+                             ptr(node_token_ids), ptr(n_nodes_dev), ptr(posterior), ptr(accepted), int(max_accept),
+                             ptr(accept_info), ptr(ws), ws.numel(), stream_of(dev))
+    check(rc, "ddt_tree_accept")
+    return accepted, accept_info, posterior
+
+
+def tree_walk(posterior: torch.Tensor, parents: torch.Tensor, node_token_ids: torch.Tensor,
+              n_nodes_dev: torch.Tensor | None = None, max_accept: int | None = None):
+    """Walk alone from a device posterior [n_rows].  Returns (accepted, accept_info)."""
+    require_cuda(posterior, "posterior")
+    post = posterior.reshape(-1).to(torch.int64).contiguous()
+    n_rows = post.numel()
+    dev = post.device
+    max_accept = n_rows if max_accept is None else max_accept
+    accepted = torch.zeros((max_accept,), dtype=torch.int64, device=dev)
+    accept_info = torch.zeros((2,), dtype=torch.int64, device=dev)
+    rc = _lib.load().ddt_tree_walk(ptr(post), n_rows, ptr(parents), ptr(node_token_ids), ptr(n_nodes_dev),
+                                   ptr(accepted), int(max_accept), ptr(accept_info), stream_of(dev))
+    check(rc, "ddt_tree_walk")
+    return accepted, accept_info
+
+
+def argmax_rows(logits: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    require_cuda(logits, "logits")
+    shape = logits.shape
+    x = logits.reshape(-1, shape[-1])
+    if x.stride(1) != 1:
+        x = x.contiguous()
+    n_rows, vocab = x.shape
+    if out is None:
+        out = torch.empty((n_rows,), dtype=torch.int64, device=x.device)
+    lib = _lib.load()
+    ws = WORKSPACES.get("accept", x.device, lib.ddt_tree_accept_workspace_size(n_rows, vocab))
+    rc = lib.ddt_argmax_rows(ptr(x), dtype_code(x.dtype), n_rows, vocab, x.stride(0), ptr(out), ptr(ws), ws.numel(),
+                             stream_of(x.device))
+    check(rc, "ddt_argmax_rows")
+    return out.view(shape[:-1])
+
+
+def eagle3_accept(logits: torch.Tensor, draft_tokens: torch.Tensor, retrieve: torch.Tensor):
+    """Kernel (3b): EAGLE3 path acceptance.  Returns (info [4] int64 =
+    {best, accept_length, sample_token, 0}, accepted [width] int64, posterior)."""
+    require_cuda(logits, "logits")
+    x = logits[0] if logits.dim() == 3 else logits
+    if x.stride(1) != 1:
+        x = x.contiguous()
+    n_rows, vocab = x.shape
+    dev = x.device
+    draft = draft_tokens.reshape(-1).to(device=dev, dtype=torch.int64).contiguous()
+    r = retrieve.to(device=dev, dtype=torch.int64).contiguous()
+    leaves, width = r.shape
+    info = torch.zeros((4,), dtype=torch.int64, device=dev)
+    accepted = torch.zeros((width,), dtype=torch.int64, device=dev)
+    posterior = torch.empty((n_rows,), dtype=torch.int64, device=dev)
+    lib = _lib.load()
+    ws = WORKSPACES.get("accept", dev, lib.ddt_tree_accept_workspace_size(n_rows, vocab))
+    rc = lib.ddt_eagle3_accept(ptr(x), dtype_code(x.dtype), n_rows, vocab, x.stride(0), ptr(draft), ptr(r), leaves,
+                               width, ptr(posterior), ptr(info), ptr(accepted), ptr(ws), ws.numel(), stream_of(dev))
+    check(rc, "ddt_eagle3_accept")
+    return info, accepted, posterior
+
+
+class PointerTable:
+    """Device array of tensor base pointers, re-uploaded only when they change."""
+
+    def __init__(self):
+        self._key = None
+        self._dev = None
+
+    def get(self, tensors, device: torch.device) -> torch.Tensor:
+        key = tuple(t.data_ptr() for t in tensors)
+        if key != self._key or self._dev is None or self._dev.device != device:
+            host = torch.tensor(key, dtype=torch.int64)
+            self._dev = host.to(device)
+            self._key = key
+        return self._dev
+
+
+_PTRS = PointerTable()
+
+
+def kv_compact(tensors, past_length: int, cur_len: int, keep: torch.Tensor, keep_count: torch.Tensor,
+               max_keep: int, table: PointerTable | None = None) -> None:
+    """In-place compaction of many [..., heads, rows, head_dim] cache tensors
+    sharing one layout: rows past+keep[k] -> past+k for k < keep_count."""
+    if not tensors:
+        return
+    t0 = tensors[0]
+    require_cuda(t0, "cache tensor")
+    for t in tensors:
+        if t.shape != t0.shape or t.stride() != t0.stride() or t.dtype != t0.dtype:
+            raise ValueError("all cache tensors of one compaction call must share shape, strides and dtype")
+    if t0.dim() < 2 or t0.stride(-1) != 1:
+        raise ValueError("cache tensors must have a contiguous last dimension")
+    esz = t0.element_size()
+    heads = math.prod(t0.shape[:-2]) if t0.dim() > 2 else 1
+    if t0.dim() > 2:
+        # collapse the leading dims into one "head" dimension
+        hs = t0.stride(-3)
+        for i in range(t0.dim() - 3):
+            if t0.stride(i) != t0.stride(i + 1) * t0.shape[i + 1]:
+                raise ValueError("leading dimensions must be collapsible")
+    else:
+        hs = 0
+    table = table or _PTRS
+    ptrs = table.get(tensors, t0.device)
+    rc = _lib.load().ddt_kv_compact(ptr(ptrs), len(tensors), heads, t0.shape[-1] * esz, hs * esz, t0.stride(-2) * esz,
+                                    int(past_length), int(cur_len), ptr(keep), ptr(keep_count), int(max_keep),
+                                    stream_of(t0.device))
+    check(rc, "ddt_kv_compact")

@@ -1,0 +1,197 @@
+/*
+ * ddtree_b200.h - C ABI of the B200 (sm_100a) DDTree draft-tree hot path.
+ *
+ * One shared library, libddtree_b200.so, exports these entry points.  They
+ * take raw device pointers, sizes and strides plus a cudaStream_t; nothing
+ * in the signatures is a torch type.  Inputs are borrowed; outputs go to
+ * caller-allocated device buffers.  Every entry point validates its
+ * arguments on the host and returns DDT_OK or an error code; the text of
+ * the last error of the calling thread is available from ddt_last_error().
+ * Kernels are launched asynchronously on `stream`.  Errors that can only be
+ * seen on the device (a non-finite log-normaliser, a bounded wait that ran
+ * out) are reported through the `info` words of the call's outputs.
+ *
+ * Each entry point names the reference function it replaces
+ * (kimwin2/ddtree_eagle3_patch, file:line).
+ */
+#ifndef DDTREE_B200_H
+#define DDTREE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* ddt_stream_t; /* same handle as cudaStream_t */
+
+#if defined(__GNUC__)
+#define DDT_API __attribute__((visibility("default")))
+#else
+#define DDT_API
+#endif
+
+enum ddt_status {
+    DDT_OK = 0,
+    DDT_EINVAL = 1,      /* bad argument (shape, stride, alignment, null pointer) */
+    DDT_ECUDA = 2,       /* a CUDA runtime call failed */
+    DDT_EUNSUPPORTED = 3,/* valid but outside what this build implements */
+    DDT_EWORKSPACE = 4   /* workspace missing or too small */
+};
+
+enum ddt_dtype { DDT_F32 = 0, DDT_BF16 = 1, DDT_F16 = 2, DDT_BOOL = 3 };
+
+/* info[2] bits written by the tree-build kernels */
+#define DDT_INFO_NONFINITE 1u /* a selected log-probability or log-normaliser was not finite */
+
+DDT_API const char* ddt_last_error(void);
+DDT_API int ddt_abi_version(void);
+DDT_API int ddt_sm_count(int device);
+
+/* ---------------------------------------------------------------------------
+ * (1) Tree build.
+ * Replaces build_ddtree_tree (ddtree.py:114-196) and the id / position
+ * buffer fills of compile_ddtree_tree (ddtree.py:233-245).
+ *
+ * logits: [rows, vocab] float32 / bf16 / fp16, row stride `row_stride`
+ * elements.  budget >= 0; topk = min(budget, vocab); rows <= 32;
+ * budget <= 1024.  The tree has n = min(budget, reachable) nodes; node i
+ * (1-based) is the i-th entry popped by the best-first expansion.
+ * ------------------------------------------------------------------------- */
+typedef struct {
+    int64_t* top_ids;        /* [rows, topk] int64 token ids, value desc / id asc (nullable) */
+    float* top_lp;           /* [rows, topk] fp32 log-probs top - logsumexp (nullable)       */
+    int64_t* node_token_ids; /* [budget] int64                                               */
+    int64_t* node_depths;    /* [budget] int64 (1-based depth)                               */
+    int32_t* parents;        /* [budget + 1] int32, parents[0] = -1                          */
+    uint32_t* visibility;    /* [budget + 1, vis_words] ancestor bitmask: bit j of row i set
+                                iff tree row j is row i or one of its ancestors (nullable)   */
+    int64_t vis_words;       /* row stride of `visibility` in uint32 words, >= ceil((budget+1)/32) */
+    int64_t* verify_ids;     /* [budget + 1] root token then node tokens (nullable)          */
+    int64_t* verify_pos;     /* [budget + 1] start + depth (nullable)                        */
+    int32_t* info;           /* [4]: node count, max depth, DDT_INFO_* flags, topk           */
+} ddt_tree_outputs;
+
+/* Workspace bytes for ddt_tree_build.  The workspace must be zero-filled
+ * before its first use; every completed call leaves its counters at zero. */
+DDT_API size_t ddt_tree_build_workspace_size(int64_t rows, int64_t vocab, int64_t budget);
+
+DDT_API int ddt_tree_build(const void* logits, int dtype, int64_t rows, int64_t vocab, int64_t row_stride,
+                   int64_t budget, const int64_t* root_token /* device scalar, nullable */, int64_t start,
+                   const ddt_tree_outputs* out, void* workspace, size_t workspace_bytes, ddt_stream_t stream);
+
+/* Best-first expansion only, from given log-probs and ids (ddtree.py:146-189).
+ * lp: [rows, topk] fp32, ids: [rows, topk] int64, both device. */
+DDT_API int ddt_tree_from_log_probs(const float* lp, const int64_t* ids, int64_t rows, int64_t topk, int64_t budget,
+                            const int64_t* root_token, int64_t start, const ddt_tree_outputs* out,
+                            ddt_stream_t stream);
+
+/* Dense additive mask rows for the HF verify forward (ddtree.py:230-251):
+ * clears the previous tree block [0, prev_len) x [prev_start, prev_start+prev_len)
+ * to 0, then writes rows [0, n_rows) x [past, past + n_rows) as 0 where the
+ * ancestor bit is set and `min_value` elsewhere.  mask: [rows_cap, row_stride]
+ * of `dtype`. */
+DDT_API int ddt_tree_mask_fill(void* mask, int dtype, int64_t row_stride, int64_t rows_cap, int64_t past_length,
+                       int64_t n_rows, const uint32_t* visibility, int64_t vis_words, int64_t prev_start,
+                       int64_t prev_len, double min_value, ddt_stream_t stream);
+
+/* Packs the tree block of a dense bool / additive mask into the ancestor
+ * bitmask layout (a visible entry is a nonzero bool or a value > min/2).
+ * Used when a caller hands the verify attention a dense mask. */
+DDT_API int ddt_mask_to_bits(const void* mask, int dtype, int64_t row_stride, int64_t col_offset, int64_t n_rows,
+                     uint32_t* visibility, int64_t vis_words, ddt_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * (2) Tree-masked verify attention (one layer).
+ * Replaces the target's attention call inside the verify forward
+ * (ddtree.py:523-531 -> transformers sdpa_attention_forward with the 4-D mask
+ * from ddtree.py:247-253), i.e. softmax(Q K^T * scale + mask) V with GQA.
+ *
+ * q:   [n_tokens, hq, 128] bf16 (token stride q_stride_tok, head stride q_stride_head, elements)
+ * k,v: [hkv, kv_rows, 128] bf16 (head stride kv_stride_head, row stride kv_stride_row)
+ *      rows [0, past) are the prefix, rows [past, past + n_tokens) the tree.
+ * out: [n_tokens, hq, 128] bf16.
+ * visibility: [n_tokens, vis_words] ancestor bitmask of the tree rows.
+ * Row t sees every prefix key and tree key j iff bit j of its mask is set.
+ * ------------------------------------------------------------------------- */
+typedef struct {
+    const void* q;
+    int64_t q_stride_tok, q_stride_head;
+    const void* k;
+    const void* v;
+    int64_t kv_stride_head, kv_stride_row;
+    int64_t kv_rows;           /* allocated rows of k / v (>= past + n_tokens) */
+    void* out;
+    int64_t o_stride_tok, o_stride_head;
+    int64_t n_tokens, hq, hkv, head_dim, past_length;
+    const uint32_t* visibility;
+    int64_t vis_words;
+    float scale;
+} ddt_attention_args;
+
+DDT_API size_t ddt_tree_attention_workspace_size(int64_t n_tokens, int64_t hq, int64_t hkv, int64_t past_length,
+                                         int device);
+DDT_API int ddt_tree_attention(const ddt_attention_args* args, void* workspace, size_t workspace_bytes,
+                       ddt_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * (3) Greedy acceptance and KV compaction.
+ * ddt_tree_accept replaces sample(logits, 0) (model/utils.py:28-30) plus
+ * follow_verified_tree (ddtree.py:290-301): row-wise argmax (first max; NaN
+ * counts as largest) and the walk from the root down the tree while the
+ * target's token is a child of the current node.
+ * logits [n_rows, vocab] with n_rows = 1 + node count; parents / node tokens
+ * as produced by ddt_tree_build; n_nodes_dev (nullable) overrides n_rows-1
+ * with the device-side node count info[0] of the build.
+ * accepted: [max_accept] int64 tree row indices (root 0 first);
+ * accept_info: [2] int64 = {accepted count, next (bonus) token}.
+ * ------------------------------------------------------------------------- */
+DDT_API size_t ddt_tree_accept_workspace_size(int64_t n_rows, int64_t vocab);
+DDT_API int ddt_tree_accept(const void* logits, int dtype, int64_t n_rows, int64_t vocab, int64_t row_stride,
+                    const int32_t* parents, const int64_t* node_token_ids, const int32_t* n_nodes_dev,
+                    int64_t* posterior /* [n_rows], nullable */, int64_t* accepted, int64_t max_accept,
+                    int64_t* accept_info, void* workspace, size_t workspace_bytes, ddt_stream_t stream);
+
+/* The walk alone, from a posterior [n_rows] int64 already on the device
+ * (follow_verified_tree, ddtree.py:290-301). */
+DDT_API int ddt_tree_walk(const int64_t* posterior, int64_t n_rows, const int32_t* parents,
+                          const int64_t* node_token_ids, const int32_t* n_nodes_dev, int64_t* accepted,
+                          int64_t max_accept, int64_t* accept_info, ddt_stream_t stream);
+
+/* Row-wise argmax alone (model/utils.py:28-30), posterior [n_rows] int64. */
+DDT_API int ddt_argmax_rows(const void* logits, int dtype, int64_t n_rows, int64_t vocab, int64_t row_stride,
+                    int64_t* posterior, void* workspace, size_t workspace_bytes, ddt_stream_t stream);
+
+/* In-place compaction of the appended window of many cache tensors in one
+ * launch.  Replaces compact_dynamic_cache's per-layer loop (ddtree.py:323-369)
+ * over compact_tail_inplace (ddtree.py:61-88): for every tensor t and head h,
+ *   rows past + keep[k] -> past + k, k < keep_count,
+ * with every read done before any write (index_select then copy_).
+ * tensors: device array of n_tensors base pointers; all share heads,
+ * row_bytes (head_dim * element size), head and row strides (bytes).
+ * keep / keep_count live on the device (keep_count may be the accept_info of
+ * ddt_tree_accept); cur_len is the appended window length: the call is a
+ * no-op when keep_count is 0 or equals cur_len (ddtree.py:80-81). */
+DDT_API int ddt_kv_compact(void* const* tensors, int64_t n_tensors, int64_t heads, int64_t row_bytes,
+                   int64_t head_stride_bytes, int64_t row_stride_bytes, int64_t past_length, int64_t cur_len,
+                   const int64_t* keep, const int64_t* keep_count_dev, int64_t max_keep, ddt_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * EAGLE3 path acceptance.  Replaces evaluate_eagle3_posterior
+ * (eagle3.py:46-79) for temperature 0: argmax of every verify row, the
+ * longest accepted prefix over the rows of retrieve_indices (-1 padded),
+ * first best path on ties, and the bonus token of the last accepted row.
+ * out_info: [4] int64 = {best_candidate, accept_length, sample_token, -};
+ * accepted: [width] int64 (first accept_length + 1 entries valid).
+ * ------------------------------------------------------------------------- */
+DDT_API int ddt_eagle3_accept(const void* logits, int dtype, int64_t n_rows, int64_t vocab, int64_t row_stride,
+                      const int64_t* draft_tokens, const int64_t* retrieve, int64_t leaves, int64_t width,
+                      int64_t* posterior /* [n_rows], nullable */, int64_t* out_info, int64_t* accepted,
+                      void* workspace, size_t workspace_bytes, ddt_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DDTREE_B200_H */

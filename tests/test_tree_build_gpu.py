@@ -1,0 +1,188 @@
+"""Kernel (1), tree build, against the oracle and the reference's own outputs."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from tests.golden_cases import regenerate_logits, tree_prefixes
+
+pytestmark = pytest.mark.gpu
+
+
+def _kernels():
+    from ddtree_eagle3_patch_b200 import kernels
+    return kernels
+
+
+def _tree_np(tree):
+    n = int(tree.info[0].item())
+    return dict(
+        n=n,
+        node_token_ids=tree.node_token_ids[:n].cpu().numpy(),
+        node_depths=tree.node_depths[:n].cpu().numpy(),
+        parents=tree.parents[: n + 1].cpu().numpy(),
+        bits=tree.visibility[: n + 1].cpu().numpy().view(np.uint32),
+        verify_ids=tree.verify_ids[: n + 1].cpu().numpy(),
+        verify_pos=tree.verify_pos[: n + 1].cpu().numpy(),
+        info=tree.info.cpu().numpy(),
+    )
+
+
+def _assert_tree_equal(got, ref_tokens, ref_depths, ref_parents, ref_vis, msg=""):
+    n = len(ref_tokens)
+    assert got["n"] == n, msg
+    assert np.array_equal(got["node_token_ids"], ref_tokens), msg
+    assert np.array_equal(got["node_depths"], ref_depths), msg
+    assert np.array_equal(got["parents"], np.asarray(ref_parents, np.int32)), msg
+    W = got["bits"].shape[1]
+    assert np.array_equal(got["bits"], O.pack_visibility(np.asarray(ref_vis, bool), W)), msg
+
+
+def test_expansion_from_reference_log_probs_is_bit_exact(golden_trees):
+    """Same (lp, ids) in -> the reference's tree out, for every fixture."""
+    K = _kernels()
+    z = golden_trees
+    for p in tree_prefixes(z):
+        b = int(z[p + "budget"])
+        if p + "lp" not in z.files:
+            continue
+        lp = torch.from_numpy(z[p + "lp"]).cuda()
+        ids = torch.from_numpy(z[p + "ids"]).cuda()
+        root = torch.tensor([12345], dtype=torch.int64, device="cuda")
+        t = K.tree_from_log_probs(lp, ids, b, root_token=root, start=100)
+        g = _tree_np(t)
+        _assert_tree_equal(g, z[p + "node_token_ids"], z[p + "node_depths"], z[p + "parents"], z[p + "visibility"], p)
+        assert g["verify_ids"][0] == 12345
+        assert np.array_equal(g["verify_ids"][1:], z[p + "node_token_ids"])
+        assert np.array_equal(g["verify_pos"], np.concatenate([[100], 100 + z[p + "node_depths"]]))
+
+
+def test_full_build_matches_oracle_and_reference(golden_trees):
+    """Logits in: top-k ids equal the oracle's (value desc, id asc), log-probs
+    within 1 ulp, tree bit-exact to the oracle fed the kernel's own lp/ids and
+    to the reference wherever torch's top-k order is defined (no value ties)."""
+    K = _kernels()
+    z = golden_trees
+    for p in tree_prefixes(z):
+        b = int(z[p + "budget"])
+        x = regenerate_logits(z, p) if (p + "logits" in z.files or p + "logits_sha256" in z.files) else None
+        if x is None or b <= 0 or x.shape[0] == 0:
+            continue
+        t = K.tree_build(torch.from_numpy(np.ascontiguousarray(x)).cuda(), b)
+        g = _tree_np(t)
+        k = min(b, x.shape[1])
+        ids_g = t.top_ids[:, :k].cpu().numpy()
+        lp_g = t.top_lp[:, :k].cpu().numpy()
+        o_ids, o_vals, o_logz = O.topk_logz(x, k)
+        assert np.array_equal(ids_g, o_ids), p
+        o_lp = O.log_probs(o_vals, o_logz)
+        ulp = np.abs(lp_g.view(np.int32).astype(np.int64) - o_lp.view(np.int32).astype(np.int64))
+        assert ulp.max() <= 2, (p, ulp.max())
+        o = O.tree_from_lp(lp_g, ids_g, b)
+        _assert_tree_equal(g, o["node_token_ids"], o["node_depths"], o["parents"], o["visibility"], p)
+        if np.array_equal(ids_g, z[p + "ids"]) and np.array_equal(lp_g, z[p + "lp"]):
+            _assert_tree_equal(g, z[p + "node_token_ids"], z[p + "node_depths"], z[p + "parents"],
+                               z[p + "visibility"], p)
+
+
+def test_configuration_1_trees_equal_reference(golden_trees):
+    K = _kernels()
+    z = golden_trees
+    for p in ("cfg1_b32_", "cfg1_b64_", "deep_b64_", "deep_b128_"):
+        x = torch.from_numpy(regenerate_logits(z, p)).cuda()
+        t = K.tree_build(x, int(z[p + "budget"]))
+        g = _tree_np(t)
+        _assert_tree_equal(g, z[p + "node_token_ids"], z[p + "node_depths"], z[p + "parents"], z[p + "visibility"], p)
+        assert g["info"][2] == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_half_precision_logits(dtype):
+    K = _kernels()
+    g = torch.Generator().manual_seed(7)
+    x = (torch.randn(15, 151936, generator=g) * 3).to(dtype)
+    t = K.tree_build(x.cuda(), 64)
+    xf = x.float().numpy()
+    o = O.build_tree(xf, 64)
+    gt = _tree_np(t)
+    assert np.array_equal(t.top_ids.cpu().numpy(), o["ids"])
+    lp = t.top_lp.cpu().numpy()
+    o2 = O.tree_from_lp(lp, o["ids"], 64)
+    _assert_tree_equal(gt, o2["node_token_ids"], o2["node_depths"], o2["parents"], o2["visibility"])
+
+
+@pytest.mark.parametrize("L,V,budget", [(15, 151936, 1), (15, 151936, 256), (15, 151936, 1024), (1, 151936, 64),
+                                        (32, 50000, 128), (4, 5, 40), (2, 3, 10), (15, 2049, 64), (7, 16384, 300)])
+def test_shapes_and_budgets(L, V, budget):
+    K = _kernels()
+    g = torch.Generator().manual_seed(L * 1000 + budget)
+    x = torch.randn(L, V, generator=g) * 2
+    if L > 2:
+        x[torch.arange(L), torch.randint(0, V, (L,), generator=g)] += 12
+    t = K.tree_build(x.cuda(), budget)
+    gt = _tree_np(t)
+    o = O.build_tree(x.numpy(), budget)
+    k = min(budget, V)
+    assert np.array_equal(t.top_ids[:, :k].cpu().numpy(), o["ids"])
+    o2 = O.tree_from_lp(t.top_lp[:, :k].cpu().numpy(), o["ids"], budget)
+    _assert_tree_equal(gt, o2["node_token_ids"], o2["node_depths"], o2["parents"], o2["visibility"], (L, V, budget))
+
+
+def test_value_ties_break_by_lowest_token_id():
+    K = _kernels()
+    x = torch.zeros(3, 5000)
+    x[:, ::7] = 1.0           # many equal maxima
+    x[1, 4999] = 2.0
+    t = K.tree_build(x.cuda(), 16)
+    ids = t.top_ids.cpu().numpy()
+    assert ids[0].tolist() == list(range(0, 7 * 16, 7))
+    assert ids[1, 0] == 4999 and ids[1, 1:].tolist() == list(range(0, 7 * 15, 7))
+
+
+def test_root_only_tree():
+    K = _kernels()
+    root = torch.tensor([42], dtype=torch.int64, device="cuda")
+    t = K.tree_build(torch.randn(15, 100, device="cuda"), 0, root_token=root, start=9)
+    assert int(t.info[0]) == 0
+    assert int(t.parents[0]) == -1
+    assert int(t.verify_ids[0]) == 42 and int(t.verify_pos[0]) == 9
+    assert int(t.visibility[0, 0]) == 1
+
+
+def test_nonfinite_logits_are_flagged():
+    K = _kernels()
+    x = torch.randn(4, 1000)
+    x[2, 5] = float("nan")
+    t = K.tree_build(x.cuda(), 8)
+    assert int(t.info[2]) & 1
+    # the flag is per call: a clean call afterwards reports nothing
+    t2 = K.tree_build(torch.randn(4, 1000).cuda(), 8)
+    assert int(t2.info[2]) == 0
+
+
+def test_repeated_calls_reuse_workspace():
+    K = _kernels()
+    x = torch.from_numpy(O.np.random.RandomState(0).randn(15, 151936).astype(np.float32)).cuda()
+    a = _tree_np(K.tree_build(x, 64))
+    for _ in range(3):
+        b = _tree_np(K.tree_build(x, 64))
+        assert np.array_equal(a["parents"], b["parents"]) and np.array_equal(a["node_token_ids"], b["node_token_ids"])
+
+
+def test_dropin_build_ddtree_tree_matches_reference(golden_trees):
+    from ddtree_eagle3_patch_b200.ddtree import build_ddtree_tree
+    z = golden_trees
+    for p in ("cfg1_b32_", "cfg1_b64_", "deep_b64_"):
+        x = torch.from_numpy(regenerate_logits(z, p)).cuda()
+        ids, depths, parents, child_maps, vis, sub = build_ddtree_tree(x, int(z[p + "budget"]))
+        assert ids.device.type == "cpu" and ids.dtype == torch.long
+        assert np.array_equal(ids.numpy(), z[p + "node_token_ids"])
+        assert np.array_equal(depths.numpy(), z[p + "node_depths"])
+        assert parents == z[p + "parents"].tolist()
+        assert np.array_equal(vis.numpy(), z[p + "visibility"])
+        assert isinstance(child_maps, list) and len(child_maps) == len(parents)
+        for i in range(1, len(parents)):
+            assert child_maps[parents[i]][int(ids[i - 1])] == i
+        assert set(sub) == {"tree_build_copy", "tree_build_heap", "tree_build_visibility"}
+    out = build_ddtree_tree(torch.randn(15, 100, device="cuda"), 0)
+    assert out[2] == [-1] and out[4].shape == (1, 1)
