@@ -1,0 +1,464 @@
+"""Benchmark of the DDTree per-step draft-tree hot path on B200.
+
+One step = the device work of one DDTree decoding round outside the model
+GEMMs, at the Qwen3-4B verify shape:
+  1. tree build from draft logits [15, 151936] fp32, node budget 64
+     (top-k + log-normaliser + best-first expansion + ancestor bitmask);
+  2. tree-masked verify attention for 36 layers: 32 query / 8 KV heads,
+     head_dim 128, bf16, 4096-token prefix + 65 verify rows (one launch per
+     layer: in a real round each layer's queries come from the model);
+  3. greedy acceptance on verify logits [65, 151936] bf16 (argmax + walk);
+  4. in-place compaction of the accepted rows in 72 cache tensors.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+``value`` is whole-job steps/s with inputs resident in HBM (CUDA-graph
+replays, CUDA events, max over ranks); ``e2e`` is the same metric through
+the public API with host buffers (pinned host inputs copied in and the
+accept result copied out every step).  ``--impl reference`` times the
+reference's CPU path (a port making the reference's library calls) on the
+host cores.  Multi-GPU: one process per GPU, independent replicas (the
+reference shards prompts across GPUs; the hot path has no exchange step),
+NCCL only for the timing barrier and the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+LAYERS, HQ, HKV, HD = 36, 32, 8, 128
+ROWS, VOCAB, BUDGET, PAST = 15, 151936, 64, 4096
+N_VERIFY = BUDGET + 1
+METRIC = "tree build+verify steps/s (DDTree hot-path step, Qwen3-4B shape, B=1)"
+UNIT = "steps/s"
+WORKLOAD = (f"tree build [{ROWS}x{VOCAB}] fp32 budget {BUDGET} + tree-verify attention {LAYERS} layers "
+            f"(hq {HQ}, hkv {HKV}, d {HD}, prefix {PAST} + {N_VERIFY} rows, bf16) + greedy accept "
+            f"[{N_VERIFY}x{VOCAB}] bf16 + KV compaction of {2 * LAYERS} tensors")
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    return rank, world, local
+
+
+def init_dist(world: int, backend: str):
+    import datetime
+    import torch.distributed as dist
+    if world > 1 and not dist.is_initialized():
+        dist.init_process_group(backend=backend, timeout=datetime.timedelta(seconds=120))
+    return dist
+
+
+# ----------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ----------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = Path(f"/tmp/ddt_clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or not self.path.exists():
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        sms, mx, reasons = [], None, set()
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sms.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"),
+                                 parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        self.path.unlink(missing_ok=True)
+        return {"sm_mhz": statistics.median(sms) if sms else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sms)}
+
+
+# ----------------------------------------------------------------------------
+# our implementation
+# ----------------------------------------------------------------------------
+class Workload:
+    """Device-resident inputs of the step (two alternating input sets for the
+    logits; 613 MB of KV per step keeps every step's working set above L2)."""
+
+    def __init__(self, device, seed: int):
+        from ddtree_eagle3_patch_b200.synthetic import cfg1_logits, posterior_for_tree, verify_logits_for_posterior
+        g = torch.Generator().manual_seed(seed)
+        self.device = device
+        self.draft = [cfg1_logits(seed=seed + i).to(device) for i in range(2)]
+        self.kcap = PAST + N_VERIFY
+        self.ks = [torch.empty((HKV, self.kcap, HD), dtype=torch.bfloat16, device=device) for _ in range(LAYERS)]
+        self.vs = [torch.empty((HKV, self.kcap, HD), dtype=torch.bfloat16, device=device) for _ in range(LAYERS)]
+        gd = torch.Generator(device=device).manual_seed(seed)
+        for t in self.ks:
+            t.normal_(generator=gd).mul_(HD ** -0.5)
+        for t in self.vs:
+            t.normal_(generator=gd)
+        self.qs = [torch.randn((N_VERIFY, HQ, HD), generator=g).to(torch.bfloat16).to(device) for _ in range(LAYERS)]
+        self.outs = [torch.empty((N_VERIFY, HQ, HD), dtype=torch.bfloat16, device=device) for _ in range(LAYERS)]
+        # verify logits whose argmax follows the configuration-1 posterior rule
+        from ddtree_eagle3_patch_b200 import kernels
+        tree = kernels.tree_build(self.draft[0], BUDGET)
+        n = int(tree.info[0])
+        post = posterior_for_tree(tree.node_token_ids[:n].cpu().numpy(), tree.node_depths[:n].cpu().numpy(),
+                                  tree.top_ids.cpu().numpy(), VOCAB, seed=seed)
+        self.verify = [verify_logits_for_posterior(post, VOCAB, seed=seed + i).to(device) for i in range(2)]
+        self.scale = HD ** -0.5
+
+
+def gpu_step(w: Workload, i: int, tree_out, accept_bufs, table):
+    from ddtree_eagle3_patch_b200 import kernels
+    tree = kernels.tree_build(w.draft[i % 2], BUDGET, out=tree_out)
+    for layer in range(LAYERS):
+        kernels.tree_attention(w.qs[layer], w.ks[layer], w.vs[layer], PAST, tree.visibility, w.scale,
+                               out=w.outs[layer])
+    acc, info, post = kernels.tree_accept(w.verify[i % 2], tree.parents, tree.node_token_ids, tree.info,
+                                          max_accept=ROWS + 1, accepted=accept_bufs[0], accept_info=accept_bufs[1],
+                                          posterior=accept_bufs[2])
+    kernels.kv_compact([t for pair in zip(w.ks, w.vs) for t in pair], PAST, N_VERIFY, acc, info[:1], ROWS + 1,
+                       table=table)
+    return info
+
+
+def run_ours(args, rank, world, local):
+    from ddtree_eagle3_patch_b200 import kernels
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    dist = init_dist(world, "nccl")
+    w = Workload(device, seed=1000 + rank)
+    tree_out = kernels.DeviceTree.allocate(ROWS, VOCAB, BUDGET, device)
+    accept_bufs = (torch.zeros(ROWS + 1, dtype=torch.int64, device=device),
+                   torch.zeros(2, dtype=torch.int64, device=device),
+                   torch.empty(N_VERIFY, dtype=torch.int64, device=device))
+    table = kernels.PointerTable()
+    stream = torch.cuda.Stream(device)
+    # warm-up eagerly (allocates workspaces, sets kernel attributes)
+    with torch.cuda.stream(stream):
+        for i in range(max(args.warmup, 1)):
+            gpu_step(w, i, tree_out, accept_bufs, table)
+    torch.cuda.synchronize()
+    status = kernels.attention_status(device)
+    # capture one step per input set
+    graphs = []
+    for i in range(2):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            gpu_step(w, i, tree_out, accept_bufs, table)
+        graphs.append(g)
+    for i in range(args.warmup):
+        graphs[i % 2].replay()
+    torch.cuda.synchronize()
+    launches_per_step = 1 + LAYERS * (2 if _attention_splits() > 1 else 1) + 1 + 1
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # timed region: K graph replays
+    with ClockSampler(_physical_index(local)) as clocks:
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for i in range(args.steps):
+                graphs[i % 2].replay()
+            e1.record(stream)
+        barrier()
+    elapsed_ms = e0.elapsed_time(e1)
+    clock = clocks.summary()
+    ms = torch.tensor([elapsed_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    elapsed_ms = float(ms.item())
+    ms_per_step = elapsed_ms / args.steps
+    value = world * args.steps / (elapsed_ms / 1e3)
+
+    # dominant kernel: the per-layer attention op, timed alone (graph of 36 layers)
+    ga = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(ga, stream=stream):
+        for layer in range(LAYERS):
+            kernels.tree_attention(w.qs[layer], w.ks[layer], w.vs[layer], PAST, tree_out.visibility, w.scale,
+                                   out=w.outs[layer])
+    for _ in range(3):
+        ga.replay()
+    torch.cuda.synchronize()
+    reps = max(5, args.steps // 2)
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        a0.record(stream)
+        for _ in range(reps):
+            ga.replay()
+        a1.record(stream)
+    torch.cuda.synchronize()
+    attn_us = a0.elapsed_time(a1) * 1e3 / (reps * LAYERS)
+    kv_bytes = 2 * HKV * (PAST + N_VERIFY) * HD * 2
+    qo_bytes = 2 * N_VERIFY * HQ * HD * 2
+    alg_bytes = kv_bytes + qo_bytes
+    peaks = _peaks()
+    achieved = alg_bytes / (attn_us * 1e-6) / 1e9
+    roofline = {"bound": "hbm", "kernel": "tree_attn_kernel + attn_combine_kernel (one layer)",
+                "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "peak_source": peaks["source"],
+                "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                "traffic": _profiled_traffic(), "algorithmic_bytes": alg_bytes, "us_per_launch": round(attn_us, 3)}
+
+    # end to end through the public API with host buffers
+    e2e = run_e2e(args, w, device, stream, tree_out, table, world, dist)
+
+    status |= kernels.attention_status(device)
+    out = None
+    if rank == 0:
+        out = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5), "us_per_step": round(ms_per_step * 1e3, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded; random-init inputs of the Qwen3-4B verify shape)",
+            "config": {"workload": WORKLOAD, "parallelism": f"replicas x{world} (prompt-sharded data parallel)",
+                       "l2": "inputs larger than L2 (613 MB of KV per step)", "cuda_graph": True},
+            "roofline": roofline, "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
+            "clocks": clock, "attention_status": status,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            out["cpu_baseline"] = cpu_baseline(sample_steps=2, attn_layers=4)
+    if world > 1:
+        dist.barrier()
+    del graphs, ga
+    return out
+
+
+def run_e2e(args, w: Workload, device, stream, tree_out, table, world, dist):
+    """Per step: pinned host draft logits, per-layer queries and new tree K/V
+    rows, and verify logits are copied in; the accept result is copied out."""
+    from ddtree_eagle3_patch_b200 import kernels
+    h_draft = [t.cpu().pin_memory() for t in w.draft]
+    h_verify = [t.cpu().pin_memory() for t in w.verify]
+    h_q = torch.stack([q.cpu() for q in w.qs]).pin_memory()
+    h_kt = torch.stack([k[:, PAST:].cpu() for k in w.ks]).pin_memory()
+    h_vt = torch.stack([v[:, PAST:].cpu() for v in w.vs]).pin_memory()
+    d_draft = torch.empty_like(w.draft[0])
+    d_verify = torch.empty_like(w.verify[0])
+    d_q = torch.empty((LAYERS, N_VERIFY, HQ, HD), dtype=torch.bfloat16, device=device)
+    h_result = torch.empty(ROWS + 3, dtype=torch.int64).pin_memory()
+    acc_bufs = (torch.zeros(ROWS + 1, dtype=torch.int64, device=device),
+                torch.zeros(2, dtype=torch.int64, device=device),
+                torch.empty(N_VERIFY, dtype=torch.int64, device=device))
+    h2d = (h_draft[0].numel() * 4 + h_verify[0].numel() * 2 + h_q.numel() * 2 + h_kt.numel() * 2 + h_vt.numel() * 2)
+    d2h = h_result.numel() * 8
+
+    def step(i):
+        with torch.cuda.stream(stream):
+            d_draft.copy_(h_draft[i % 2], non_blocking=True)
+            tree = kernels.tree_build(d_draft, BUDGET, out=tree_out)
+            d_q.copy_(h_q, non_blocking=True)
+            for layer in range(LAYERS):
+                w.ks[layer][:, PAST:].copy_(h_kt[layer], non_blocking=True)
+                w.vs[layer][:, PAST:].copy_(h_vt[layer], non_blocking=True)
+                kernels.tree_attention(d_q[layer], w.ks[layer], w.vs[layer], PAST, tree.visibility, w.scale,
+                                       out=w.outs[layer])
+            d_verify.copy_(h_verify[i % 2], non_blocking=True)
+            acc, info, _ = kernels.tree_accept(d_verify, tree.parents, tree.node_token_ids, tree.info,
+                                               max_accept=ROWS + 1, accepted=acc_bufs[0], accept_info=acc_bufs[1],
+                                               posterior=acc_bufs[2])
+            kernels.kv_compact([t for pair in zip(w.ks, w.vs) for t in pair], PAST, N_VERIFY, acc, info[:1],
+                               ROWS + 1, table=table)
+            h_result[: ROWS + 1].copy_(acc, non_blocking=True)
+            h_result[ROWS + 1:].copy_(info, non_blocking=True)
+        stream.synchronize()
+        return int(h_result[ROWS + 1])
+
+    for i in range(max(args.warmup, 1)):
+        step(i)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    el = float(ms.item())
+    return {"value": round(world * args.steps / (el / 1e3), 2), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(d2h), "ms_per_step": round(el / args.steps, 4),
+            "api": "ddtree_eagle3_patch_b200.kernels (C-ABI via ctypes), eager launches"}
+
+
+def _attention_splits() -> int:
+    from ddtree_eagle3_patch_b200 import _lib
+    sms = _lib.load().ddt_sm_count(torch.cuda.current_device())
+    mtiles = -(-N_VERIFY // (128 // (HQ // HKV)))
+    n_kt = -(-(PAST + N_VERIFY) // 128)
+    return max(1, min(n_kt, sms // (HKV * mtiles)))
+
+
+def _physical_index(local: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        parts = vis.split(",")
+        if local < len(parts) and parts[local].strip().isdigit():
+            return int(parts[local])
+    return local
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def _profiled_traffic():
+    """DRAM bytes per attention launch from the committed ncu summary, or None."""
+    f = ROOT / "profiles" / "tree_attn_kernel_qwen3_4b_verify.md"
+    if not f.exists():
+        return None
+    for line in f.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_layer:"):
+            try:
+                return int(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+# ----------------------------------------------------------------------------
+# the reference's CPU path
+# ----------------------------------------------------------------------------
+def _cpu_step_inputs(layers_alloc: int, attn_layers: int):
+    from ddtree_eagle3_patch_b200.synthetic import cfg1_logits, posterior_for_tree, verify_logits_for_posterior
+    from oracle import cpu_reference as C
+    draft = cfg1_logits(seed=0)
+    toks, deps, parents, cm, vis = C.build_tree(draft, BUDGET)
+    top = torch.topk(draft, 1, dim=-1).indices.numpy()
+    post = posterior_for_tree(toks, deps, np.repeat(top, 1, axis=1), VOCAB, seed=0)
+    verify = verify_logits_for_posterior(post, VOCAB, seed=0)[None]
+    g = torch.Generator().manual_seed(5)
+    base_k = (torch.randn(1, HKV, PAST + N_VERIFY, HD, generator=g) * HD ** -0.5).to(torch.bfloat16)
+    base_v = torch.randn(1, HKV, PAST + N_VERIFY, HD, generator=g).to(torch.bfloat16)
+    ks = [base_k.clone() for _ in range(layers_alloc)]
+    vs = [base_v.clone() for _ in range(layers_alloc)]
+    qs = [torch.randn(1, HQ, N_VERIFY, HD, generator=g).to(torch.bfloat16) for _ in range(attn_layers)]
+    return C.CpuStep(draft, verify, qs, ks, vs, PAST, BUDGET, HD ** -0.5, LAYERS)
+
+
+def cpu_step_seconds(step, attn_layers: int):
+    r = step.run(attn_layers)
+    return r["build"] + r["accept_compact"] + r["attention"] * LAYERS / attn_layers, r
+
+
+def cpu_baseline(sample_steps: int, attn_layers: int):
+    torch.set_num_threads(os.cpu_count() or 1)
+    step = _cpu_step_inputs(LAYERS, attn_layers)
+    cpu_step_seconds(step, attn_layers)  # warm
+    secs = [cpu_step_seconds(step, attn_layers)[0] for _ in range(sample_steps)]
+    s = statistics.median(secs)
+    return {"value": round(1.0 / s, 4), "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+            "sample": (f"{sample_steps} steps; per step the full tree build, accept and 72-tensor compaction "
+                       f"plus {attn_layers} of {LAYERS} attention layers, attention time scaled x{LAYERS // attn_layers}"),
+            "s_per_step": round(s, 4)}
+
+
+def run_reference(args, rank, world, local):
+    if world > 1:
+        init_dist(world, "gloo")
+        import torch.distributed as dist
+        dist.barrier()
+        if rank != 0:
+            return None
+    torch.set_num_threads(os.cpu_count() or 1)
+    attn_layers = 2
+    step = _cpu_step_inputs(LAYERS, attn_layers)
+    for _ in range(args.warmup):
+        cpu_step_seconds(step, attn_layers)
+    t0 = time.perf_counter()
+    secs = [cpu_step_seconds(step, attn_layers)[0] for _ in range(args.steps)]
+    wall = time.perf_counter() - t0
+    s = sum(secs) / len(secs)
+    value = 1.0 / s
+    sample = (f"each step: full tree build, accept and 72-tensor compaction plus {attn_layers} of {LAYERS} "
+              f"attention layers (bf16 SDPA with repeat_kv and the dense mask), attention scaled x{LAYERS // attn_layers}")
+    return {"metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(s * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "impl": "reference",
+            "config": {"workload": WORKLOAD, "parallelism": "host CPU, rank 0"},
+            "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": torch.get_num_threads(),
+                             "kind": "port", "sample": sample},
+            "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "wall_s": round(wall, 2)}
+
+
+def main():
+    args = parse()
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        out = run_reference(args, rank, world, local)
+    else:
+        out = run_ours(args, rank, world, local)
+    if rank == 0 and out is not None:
+        print(json.dumps(out), flush=True)
+    try:
+        import torch.distributed as dist
+        if dist.is_initialized():
+            dist.destroy_process_group()
+    except Exception:
+        pass
+
+
+if __name__ == "__main__":
+    main()

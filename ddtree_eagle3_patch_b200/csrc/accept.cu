@@ -36,17 +36,20 @@ __device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long k)
     return ((unsigned long long)hi << 32) | lo;
 }
 
+// Workspace layout.  The counters sit at fixed offsets for every shape (a
+// counter word is never data in another call's layout), so a zero-filled
+// workspace stays valid across calls of any shape: every completed call
+// leaves its counters at zero again.
+constexpr int64_t kMaxRowsPerLaunch = 4096;
 struct WsLayout {
     size_t row_cnt, done_cnt, part, post, total;
 };
 __host__ __device__ inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 __host__ __device__ inline WsLayout ws_layout(int64_t rows, int64_t chunks) {
     WsLayout w;
-    size_t o = 0;
-    w.row_cnt = o;
-    o = align256(o + sizeof(uint32_t) * rows);
-    w.done_cnt = o;
-    o = align256(o + sizeof(uint32_t) * 4);
+    w.row_cnt = 0;
+    w.done_cnt = sizeof(uint32_t) * kMaxRowsPerLaunch;
+    size_t o = align256(w.done_cnt + sizeof(uint32_t) * 4);
     w.part = o;
     o = align256(o + sizeof(unsigned long long) * rows * chunks);
     w.post = o;
@@ -323,30 +326,38 @@ static int launch_argmax(const void* logits, int dtype, int64_t n_rows, int64_t 
     const int64_t chunks = choose_chunks(n_rows, vocab, ddt_sm_count(dev));
     const int64_t clen = chunk_len_for(vocab, chunks);
     const int64_t nchunks = ceil_div(vocab, clen);
-    const WsLayout L = ws_layout(n_rows, nchunks);
+    if (mode != kArgmaxOnly && n_rows > kMaxRowsPerLaunch)
+        return set_error(DDT_EUNSUPPORTED, "n_rows=%lld > %lld", (long long)n_rows, (long long)kMaxRowsPerLaunch);
+    const WsLayout L = ws_layout(n_rows < kMaxRowsPerLaunch ? n_rows : kMaxRowsPerLaunch, nchunks);
     if (!workspace || workspace_bytes < L.total)
         return set_error(DDT_EWORKSPACE, "accept workspace needs %zu bytes, got %zu", L.total, workspace_bytes);
     if (reinterpret_cast<uintptr_t>(workspace) % 256) return set_error(DDT_EINVAL, "workspace must be 256-byte aligned");
     const size_t esz = dtype == DDT_F32 ? 4 : 2;
     const bool vec = (reinterpret_cast<uintptr_t>(logits) % 16 == 0) && ((row_stride * esz) % 16 == 0);
     const size_t smem = mode == kTreeWalk ? (sizeof(int32_t) + sizeof(int64_t)) * kMaxNodes : 0;
-    dim3 grid((unsigned)nchunks, (unsigned)n_rows);
     unsigned char* ws = static_cast<unsigned char*>(workspace);
+    const char* base = static_cast<const char*>(logits);
+    for (int64_t r0 = 0; r0 < n_rows; r0 += kMaxRowsPerLaunch) {
+        const int64_t nr = n_rows - r0 < kMaxRowsPerLaunch ? n_rows - r0 : kMaxRowsPerLaunch;
+        const void* lg = base + r0 * row_stride * (int64_t)esz;
+        int64_t* post_out = posterior ? posterior + r0 : nullptr;
+        dim3 grid((unsigned)nchunks, (unsigned)nr);
 #define DDT_LAUNCH_AM(T, V)                                                                                      \
     do {                                                                                                         \
         auto k = argmax_kernel<T, V>;                                                                            \
         if (smem > 48 * 1024 &&                                                                                  \
             cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)      \
             return check_launch("cudaFuncSetAttribute(argmax_kernel)");                                          \
-        k<<<grid, kThreads, smem, st>>>(static_cast<const T*>(logits), n_rows, vocab, row_stride, (int)nchunks,  \
-                                        clen, posterior, ws, mode, tail);                                        \
+        k<<<grid, kThreads, smem, st>>>(static_cast<const T*>(lg), nr, vocab, row_stride, (int)nchunks, clen,    \
+                                        post_out, ws, mode, tail);                                               \
     } while (0)
-    if (dtype == DDT_F32) {
-        if (vec) DDT_LAUNCH_AM(float, true); else DDT_LAUNCH_AM(float, false);
-    } else if (dtype == DDT_BF16) {
-        if (vec) DDT_LAUNCH_AM(__nv_bfloat16, true); else DDT_LAUNCH_AM(__nv_bfloat16, false);
-    } else {
-        if (vec) DDT_LAUNCH_AM(__half, true); else DDT_LAUNCH_AM(__half, false);
+        if (dtype == DDT_F32) {
+            if (vec) DDT_LAUNCH_AM(float, true); else DDT_LAUNCH_AM(float, false);
+        } else if (dtype == DDT_BF16) {
+            if (vec) DDT_LAUNCH_AM(__nv_bfloat16, true); else DDT_LAUNCH_AM(__nv_bfloat16, false);
+        } else {
+            if (vec) DDT_LAUNCH_AM(__half, true); else DDT_LAUNCH_AM(__half, false);
+        }
     }
 #undef DDT_LAUNCH_AM
     return check_launch("argmax_kernel");
@@ -356,7 +367,7 @@ extern "C" size_t ddt_tree_accept_workspace_size(int64_t n_rows, int64_t vocab) 
     if (n_rows <= 0 || vocab <= 0) return 256;
     // largest chunk count any device could choose (chunks of >= 4096 elements)
     const int64_t chunks = ceil_div(vocab, 4096);
-    return ws_layout(n_rows, chunks).total;
+    return ws_layout(n_rows < kMaxRowsPerLaunch ? n_rows : kMaxRowsPerLaunch, chunks).total;
 }
 
 extern "C" int ddt_argmax_rows(const void* logits, int dtype, int64_t n_rows, int64_t vocab, int64_t row_stride,

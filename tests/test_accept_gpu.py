@@ -174,3 +174,12 @@ def test_kv_compact_many_layers_from_device_count():
         exp = r.clone()
         exp[:, past:past + 5] = r[:, past + keep.cpu()]
         assert torch.equal(t, exp)
+
+
+def test_workspace_reuse_across_shapes():
+    """Calls of different shapes share one workspace; counters must stay valid."""
+    K = _k()
+    for rows, V in [(3, 7), (130, 20000), (65, 151936), (2, 9), (4097, 300), (65, 151936)]:
+        x = torch.randn(rows, V).to(torch.bfloat16)
+        got = K.argmax_rows(x.cuda()).cpu()
+        assert torch.equal(got, torch.argmax(x.float(), dim=-1)), (rows, V)
