@@ -55,6 +55,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel", choices=["attention", "tree_build", "expand", "accept", "compact"], default=None,
+                    help="launch only this kernel of the step (warmup + steps times, eager) and print its "
+                         "average CUDA-event time; used for small profiler captures")
     return ap.parse_args()
 
 
@@ -443,9 +446,51 @@ def run_reference(args, rank, world, local):
             "wall_s": round(wall, 2)}
 
 
+def run_kernel_only(args, local):
+    """One kernel of the step on the bench workload, eager launches."""
+    from ddtree_eagle3_patch_b200 import kernels
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    w = Workload(device, seed=1000)
+    tree = kernels.tree_build(w.draft[0], BUDGET)
+    lp, ids = tree.top_lp.clone(), tree.top_ids.clone()
+    acc, info, _ = kernels.tree_accept(w.verify[0], tree.parents, tree.node_token_ids, tree.info, max_accept=ROWS + 1)
+    tensors = [t for pair in zip(w.ks, w.vs) for t in pair]
+
+    def once(i):
+        if args.kernel == "attention":
+            layer = i % LAYERS
+            kernels.tree_attention(w.qs[layer], w.ks[layer], w.vs[layer], PAST, tree.visibility, w.scale,
+                                   out=w.outs[layer])
+        elif args.kernel == "tree_build":
+            kernels.tree_build(w.draft[i % 2], BUDGET, out=tree)
+        elif args.kernel == "expand":
+            kernels.tree_from_log_probs(lp, ids, BUDGET)
+        elif args.kernel == "accept":
+            kernels.tree_accept(w.verify[i % 2], tree.parents, tree.node_token_ids, tree.info, max_accept=ROWS + 1)
+        else:
+            kernels.kv_compact(tensors, PAST, N_VERIFY, acc, info[:1], ROWS + 1)
+
+    for i in range(args.warmup):
+        once(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        once(i)
+    e1.record()
+    torch.cuda.synchronize()
+    print(json.dumps({"kernel": args.kernel, "launches": args.steps,
+                      "us_per_launch_eager": round(e0.elapsed_time(e1) * 1e3 / args.steps, 3),
+                      "attention_status": kernels.attention_status(device)}))
+
+
 def main():
     args = parse()
     rank, world, local = dist_env()
+    if args.kernel:
+        run_kernel_only(args, local)
+        return
     if args.impl == "reference":
         out = run_reference(args, rank, world, local)
     else:
