@@ -69,6 +69,8 @@ _SIGNATURES = {
     "ddt_tree_build_workspace_size": (ctypes.c_size_t, [_c_i64, _c_i64, _c_i64]),
     "ddt_tree_build": (ctypes.c_int, [_c_p, ctypes.c_int, _c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_i64,
                                       ctypes.POINTER(TreeOutputs), _c_p, ctypes.c_size_t, _c_p]),
+    "ddt_tree_build_noalloc": (ctypes.c_int, [_c_p, ctypes.c_int, _c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_i64,
+                                              ctypes.POINTER(TreeOutputs), _c_p]),
     "ddt_tree_from_log_probs": (ctypes.c_int, [_c_p, _c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64,
                                                ctypes.POINTER(TreeOutputs), _c_p]),
     "ddt_tree_mask_fill": (ctypes.c_int, [_c_p, ctypes.c_int, _c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_i64,

@@ -15,6 +15,7 @@
 // and an atomic counter); no CTA ever waits on another.
 
 #include <cstdio>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -830,4 +831,77 @@ extern "C" int ddt_tree_from_log_probs(const float* lp, const int64_t* ids, int6
         return check_launch("cudaFuncSetAttribute(tree_expand_kernel)");
     tree_expand_kernel<<<1, kThreads, smem, st>>>(lp, ids, (int)rows, (int)topk, (int)budget, root_token, start, *out);
     return check_launch("tree_expand_kernel");
+}
+
+// ---------------------------------------------------------------------------
+// Tree build for callers that cannot allocate device memory.
+//
+// Some callers of this library cannot call cudaMalloc: code running inside a
+// CUDA-graph capture, or a host application whose device memory is owned
+// by another allocator (a serving framework's memory pool, a game engine
+// budget) and that must not grow it behind that allocator's back.  For them
+// ddt_tree_build_noalloc runs the same kernel as ddt_tree_build, with its
+// scratch in a fixed 1 MiB array that lives in this library's device image.
+// Every GPU that loads the library holds that MiB until the process exits.
+// 1 MiB covers 15 draft rows x 151936 vocabulary up to a node budget of 512;
+// larger shapes are rejected with DDT_EUNSUPPORTED.
+// ---------------------------------------------------------------------------
+namespace ddt {
+namespace tree {
+
+constexpr size_t kNoAllocScratchBytes = size_t(1) << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch on `dev`.  In host code the symbol is
+// only a host-side stand-in, so the address is looked up with
+// cudaGetSymbolAddress once per device (with that device current) and cached.
+static int noalloc_scratch(int dev, void** out) {
+    static std::mutex mu;
+    static void* addr[64] = {nullptr};
+    if (dev < 0 || dev >= 64) return set_error(DDT_EUNSUPPORTED, "device %d out of range", dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p) {
+            cudaGetLastError();
+            return set_error(DDT_ECUDA, "cudaGetSymbolAddress(no-alloc scratch): %s", cudaGetErrorString(e));
+        }
+        addr[dev] = p;
+    }
+    *out = addr[dev];
+    return DDT_OK;
+}
+
+}  // namespace tree
+}  // namespace ddt
+
+extern "C" int ddt_tree_build_noalloc(const void* logits, int dtype, int64_t rows, int64_t vocab, int64_t row_stride,
+                                      int64_t budget, const int64_t* root_token, int64_t start,
+                                      const ddt_tree_outputs* out, ddt_stream_t stream) {
+    if (budget > 0 && rows > 0 && vocab > 0 && rows <= kMaxRows) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        const int64_t topk = budget < vocab ? budget : vocab;
+        int64_t chunks, chunk_len;
+        choose_chunks(rows, vocab, topk, ddt_sm_count(dev), &chunks, &chunk_len);
+        const size_t need = ws_layout(rows, chunks, topk).total;
+        if (need > kNoAllocScratchBytes)
+            return set_error(DDT_EUNSUPPORTED,
+                             "ddt_tree_build_noalloc: rows=%lld vocab=%lld budget=%lld needs %zu bytes of scratch, "
+                             "more than its fixed %zu; use ddt_tree_build with a caller workspace",
+                             (long long)rows, (long long)vocab, (long long)budget, need, kNoAllocScratchBytes);
+    }
+    int dev = 0;
+    cudaGetDevice(&dev);
+    void* scratch = nullptr;
+    int rc = noalloc_scratch(dev, &scratch);
+    if (rc) return rc;
+    // The array keeps whatever the previous call left.  The kernel's
+    // hand-off counters and error flags (the first 512 bytes) must start at
+    // zero, so they are cleared on the caller's stream before every launch.
+    if (cudaMemsetAsync(scratch, 0, 512, reinterpret_cast<cudaStream_t>(stream)) != cudaSuccess)
+        return check_launch("cudaMemsetAsync(no-alloc scratch)");
+    return ddt_tree_build(logits, dtype, rows, vocab, row_stride, budget, root_token, start, out, scratch,
+                          kNoAllocScratchBytes, stream);
 }

@@ -81,6 +81,26 @@ DDT_API int ddt_tree_build(const void* logits, int dtype, int64_t rows, int64_t 
                    int64_t budget, const int64_t* root_token /* device scalar, nullable */, int64_t start,
                    const ddt_tree_outputs* out, void* workspace, size_t workspace_bytes, ddt_stream_t stream);
 
+/* ddt_tree_build for callers that cannot allocate device memory.
+ * This entry point has no counterpart in the reference.  Some callers of this
+ * library cannot call cudaMalloc: code running inside a CUDA-graph capture,
+ * or a host application whose device memory is owned by another allocator
+ * (a serving framework's pool) and must not grow behind its back.  This call
+ * takes the same inputs and outputs as ddt_tree_build but no workspace: its
+ * scratch is a fixed 1 MiB array inside the library's device image, held by
+ * every GPU that loads the library until the process exits.  1 MiB covers 15
+ * draft rows x 151936 vocabulary up to a node budget of 512; larger shapes
+ * return DDT_EUNSUPPORTED.  It calls no cudaMalloc / cudaFree.
+ * The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress, with that device current); make that first call
+ * before any stream capture.  All calls share the one array: calls that
+ * overlap on the GPU (different streams without ordering) race.  Each call
+ * clears the counters at the start of the array on `stream` before its
+ * launch. */
+DDT_API int ddt_tree_build_noalloc(const void* logits, int dtype, int64_t rows, int64_t vocab, int64_t row_stride,
+                                   int64_t budget, const int64_t* root_token, int64_t start,
+                                   const ddt_tree_outputs* out, ddt_stream_t stream);
+
 /* Best-first expansion only, from given log-probs and ids (ddtree.py:146-189).
  * lp: [rows, topk] fp32, ids: [rows, topk] int64, both device. */
 DDT_API int ddt_tree_from_log_probs(const float* lp, const int64_t* ids, int64_t rows, int64_t topk, int64_t budget,
