@@ -480,8 +480,33 @@ def run_kernel_only(args, local):
         once(i)
     e1.record()
     torch.cuda.synchronize()
+    eager_us = e0.elapsed_time(e1) * 1e3 / args.steps
+    # the same launches captured once in a CUDA graph: device time without launch gaps
+    per_graph = LAYERS
+    stream = torch.cuda.Stream(device)
+    stream.wait_stream(torch.cuda.current_stream(device))
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        once(0)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(per_graph):
+                once(i)
+    torch.cuda.synchronize()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    reps = max(1, args.steps // per_graph)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(reps):
+            g.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    graph_us = e0.elapsed_time(e1) * 1e3 / (reps * per_graph)
+    del g
     print(json.dumps({"kernel": args.kernel, "launches": args.steps,
-                      "us_per_launch_eager": round(e0.elapsed_time(e1) * 1e3 / args.steps, 3),
+                      "us_per_launch_eager": round(eager_us, 3), "us_per_launch_graph": round(graph_us, 3),
                       "attention_status": kernels.attention_status(device)}))
 
 

@@ -364,6 +364,695 @@ attn_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ 
 }
 
 // ---------------------------------------------------------------------------
+// Split-key kernel: one CTA per (key split, M-tile pair, KV head), holding at
+// most two key tiles of 128 keys and up to two M tiles of its KV head.
+//
+// The rows of a KV head are cut into 128-row M tiles, taken two at a time
+// (tiles A and B, one softmax warpgroup each), plus a tail of <= 16 rows
+// that runs transposed on its own warpgroup: S_t^T = K Q_t^T (M = 128 keys,
+// N = 16) and O_t^T = V^T P_t^T (M = 128 dims, N = 16), its column max
+// and sum reduced with warp-wide redux instructions.  Every load is issued
+// when the CTA starts; the MMA warp then issues the products in the order
+// their operands become ready, and every barrier completes exactly once, so
+// each wait is on parity 0.
+//
+//   warps 0-3    softmax + epilogue of M tile A (TMEM lane = row)
+//   warps 4-7    softmax + epilogue of M tile B
+//   warps 8-11   tail softmax + epilogue (TMEM lane = key, then dim)
+//   warp 12      TMEM owner; runs the load and MMA schedule in step, one
+//                elected lane issuing each TMA copy and tcgen05.mma
+//                (warps 13-15 only complete the warpgroup so registers can
+//                move to the softmax warpgroups)
+//
+// Shared memory: Q_A, Q_B, K_0, K_1, V_0, V_1 (32 KB each), Q_t (4 KB),
+// P_t[2] (4 KB each).  P of a main tile goes to shared memory (the P.V
+// product reads it as an SS operand) into a slot whose last reader has
+// completed: P(A,0) -> K_0, P(B,0) -> Q_A, P(A,1) -> Q_B, P(B,1) -> K_1.
+// Since P does not stay in TMEM, an S buffer is free as soon as its softmax
+// has loaded it.
+// TMEM columns: S(A,0) then O_A at 0, S(B,0) then O_B at 128, S(A,1) at
+// 256, S(B,1) at 256 once S(A,1) has been loaded (at 384 without a tail),
+// tail S_t(j) at 384 + 16j and O_t(j) at 416 + 16j.  The two key tiles of a
+// main row merge online (lazy rescaling of O); the tail merges at the end.
+// ---------------------------------------------------------------------------
+namespace split {
+
+constexpr int kThreads = 512;
+constexpr uint32_t kSlot = 2 * kHalf;                 // 32 KB
+constexpr uint32_t kQA = 0, kQB = kSlot, kK0 = 2 * kSlot, kK1 = 3 * kSlot, kV0 = 4 * kSlot, kV1 = 5 * kSlot;
+constexpr uint32_t kQT = 6 * kSlot;                   // 16 rows x 128 dims: two 2 KB halves
+constexpr uint32_t kPT = kQT + 4096;                  // P_t(j): 16 rows x 128 keys, 4 KB each
+constexpr uint32_t kRed = kPT + 8192;                 // tail reductions and per-tile statistics
+constexpr uint32_t kBar = kRed + 4096;
+constexpr uint32_t kSmemBytes = kBar + 512 + 1024;
+constexpr uint32_t kTHalf = 16 * 128;
+constexpr uint32_t kColA = 0, kColB = 128, kCol1 = 256, kColT = 384;
+constexpr uint32_t kIdescQKt = idesc_bf16_f32(128, 16, false, false);
+constexpr uint32_t kIdescPVt = idesc_bf16_f32(128, 16, true, false);
+constexpr uint32_t kIdescPVs = idesc_bf16_f32(BM, HD, false, true);   // P K-major from shared memory
+constexpr float kFix = 16777216.f;                    // 2^24: fixed-point scale of tail probabilities
+
+struct Params {
+    int n_tokens, hq, hkv, group, tpt, past, n_kt, tpc, splits;
+    int n_mt, n_groups, tail_rows, tail_token0;
+    const uint32_t* vis;
+    int vis_words;
+    float scale_log2;
+    __nv_bfloat16* out;
+    int64_t o_stride_tok, o_stride_head;
+    __nv_bfloat16* part_o;
+    float* part_lse;
+    int* status;
+};
+
+// Barriers; each completes exactly once per CTA.
+enum : int {
+    bQ = 0,
+    bK0 = 1,       // + j
+    bV0 = 3,       // + j
+    bS0 = 5,       // + 2 * slot + j      (S ready)
+    bSt0 = 9,      // + j                 (tail S ready)
+    bFreeQA = 11,  // last MMA reading Q_A completed
+    bFreeK0 = 12,
+    bFreeQB = 13,
+    bFreeK1 = 14,
+    bX1 = 15,      // S(A,1) loaded: column block 256 may take S(B,1)
+    bP0 = 16,      // + 2 * slot + j      (P in shared memory)
+    bPt0 = 20,     // + j
+    bPV0 = 22,     // + 2 * slot + j      (P.V complete)
+    bPVt = 26,     // every tail P.V complete
+    bDrain = 27,
+    kNumBars = 28
+};
+
+__device__ __forceinline__ uint32_t p_slot(int slot, int j) {
+    return slot == 0 ? (j == 0 ? kK0 : kQB) : (j == 0 ? kQA : kK1);
+}
+__device__ __forceinline__ int free_bar(int slot, int j) {
+    return slot == 0 ? (j == 0 ? bFreeK0 : bFreeQB) : (j == 0 ? bFreeQA : bFreeK1);
+}
+__device__ __forceinline__ float warp_max(float v) {
+    float m;
+    asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(m) : "f"(v));
+    return m;
+}
+__device__ __forceinline__ uint32_t warp_sum_u32(uint32_t v) {
+    uint32_t s;
+    asm volatile("redux.sync.add.u32 %0, %1, 0xffffffff;" : "=r"(s) : "r"(v));
+    return s;
+}
+
+// Merge of one row's split partials: bf16 partials normalised by their own
+// sum, weights 2^(lse_s - max).  One warp: lane s loads split s's
+// log-sum-exp while every lane loads its 4 dims of up to CHUNK splits, all
+// in one batch of independent loads (neither depends on the max), so a row
+// costs one memory round trip per CHUNK splits.  Loads bypass L1: the partials
+// were written by other SMs during this launch.
+template <int CHUNK>
+__device__ __forceinline__ void merge_row(const __nv_bfloat16* part_o, const float* part_lse, int splits,
+                                          int64_t split_stride, int64_t base, int lane, __nv_bfloat16* dst) {
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f, wsum = 0.f, M = -INFINITY;
+    for (int s0 = 0; s0 < splits; s0 += CHUNK) {
+        const int ns = min(CHUNK, splits - s0);
+        const float l = lane < ns ? __ldcg(part_lse + (s0 + lane) * split_stride + base) : -INFINITY;
+        uint2 raw[CHUNK];
+#pragma unroll
+        for (int i = 0; i < CHUNK; ++i)
+            raw[i] = i < ns ? __ldcg(reinterpret_cast<const uint2*>(part_o + ((s0 + i) * split_stride + base) * HD) + lane)
+                            : make_uint2(0u, 0u);
+        float m;
+        asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(m) : "f"(l));
+        const float m_new = fmaxf(M, m);
+        if (m_new == -INFINITY) continue;
+        // rescale what earlier passes accumulated (only with more than CHUNK splits)
+        const float c = M == -INFINITY ? 0.f : exp2f(M - m_new);
+        a0 *= c;
+        a1 *= c;
+        a2 *= c;
+        a3 *= c;
+        wsum *= c;
+        M = m_new;
+        const float w_lane = l == -INFINITY ? 0.f : exp2f(l - M);
+#pragma unroll
+        for (int i = 0; i < CHUNK; ++i) {
+            if (i < ns) {
+                const float w = __shfl_sync(DDT_FULL_MASK, w_lane, i);
+                const __nv_bfloat162 x = *reinterpret_cast<const __nv_bfloat162*>(&raw[i].x);
+                const __nv_bfloat162 y = *reinterpret_cast<const __nv_bfloat162*>(&raw[i].y);
+                a0 = fmaf(w, __low2float(x), a0);
+                a1 = fmaf(w, __high2float(x), a1);
+                a2 = fmaf(w, __low2float(y), a2);
+                a3 = fmaf(w, __high2float(y), a3);
+                wsum += w;
+            }
+        }
+    }
+    const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+    __nv_bfloat162 a = __floats2bfloat162_rn(a0 * inv, a1 * inv);
+    __nv_bfloat162 b2 = __floats2bfloat162_rn(a2 * inv, a3 * inv);
+    uint2 pkt;
+    pkt.x = *reinterpret_cast<uint32_t*>(&a);
+    pkt.y = *reinterpret_cast<uint32_t*>(&b2);
+    *reinterpret_cast<uint2*>(dst + lane * 4) = pkt;
+}
+
+// Eight K16 steps of one product, fully unrolled: the k-step offsets are
+// compile-time constants in 16-byte units (hi per group of four steps, lo
+// per step), so each step costs one 64-bit add and the MMA; a single
+// issuing thread can then keep pace with the tensor core.  A 128-row K-major
+// tile has (hi, lo) = (1024, 2), a 16-row K-major tile (128, 2) and the
+// MN-major V tile (512, 128).  A descriptor advances by adding offset >> 4
+// (shared addresses fit its 14-bit field).
+template <uint32_t AH, uint32_t AL, uint32_t BH, uint32_t BL>
+__device__ __forceinline__ void mma8(uint32_t d, uint64_t ad, uint64_t bd, uint32_t idesc, uint32_t acc0) {
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk)
+        mma_ss(d, ad + (uint64_t)((kk >> 2) * AH + (kk & 3) * AL), bd + (uint64_t)((kk >> 2) * BH + (kk & 3) * BL),
+               idesc, kk == 0 ? acc0 : 1u);
+}
+
+// Epilogue of one 128-row M tile.  Each thread owns one row of O in TMEM.
+// Rows are normalised, packed to bf16 and staged in the tile's own last P
+// slot (dead once its last P.V completed) with the 16-byte chunks of row r
+// XOR-swizzled by r & 15; then each warp writes two whole rows per
+// instruction with coalesced 16-byte stores.  One split: rows go to
+// out[token][head]; several: to the bf16 partial part_o[split][g][r]
+// (r = row within the KV head) with its log-sum-exp in part_lse.
+__device__ __forceinline__ void tile_epilogue(const Params& p, uint32_t o_col, unsigned char* stage, int row, int qw,
+                                              int lane, int mt, int split, int g, float inv, float lse, int bar_id) {
+    const int rows_head = p.group * p.n_tokens;
+    {
+        uint32_t r[4][32];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) tmem_ld32(o_col + q * 32, r[q]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+                uint4 pkt;
+                uint32_t* w = reinterpret_cast<uint32_t*>(&pkt);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(r[q][v * 8 + 2 * e]) * inv,
+                                                             __uint_as_float(r[q][v * 8 + 2 * e + 1]) * inv);
+                    w[e] = *reinterpret_cast<uint32_t*>(&h);
+                }
+                const int chunk = q * 4 + v;
+                *reinterpret_cast<uint4*>(stage + row * 256 + ((chunk ^ (row & 15)) << 4)) = pkt;
+            }
+        }
+    }
+    const int rg = mt * BM + row;
+    if (p.splits > 1 && rg < rows_head) p.part_lse[((int64_t)split * p.hkv + g) * rows_head + rg] = lse;
+    named_bar_sync(bar_id, 128);
+    const int chunk = lane & 15;
+#pragma unroll 4
+    for (int it = 0; it < 16; ++it) {
+        const int rl = qw * 32 + it * 2 + (lane >> 4);
+        const int rgl = mt * BM + rl;
+        if (rgl >= rows_head) continue;
+        const uint4 v = *reinterpret_cast<const uint4*>(stage + rl * 256 + ((chunk ^ (rl & 15)) << 4));
+        __nv_bfloat16* dst;
+        if (p.splits == 1) {
+            const int token = rgl / p.group, head = g * p.group + rgl % p.group;
+            dst = p.out + (int64_t)token * p.o_stride_tok + (int64_t)head * p.o_stride_head;
+        } else {
+            dst = p.part_o + (((int64_t)split * p.hkv + g) * rows_head + rgl) * HD;
+        }
+        *reinterpret_cast<uint4*>(dst + chunk * 8) = v;
+    }
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tqt,
+                       const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
+                       const Params p) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBar);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
+    float* wmax = reinterpret_cast<float*>(smem + kRed);   // [j][4 warps][16]
+    float* wsum = wmax + 128;                               // [j][4 warps][16]
+    float* tmax = wsum + 128;                               // [j][16] column max of tile j
+    float* wts = tmax + 32;                                 // [j][16] merge weights, then [16] lse
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int split = blockIdx.x, grp = blockIdx.y, g = blockIdx.z;
+    const int kt0 = split * p.tpc;
+    const int nj = min(p.tpc, p.n_kt - kt0);     // 1 or 2
+    const int mA = 2 * grp, mB = 2 * grp + 1;
+    const bool hasA = mA < p.n_mt, hasB = mB < p.n_mt;
+    const bool hasT = grp == p.n_groups - 1 && p.tail_rows > 0;
+    const bool shareX1 = hasT && hasB && nj == 2;   // S(B,1) waits for S(A,1) to leave column block 256
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kNumBars; ++i) {
+            const bool by_wg = (i >= bP0 && i < bP0 + 4) || i == bPt0 || i == bPt0 + 1 || i == bX1;
+            mbar_init(&bars[i], by_wg ? 128 : 1);
+        }
+        fence_mbar_init();
+    }
+    if (warp == 12) {
+        tmem_alloc(tmem_slot, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t s_addr = smem_u32(smem);
+
+    // 512 threads x 128 registers at launch: warpgroup 3 gives 88 per thread,
+    // warpgroup 2 gives 56, the two softmax warpgroups take 72 each.  Each
+    // role's setmaxnreg sits in its own branch so the compiler sizes that
+    // role's code to the new limit; the code after the branches is trivial.
+    if (warp >= 12) {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 40;\n" ::: "memory");
+        if (warp == 12) {
+            // The whole warp runs this branch in step, so the operand
+            // descriptors are warp-uniform values; one elected lane issues
+            // each TMA copy, MMA and commit.
+            const bool leader = elect_one_sync();
+            // ------------------------------------------------------------ loads
+            if (leader) {
+            prefetch_tmap(&tq);
+            prefetch_tmap(&tk);
+            prefetch_tmap(&tv);
+            const uint64_t kv_policy = policy_evict_first();
+            const uint32_t qbytes = (hasA ? kSlot : 0) + (hasB ? kSlot : 0) + (hasT ? 2 * kTHalf : 0);
+            mbar_arrive_expect_tx(&bars[bQ], qbytes);
+            if (hasA) {
+                tma_load_3d(smem + kQA, &tq, 0, g * p.group, mA * p.tpt, &bars[bQ]);
+                tma_load_3d(smem + kQA + kHalf, &tq, 64, g * p.group, mA * p.tpt, &bars[bQ]);
+            }
+            if (hasB) {
+                tma_load_3d(smem + kQB, &tq, 0, g * p.group, mB * p.tpt, &bars[bQ]);
+                tma_load_3d(smem + kQB + kHalf, &tq, 64, g * p.group, mB * p.tpt, &bars[bQ]);
+            }
+            if (hasT) {
+                prefetch_tmap(&tqt);
+                tma_load_3d(smem + kQT, &tqt, 0, g * p.group, p.tail_token0, &bars[bQ]);
+                tma_load_3d(smem + kQT + kTHalf, &tqt, 64, g * p.group, p.tail_token0, &bars[bQ]);
+            }
+            for (int j = 0; j < nj; ++j) {
+                const int key0 = (kt0 + j) * BN;
+                unsigned char* kb = smem + (j ? kK1 : kK0);
+                mbar_arrive_expect_tx(&bars[bK0 + j], kSlot);
+                tma_load_3d_hint(kb, &tk, 0, key0, g, &bars[bK0 + j], kv_policy);
+                tma_load_3d_hint(kb + kHalf, &tk, 64, key0, g, &bars[bK0 + j], kv_policy);
+            }
+            for (int j = 0; j < nj; ++j) {
+                const int key0 = (kt0 + j) * BN;
+                unsigned char* vb = smem + (j ? kV1 : kV0);
+                mbar_arrive_expect_tx(&bars[bV0 + j], kSlot);
+                tma_load_3d_hint(vb, &tv, 0, key0, g, &bars[bV0 + j], kv_policy);
+                tma_load_3d_hint(vb + kHalf, &tv, 64, key0, g, &bars[bV0 + j], kv_policy);
+            }
+            }
+            __syncwarp();
+            // ------------------------------------------------------------ MMA issue
+            auto desc = [&](uint32_t off, uint32_t lbo) { return smem_desc_sw128(s_addr + off, lbo, 1024); };
+            // Issue order follows the order operands become ready: S products as
+            // K tiles land, then each P.V as its P is written (main tiles before
+            // the tail, whose result is needed last).  Waits suspend in hardware.
+            auto s_main = [&](int sl, int j, uint32_t col) {
+                if (leader) {
+                    mma8<1024, 2, 1024, 2>(tmem + col, desc(sl ? kQB : kQA, 16), desc(j ? kK1 : kK0, 16), kIdescQK, 0u);
+                    mma_commit(&bars[bS0 + 2 * sl + j]);
+                }
+            };
+            auto s_tail = [&](int j) {
+                if (leader) {
+                    mma8<1024, 2, 128, 2>(tmem + kColT + 16 * j, desc(j ? kK1 : kK0, 16), desc(kQT, 16), kIdescQKt, 0u);
+                    mma_commit(&bars[bSt0 + j]);
+                }
+            };
+            auto pv_main = [&](int sl, int j) {
+                if (leader) {
+                    mma8<1024, 2, 512, 128>(tmem + (sl ? kColB : kColA), desc(p_slot(sl, j), 16), desc(j ? kV1 : kV0, kHalf),
+                                            kIdescPVs, j > 0 ? 1u : 0u);
+                    mma_commit(&bars[bPV0 + 2 * sl + j]);
+                }
+            };
+            auto pv_tail = [&](int j) {
+                if (leader)
+                    mma8<512, 128, 128, 2>(tmem + kColT + 32 + 16 * j, desc(j ? kV1 : kV0, kHalf), desc(kPT + j * 4096, 16),
+                                           kIdescPVt, 0u);
+            };
+            auto commit = [&](int b) {
+                if (leader) mma_commit(&bars[b]);
+            };
+            auto wait = [&](int b) -> bool {
+                const bool r = mbar_wait(&bars[b], 0);
+                tc_fence_after();
+                return __all_sync(DDT_FULL_MASK, r);
+            };
+            bool ok = wait(bQ) && wait(bK0);
+            if (ok) {
+                if (hasA) s_main(0, 0, kColA);
+                if (hasB) s_main(1, 0, kColB);
+                if (hasT) s_tail(0);
+                commit(bFreeK0);
+                if (nj == 1) {
+                    commit(bFreeQA);
+                    commit(bFreeQB);
+                }
+            }
+            if (ok && nj > 1) {
+                ok = wait(bK0 + 1);
+                if (ok) {
+                    if (hasA) s_main(0, 1, kCol1);
+                    commit(bFreeQA);
+                    if (hasT) s_tail(1);
+                    if (!shareX1) {
+                        if (hasB) s_main(1, 1, hasT ? kCol1 : kColT);
+                        commit(bFreeQB);
+                        commit(bFreeK1);
+                    }
+                }
+            }
+            if (ok) ok = wait(bV0);
+            if (ok && hasA) {
+                ok = wait(bP0 + 0);
+                if (ok) pv_main(0, 0);
+            }
+            if (ok && shareX1) {
+                ok = wait(bX1);
+                if (ok) {
+                    s_main(1, 1, kCol1);
+                    commit(bFreeQB);
+                    commit(bFreeK1);
+                }
+            }
+            if (ok && hasB) {
+                ok = wait(bP0 + 2);
+                if (ok) pv_main(1, 0);
+            }
+            if (ok && hasT) {
+                ok = wait(bPt0);
+                if (ok) pv_tail(0);
+            }
+            if (ok && nj > 1) {
+                ok = wait(bV0 + 1);
+                if (ok && hasA) {
+                    ok = wait(bP0 + 1);
+                    if (ok) pv_main(0, 1);
+                }
+                if (ok && hasB) {
+                    ok = wait(bP0 + 3);
+                    if (ok) pv_main(1, 1);
+                }
+                if (ok && hasT) {
+                    ok = wait(bPt0 + 1);
+                    if (ok) pv_tail(1);
+                }
+            }
+            if (ok && hasT) commit(bPVt);
+            __syncwarp();
+            if (!ok && leader) flag_error(p.status, 2);
+            // drain: nothing this warp issued may still be in flight when the CTA exits
+            if (leader) mma_commit(&bars[bDrain]);
+            __syncwarp();
+            mbar_wait(&bars[bDrain], 0);
+            for (int j = 0; j < nj; ++j) {
+                mbar_wait(&bars[bK0 + j], 0);
+                mbar_wait(&bars[bV0 + j], 0);
+            }
+            mbar_wait(&bars[bQ], 0);
+        }
+    } else if (warp < 8) {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 200;\n" ::: "memory");
+        // ---------------------------------------------------------------- softmax of M tile A / B
+        const int slot = warp >> 2;
+        const bool has = slot == 0 ? hasA : hasB;
+        const int qw = warp & 3;
+        const int row = qw * 32 + lane;
+        const uint32_t lane_addr = (uint32_t)(qw * 32) << 16;
+        const int mt = slot == 0 ? mA : mB;
+        const int rows_head = p.group * p.n_tokens;
+        const int rg = mt * BM + row;
+        const bool valid = rg < rows_head;
+        const int token = rg / p.group;
+        const uint32_t o_col = tmem + lane_addr + (slot ? kColB : kColA);
+        float m_ref = -INFINITY, l = 0.f;
+        bool ok = true;
+        if (has) {
+            const uint32_t* vrow = valid ? p.vis + (int64_t)token * p.vis_words : p.vis;
+            const float sl2 = p.scale_log2;
+            for (int j = 0; j < nj; ++j) {
+                const uint32_t s_col =
+                    tmem + lane_addr + (j == 0 ? (slot ? kColB : kColA) : (slot == 0 || hasT ? kCol1 : kColT));
+                ok = ok && mbar_wait(&bars[bS0 + 2 * slot + j], 0);
+                tc_fence_after();
+                const int u0 = (kt0 + j) * BN - p.past;
+                const bool masked = u0 + BN > 0;
+                uint32_t r[4][32];
+                uint32_t vb[4];
+                if (ok) {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) tmem_ld32(s_col + q * 32, r[q]);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+                        vb[q] = masked ? vis_bits(vrow, p.vis_words, u0 + q * 32, p.n_tokens, valid) : 0xffffffffu;
+                    tmem_wait_ld();
+                }
+                if (slot == 0 && j == 1 && shareX1) {
+                    tc_fence_before();
+                    mbar_arrive(&bars[bX1]);
+                }
+                if (!ok) break;
+                float mk[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) mk[e] = -INFINITY;
+                if (masked) {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+#pragma unroll
+                        for (int c = 0; c < 32; ++c)
+                            mk[c & 7] = fmaxf(mk[c & 7], ((vb[q] >> c) & 1u) ? __uint_as_float(r[q][c]) : -INFINITY);
+                } else {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+#pragma unroll
+                        for (int c = 0; c < 32; ++c) mk[c & 7] = fmaxf(mk[c & 7], __uint_as_float(r[q][c]));
+                }
+                const float mx = fmaxf(fmaxf(fmaxf(mk[0], mk[1]), fmaxf(mk[2], mk[3])),
+                                       fmaxf(fmaxf(mk[4], mk[5]), fmaxf(mk[6], mk[7])));
+                const float m_new = fmaxf(m_ref, mx * sl2);
+                if (j == 0) {
+                    m_ref = m_new;
+                } else if (m_new > m_ref + 8.0f) {
+                    // rare: the running max grew by more than 2^8; rescale O once P.V of tile 0 is done
+                    const float alpha = ex2_approx(m_ref - m_new);
+                    ok = mbar_wait(&bars[bPV0 + 2 * slot], 0);
+                    if (!ok) break;
+                    tc_fence_after();
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        uint32_t o[32];
+                        tmem_ld32(o_col + q * 32, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+                        tmem_st32(o_col + q * 32, o);
+                    }
+                    tmem_wait_st();
+                    tc_fence_before();
+                    l *= alpha;
+                    m_ref = m_new;
+                }
+                const float neg_m = m_ref == -INFINITY ? 0.f : -m_ref;
+                ok = mbar_wait(&bars[free_bar(slot, j)], 0);
+                if (!ok) break;
+                unsigned char* pdst = smem + p_slot(slot, j) + (row >> 3) * 1024 + (row & 7) * 128;
+                float ls[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    uint32_t pk[16];
+#pragma unroll
+                    for (int c = 0; c < 32; c += 2) {
+                        float p0 = ex2_approx(fmaf(__uint_as_float(r[q][c]), sl2, neg_m));
+                        float p1 = ex2_approx(fmaf(__uint_as_float(r[q][c + 1]), sl2, neg_m));
+                        if (masked) {
+                            p0 = ((vb[q] >> c) & 1u) ? p0 : 0.f;
+                            p1 = ((vb[q] >> (c + 1)) & 1u) ? p1 : 0.f;
+                        }
+                        ls[(c >> 1) & 3] += p0 + p1;
+                        __nv_bfloat162 h = __floats2bfloat162_rn(p0, p1);
+                        pk[c >> 1] = *reinterpret_cast<uint32_t*>(&h);
+                    }
+                    // keys 32q .. 32q+31: half q >> 1, 16-byte chunks (q & 1) * 4 .. + 3
+                    unsigned char* hb = pdst + (q >> 1) * kHalf;
+#pragma unroll
+                    for (int v = 0; v < 4; ++v) {
+                        const int chunk = (q & 1) * 4 + v;
+                        *reinterpret_cast<uint4*>(hb + ((chunk ^ (row & 7)) << 4)) =
+                            make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+                    }
+                }
+                l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+                fence_proxy_async_smem();
+                mbar_arrive(&bars[bP0 + 2 * slot + j]);
+            }
+            if (ok) ok = mbar_wait(&bars[bPV0 + 2 * slot + nj - 1], 0);
+            if (!ok) flag_error(p.status, 3);
+            tc_fence_after();
+            // every thread of the warpgroup reaches the named barrier inside
+            if (ok)
+                tile_epilogue(p, o_col, smem + p_slot(slot, nj - 1), row, qw, lane, mt, split, g,
+                              l > 0.f ? 1.f / l : 0.f, l > 0.f ? m_ref + log2f(l) : -INFINITY, 2 + slot);
+            else
+                named_bar_sync(2 + slot, 128);
+        }
+    } else {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 72;\n" ::: "memory");
+        // ---------------------------------------------------------------- tail (transposed), warps 8-11
+        const int tw = warp - 8;
+        const int k = tw * 32 + lane;               // key lane (S_t^T), then dim lane (O_t^T)
+        const uint32_t lane_addr = (uint32_t)(tw * 32) << 16;
+        if (hasT) {
+            const int nt = p.tail_rows;
+            const float sl2 = p.scale_log2;
+            bool ok = true;
+            for (int j = 0; j < nj; ++j) {
+                ok = ok && mbar_wait(&bars[bSt0 + j], 0);
+                tc_fence_after();
+                uint32_t r[16];
+                if (ok) {
+                    tmem_ld16(tmem + lane_addr + kColT + 16 * j, r);
+                    tmem_wait_ld();
+                }
+                const int u = (kt0 + j) * BN + k - p.past;
+                float s[16];
+#pragma unroll
+                for (int c = 0; c < 16; ++c) {
+                    bool vis = false;
+                    if (c < nt) {
+                        const int token = p.tail_token0 + c / p.group;
+                        if (u < 0)
+                            vis = true;
+                        else if (u < p.n_tokens)
+                            vis = (__ldg(p.vis + (int64_t)token * p.vis_words + (u >> 5)) >> (u & 31)) & 1u;
+                    }
+                    s[c] = (vis && ok) ? __uint_as_float(r[c]) * sl2 : -INFINITY;
+                }
+                // column max: one redux per warp, then one exchange across the 4 warps
+                float* wm = wmax + j * 64;
+#pragma unroll
+                for (int c = 0; c < 16; ++c) {
+                    if (c < nt) {
+                        const float v = warp_max(s[c]);
+                        if (lane == 0) wm[tw * 16 + c] = v;
+                    }
+                }
+                named_bar_sync(1, 128);
+                float* ws = wsum + j * 64;
+#pragma unroll
+                for (int c = 0; c < 16; ++c) {
+                    if (c < nt) {
+                        const float mt = fmaxf(fmaxf(wm[c], wm[16 + c]), fmaxf(wm[32 + c], wm[48 + c]));
+                        const float pc = ex2_approx(s[c] - (mt == -INFINITY ? 0.f : mt));   // s = -inf gives 0
+                        s[c] = pc;
+                        // column sum in 2^-24 fixed point: every p <= 1, so a warp's sum fits 32 bits
+                        const uint32_t sum = warp_sum_u32(__float2uint_rn(pc * kFix));
+                        if (lane == 0) ws[tw * 16 + c] = (float)sum * (1.f / kFix);
+                        if (k == 0) tmax[j * 16 + c] = mt;
+                    } else {
+                        s[c] = 0.f;
+                    }
+                }
+                // P_t(j) as the [16 rows x 128 keys] K-major, 128-byte-swizzled B operand
+                unsigned char* ptb = smem + kPT + j * 4096 + (k >> 6) * kTHalf;
+                const int kk = k & 63;
+#pragma unroll
+                for (int c = 0; c < 16; ++c) {
+                    const uint32_t off = c * 128 + ((((kk >> 3) ^ (c & 7)) & 7) << 4) + (kk & 7) * 2;
+                    *reinterpret_cast<__nv_bfloat16*>(ptb + off) = __float2bfloat16_rn(s[c]);
+                }
+                fence_proxy_async_smem();
+                mbar_arrive(&bars[bPt0 + j]);
+            }
+            if (ok) ok = mbar_wait(&bars[bPVt], 0);
+            named_bar_sync(1, 128);   // every tile's statistics are visible
+            // thread c < nt merges column c's per-tile statistics into the
+            // weights of O_t(j) and the column's log-sum-exp
+            if (k < nt) {
+                const float m0 = tmax[k], m1 = nj > 1 ? tmax[16 + k] : -INFINITY;
+                const float l0 = wsum[k] + wsum[16 + k] + wsum[32 + k] + wsum[48 + k];
+                const float l1 = nj > 1 ? wsum[64 + k] + wsum[80 + k] + wsum[96 + k] + wsum[112 + k] : 0.f;
+                const float mm = fmaxf(m0, m1);
+                const float w0 = m0 == -INFINITY ? 0.f : ex2_approx(m0 - mm);
+                const float w1 = m1 == -INFINITY ? 0.f : ex2_approx(m1 - mm);
+                const float L = w0 * l0 + w1 * l1;
+                const float inv = L > 0.f ? 1.f / L : 0.f;
+                wts[k] = w0 * inv;
+                wts[16 + k] = w1 * inv;
+                wts[32 + k] = L > 0.f ? mm + log2f(L) : -INFINITY;
+            }
+            named_bar_sync(1, 128);
+            if (!ok) {
+                flag_error(p.status, 4);
+            } else {
+                tc_fence_after();
+                float acc[16];
+#pragma unroll
+                for (int c = 0; c < 16; ++c) acc[c] = 0.f;
+                for (int j = 0; j < nj; ++j) {
+                    uint32_t o[16];
+                    tmem_ld16(tmem + lane_addr + kColT + 32 + 16 * j, o);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int c = 0; c < 16; ++c) acc[c] = fmaf(wts[16 * j + c], __uint_as_float(o[c]), acc[c]);
+                }
+                const int d = k;
+                const int rows_head = p.group * p.n_tokens;
+#pragma unroll
+                for (int c = 0; c < 16; ++c) {
+                    if (c < nt) {
+                        const int token = p.tail_token0 + c / p.group;
+                        const int head = g * p.group + c % p.group;
+                        if (token < p.n_tokens) {
+                            if (p.splits == 1) {
+                                p.out[(int64_t)token * p.o_stride_tok + (int64_t)head * p.o_stride_head + d] =
+                                    __float2bfloat16_rn(acc[c]);
+                            } else {
+                                const int64_t prow =
+                                    ((int64_t)split * p.hkv + g) * rows_head + p.tail_token0 * p.group + c;
+                                p.part_o[prow * HD + d] = __float2bfloat16_rn(acc[c]);
+                                if (d == 0) p.part_lse[prow] = wts[32 + c];
+                            }
+                        }
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 12) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+// Merge of the split partials: one warp per row over hkv * rows_head rows.
+__global__ void __launch_bounds__(128)
+combine_kernel(const __nv_bfloat16* __restrict__ part_o, const float* __restrict__ part_lse, int splits, int hkv,
+               int group, int n_tokens, __nv_bfloat16* out, int64_t o_stride_tok, int64_t o_stride_head) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int rows_head = group * n_tokens;
+    const int64_t row = (int64_t)blockIdx.x * 4 + warp;
+    if (row >= (int64_t)hkv * rows_head) return;
+    const int g = (int)(row / rows_head), r = (int)(row % rows_head);
+    const int token = r / group, head = g * group + r % group;
+    merge_row<16>(part_o, part_lse, splits, (int64_t)hkv * rows_head, (int64_t)g * rows_head + r, lane,
+              out + (int64_t)token * o_stride_tok + (int64_t)head * o_stride_head);
+}
+
+}  // namespace split
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -422,17 +1111,138 @@ static Plan plan_for(int64_t n_tokens, int64_t hq, int64_t hkv, int64_t past, in
     return pl;
 }
 
+// Split-kernel workspace: status word, then the partials.
+constexpr size_t kSplitPartOffset = 256;
+
+struct SplitPlan {
+    int group, tpt, n_kt, tpc, splits, n_mt, n_groups, tail_rows, tail_token0;
+    bool usable;
+    size_t ws_bytes;
+};
+
+// The split kernel applies when the rows of a KV head are too few to fill
+// the GPU without splitting keys (fewer M tiles x KV heads than SMs), the
+// tail fits the 16-column transposed pass, and at most 16 waves of CTAs of
+// at most two key tiles each cover the keys.
+static SplitPlan plan_split(int64_t n_tokens, int64_t hq, int64_t hkv, int64_t past, int sms) {
+    SplitPlan pl = {};
+    if (sms <= 0) sms = 148;
+    pl.group = (int)(hq / hkv);
+    pl.tpt = BM / pl.group;
+    const int64_t rows = (int64_t)pl.group * n_tokens;
+    int64_t n_mt = rows / BM, rem = rows % BM, tail = 0;
+    if (rem > 16 || (rem > 0 && 16 % pl.group != 0))
+        n_mt += 1;
+    else
+        tail = rem;
+    pl.n_mt = (int)n_mt;
+    pl.tail_rows = (int)tail;
+    pl.tail_token0 = (int)((rows - tail) / pl.group);
+    pl.n_groups = (int)(n_mt > 0 ? (n_mt + 1) / 2 : 1);
+    pl.n_kt = (int)ceil_div(past + n_tokens, BN);
+    const int64_t units = hkv * pl.n_groups;
+    pl.tpc = (int64_t)pl.n_kt * units <= sms ? 1 : 2;
+    pl.splits = (int)ceil_div(pl.n_kt, pl.tpc);
+    const int64_t ctas = (int64_t)pl.splits * units;
+    pl.usable = ceil_div(rows, (int64_t)BM) * hkv < sms && ctas <= 16 * (int64_t)sms;
+    size_t o = kSplitPartOffset;
+    if (pl.splits > 1) {
+        o += sizeof(__nv_bfloat16) * (size_t)pl.splits * n_tokens * hq * HD;
+        o = (o + 255) & ~size_t(255);
+        o += sizeof(float) * (size_t)pl.splits * n_tokens * hq;
+        o = (o + 255) & ~size_t(255);
+    }
+    pl.ws_bytes = o;
+    return pl;
+}
+
 }  // namespace attn
 }  // namespace ddt
 
 using namespace ddt;
 using namespace ddt::attn;
 
+// Launch of the split kernel (and, with several key splits, the merge).
+static int launch_split(const ddt_attention_args* a, const SplitPlan& sp, void* workspace, size_t workspace_bytes,
+                        ddt_stream_t stream) {
+    if (!workspace || workspace_bytes < sp.ws_bytes || reinterpret_cast<uintptr_t>(workspace) % 256)
+        return set_error(DDT_EWORKSPACE, "attention workspace needs %zu bytes (256-aligned), got %zu", sp.ws_bytes,
+                         workspace_bytes);
+    const int64_t group = a->hq / a->hkv;
+    const int64_t kv_len = a->past_length + a->n_tokens;
+    // K/V maps end at past + n_tokens: rows of a larger cache past the tree
+    // read as zeros, so whatever they hold never reaches P.V.
+    CUtensorMap tq, tqt, tk, tv;
+    int rc = make_map(&tq, a->q, HD, a->hq, a->n_tokens, a->q_stride_head * 2, a->q_stride_tok * 2, 64,
+                      (uint32_t)group, (uint32_t)sp.tpt);
+    if (!rc && sp.tail_rows > 0)
+        rc = make_map(&tqt, a->q, HD, a->hq, a->n_tokens, a->q_stride_head * 2, a->q_stride_tok * 2, 64,
+                      (uint32_t)group, (uint32_t)(16 / group));
+    else
+        tqt = tq;
+    if (!rc) rc = make_map(&tk, a->k, HD, kv_len, a->hkv, a->kv_stride_row * 2, a->kv_stride_head * 2, 64, BN, 1);
+    if (!rc) rc = make_map(&tv, a->v, HD, kv_len, a->hkv, a->kv_stride_row * 2, a->kv_stride_head * 2, 64, BN, 1);
+    if (rc) return rc;
+    static std::once_flag once;
+    static cudaError_t attr_err = cudaSuccess;
+    std::call_once(once, [] {
+        attr_err = cudaFuncSetAttribute(split::tree_attn_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)split::kSmemBytes);
+    });
+    if (attr_err != cudaSuccess) return set_error(DDT_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(attr_err));
+    unsigned char* ws = static_cast<unsigned char*>(workspace);
+    split::Params q;
+    q.n_tokens = (int)a->n_tokens;
+    q.hq = (int)a->hq;
+    q.hkv = (int)a->hkv;
+    q.group = sp.group;
+    q.tpt = sp.tpt;
+    q.past = (int)a->past_length;
+    q.n_kt = sp.n_kt;
+    q.tpc = sp.tpc;
+    q.splits = sp.splits;
+    q.n_mt = sp.n_mt;
+    q.n_groups = sp.n_groups;
+    q.tail_rows = sp.tail_rows;
+    q.tail_token0 = sp.tail_token0;
+    q.vis = a->visibility;
+    q.vis_words = (int)a->vis_words;
+    q.scale_log2 = a->scale * 1.4426950408889634f;
+    q.out = static_cast<__nv_bfloat16*>(a->out);
+    q.o_stride_tok = a->o_stride_tok;
+    q.o_stride_head = a->o_stride_head;
+    q.status = reinterpret_cast<int*>(ws);
+    q.part_o = nullptr;
+    q.part_lse = nullptr;
+    if (sp.splits > 1) {
+        size_t o = kSplitPartOffset;
+        q.part_o = reinterpret_cast<__nv_bfloat16*>(ws + o);
+        o += sizeof(__nv_bfloat16) * (size_t)sp.splits * a->n_tokens * a->hq * HD;
+        o = (o + 255) & ~size_t(255);
+        q.part_lse = reinterpret_cast<float*>(ws + o);
+    }
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    dim3 grid((unsigned)sp.splits, (unsigned)sp.n_groups, (unsigned)a->hkv);
+    split::tree_attn_split_kernel<<<grid, split::kThreads, split::kSmemBytes, st>>>(tq, tqt, tk, tv, q);
+    rc = check_launch("tree_attn_split_kernel");
+    if (rc) return rc;
+    if (sp.splits > 1) {
+        const int64_t rows = a->n_tokens * a->hq;
+        split::combine_kernel<<<(unsigned)ceil_div(rows, 4), 128, 0, st>>>(q.part_o, q.part_lse, sp.splits,
+                                                                          (int)a->hkv, sp.group, (int)a->n_tokens,
+                                                                          q.out, a->o_stride_tok, a->o_stride_head);
+        rc = check_launch("split_combine_kernel");
+    }
+    return rc;
+}
+
 extern "C" size_t ddt_tree_attention_workspace_size(int64_t n_tokens, int64_t hq, int64_t hkv, int64_t past_length,
                                                     int device) {
     if (n_tokens <= 0 || hq <= 0 || hkv <= 0 || hq % hkv || past_length < 0) return 256;
     const int sms = ddt_sm_count(device);
-    return plan_for(n_tokens, hq, hkv, past_length, sms > 0 ? sms : 148).ws_bytes;
+    const size_t a = plan_for(n_tokens, hq, hkv, past_length, sms > 0 ? sms : 148).ws_bytes;
+    const SplitPlan sp = plan_split(n_tokens, hq, hkv, past_length, sms);
+    return sp.usable && sp.ws_bytes > a ? sp.ws_bytes : a;
 }
 
 extern "C" int ddt_tree_attention(const ddt_attention_args* a, void* workspace, size_t workspace_bytes,
@@ -462,13 +1272,16 @@ extern "C" int ddt_tree_attention(const ddt_attention_args* a, void* workspace, 
     if (!workspace || workspace_bytes < pl.ws_bytes || reinterpret_cast<uintptr_t>(workspace) % 256)
         return set_error(DDT_EWORKSPACE, "attention workspace needs %zu bytes (256-aligned), got %zu", pl.ws_bytes,
                          workspace_bytes);
+    const SplitPlan sp = plan_split(a->n_tokens, a->hq, a->hkv, a->past_length, ddt_sm_count(dev));
+    if (sp.usable) return launch_split(a, sp, workspace, workspace_bytes, stream);
     CUtensorMap tq, tk, tv;
     int rc = make_map(&tq, a->q, HD, a->hq, a->n_tokens, a->q_stride_head * 2, a->q_stride_tok * 2, 64,
                       (uint32_t)group, (uint32_t)pl.tpt);
     if (rc) return rc;
-    rc = make_map(&tk, a->k, HD, a->kv_rows, a->hkv, a->kv_stride_row * 2, a->kv_stride_head * 2, 64, BN, 1);
+    // K/V maps end at past + n_tokens: cache rows past the tree read as zeros
+    rc = make_map(&tk, a->k, HD, a->past_length + a->n_tokens, a->hkv, a->kv_stride_row * 2, a->kv_stride_head * 2, 64, BN, 1);
     if (rc) return rc;
-    rc = make_map(&tv, a->v, HD, a->kv_rows, a->hkv, a->kv_stride_row * 2, a->kv_stride_head * 2, 64, BN, 1);
+    rc = make_map(&tv, a->v, HD, a->past_length + a->n_tokens, a->hkv, a->kv_stride_row * 2, a->kv_stride_head * 2, 64, BN, 1);
     if (rc) return rc;
     static std::once_flag attr_once;
     static cudaError_t attr_err = cudaSuccess;

@@ -64,6 +64,12 @@ def test_matches_hf_sdpa_fixtures(golden_attention):
     (50, 17, 16, 2),        # group 8
     (700, 40, 4, 2),        # group 2
     (2500, 65, 32, 8),
+    (4096, 4, 32, 8),       # 16 rows: tail pass only
+    (4096, 5, 32, 8),       # 20 rows: one padded M tile
+    (900, 97, 32, 8),       # 388 rows: an M-tile pair, then one M tile + tail
+    (1000, 9, 32, 2),       # group 16: one M tile + 16-row tail
+    (20000, 65, 32, 8),     # long context: several waves of key splits
+    (64, 600, 32, 8),       # many M tiles: unsplit kernel
 ])
 def test_random_trees_vs_float64(past, n, hq, hkv):
     from ddtree_eagle3_patch_b200.synthetic import tree_attention_inputs
@@ -86,6 +92,7 @@ def test_strided_hf_layouts():
     kc[:, : past + n] = torch.from_numpy(k).to(torch.bfloat16).cuda()
     vc[:, : past + n] = torch.from_numpy(v).to(torch.bfloat16).cuda()
     kc[:, past + n:] = 50.0    # rows past the tree must not be read
+    vc[:, past + n:] = float("nan")
     bits = torch.from_numpy(O.pack_visibility(vis).view(np.int32)).cuda()
     out = K.tree_attention(q_hf, kc, vc, past, bits, scale)
     ref = O.tree_attention_ref(q_hf.float().cpu().numpy(), kc[:, : past + n].float().cpu().numpy(),
