@@ -368,47 +368,43 @@ attn_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ 
 // most two key tiles of 128 keys and up to two M tiles of its KV head.
 //
 // The rows of a KV head are cut into 128-row M tiles, taken two at a time
-// (tiles A and B, one softmax warpgroup each), plus a tail of <= 16 rows
-// that runs transposed on its own warpgroup: S_t^T = K Q_t^T (M = 128 keys,
-// N = 16) and O_t^T = V^T P_t^T (M = 128 dims, N = 16), its column max
-// and sum reduced with warp-wide redux instructions.  Every load is issued
-// when the CTA starts; the MMA warp then issues the products in the order
-// their operands become ready, and every barrier completes exactly once, so
-// each wait is on parity 0.
+// (tiles A and B, one softmax warpgroup each), plus a tail of <= 4 rows (one
+// token of a group of <= 4 heads) that its own warpgroup computes on CUDA
+// cores in fp32 from the K/V tiles already in shared memory.  Every load is
+// issued when the CTA starts; the MMA warp then issues the products in the
+// order their operands become ready, and every barrier completes exactly
+// once, so each wait is on parity 0.
 //
 //   warps 0-3    softmax + epilogue of M tile A (TMEM lane = row)
 //   warps 4-7    softmax + epilogue of M tile B
-//   warps 8-11   tail softmax + epilogue (TMEM lane = key, then dim)
+//   warps 8-11   the tail rows
 //   warp 12      TMEM owner; runs the load and MMA schedule in step, one
 //                elected lane issuing each TMA copy and tcgen05.mma
 //                (warps 13-15 only complete the warpgroup so registers can
 //                move to the softmax warpgroups)
 //
-// Shared memory: Q_A, Q_B, K_0, K_1, V_0, V_1 (32 KB each), Q_t (4 KB),
-// P_t[2] (4 KB each).  P of a main tile goes to shared memory (the P.V
-// product reads it as an SS operand) into a slot whose last reader has
-// completed: P(A,0) -> K_0, P(B,0) -> Q_A, P(A,1) -> Q_B, P(B,1) -> K_1.
-// Since P does not stay in TMEM, an S buffer is free as soon as its softmax
-// has loaded it.
-// TMEM columns: S(A,0) then O_A at 0, S(B,0) then O_B at 128, S(A,1) at
-// 256, S(B,1) at 256 once S(A,1) has been loaded (at 384 without a tail),
-// tail S_t(j) at 384 + 16j and O_t(j) at 416 + 16j.  The two key tiles of a
-// main row merge online (lazy rescaling of O); the tail merges at the end.
+// Shared memory: Q_A, Q_B, K_0, K_1, V_0, V_1 (32 KB each) and the tail's Q
+// tile, fp32 Q and P.  P of a main tile goes to shared memory (the P.V
+// product reads it as an SS operand) into a slot whose last reader is done:
+// P(A,0) -> Q_A, P(B,0) -> Q_B, P(A,1) -> K_0, P(B,1) -> K_1 (K slots wait
+// for the tail as well).  Since P does not stay in TMEM, an S buffer is free
+// as soon as its softmax has loaded it.
+// TMEM columns: S(A,0) then O_A at 0, S(B,0) then O_B at 128, S(A,1) at 256,
+// S(B,1) at 384.  The two key tiles of a main row merge online (lazy
+// rescaling of O); the tail's tiles merge at the end.
 // ---------------------------------------------------------------------------
 namespace split {
 
 constexpr int kThreads = 512;
 constexpr uint32_t kSlot = 2 * kHalf;                 // 32 KB
 constexpr uint32_t kQA = 0, kQB = kSlot, kK0 = 2 * kSlot, kK1 = 3 * kSlot, kV0 = 4 * kSlot, kV1 = 5 * kSlot;
-constexpr uint32_t kQT = 6 * kSlot;                   // 16 rows x 128 dims: two 2 KB halves
-constexpr uint32_t kPT = kQT + 4096;                  // P_t(j): 16 rows x 128 keys, 4 KB each
-constexpr uint32_t kRed = kPT + 8192;                 // tail reductions and per-tile statistics
+constexpr uint32_t kQT = 6 * kSlot;                   // tail Q tile, 16 rows x 128 dims: two 2 KB halves
+constexpr uint32_t kPT = kQT + 4096;                  // tail Q in fp32 [128 dims][4 rows], then P(j) [128 keys][4 rows]
+constexpr uint32_t kRed = kPT + 8192;                 // tail reductions, per-tile statistics, P.V exchange
 constexpr uint32_t kBar = kRed + 4096;
 constexpr uint32_t kSmemBytes = kBar + 512 + 1024;
 constexpr uint32_t kTHalf = 16 * 128;
 constexpr uint32_t kColA = 0, kColB = 128, kCol1 = 256, kColT = 384;
-constexpr uint32_t kIdescQKt = idesc_bf16_f32(128, 16, false, false);
-constexpr uint32_t kIdescPVt = idesc_bf16_f32(128, 16, true, false);
 constexpr uint32_t kIdescPVs = idesc_bf16_f32(BM, HD, false, true);   // P K-major from shared memory
 constexpr float kFix = 16777216.f;                    // 2^24: fixed-point scale of tail probabilities
 
@@ -431,25 +427,24 @@ enum : int {
     bK0 = 1,       // + j
     bV0 = 3,       // + j
     bS0 = 5,       // + 2 * slot + j      (S ready)
-    bSt0 = 9,      // + j                 (tail S ready)
-    bFreeQA = 11,  // last MMA reading Q_A completed
-    bFreeK0 = 12,
-    bFreeQB = 13,
-    bFreeK1 = 14,
-    bX1 = 15,      // S(A,1) loaded: column block 256 may take S(B,1)
-    bP0 = 16,      // + 2 * slot + j      (P in shared memory)
-    bPt0 = 20,     // + j
-    bPV0 = 22,     // + 2 * slot + j      (P.V complete)
-    bPVt = 26,     // every tail P.V complete
-    bDrain = 27,
-    kNumBars = 28
+    bFreeQA = 9,   // every reader of Q_A done (MMA commit)
+    bFreeK0 = 10,  // every reader of K_0 done (MMA commit, plus the tail's 128 threads)
+    bFreeQB = 11,
+    bFreeK1 = 12,
+    bP0 = 13,      // + 2 * slot + j      (P in shared memory)
+    bPV0 = 17,     // + 2 * slot + j      (P.V complete)
+    bDrain = 21,
+    kNumBars = 22
 };
 
+// P(slot, j) goes to the slot freed earliest for it: tile 0's P to the
+// M tile's own Q slot (free once both its S products completed), tile 1's
+// P to a K slot (free once both M tiles' S products and the tail read it).
 __device__ __forceinline__ uint32_t p_slot(int slot, int j) {
-    return slot == 0 ? (j == 0 ? kK0 : kQB) : (j == 0 ? kQA : kK1);
+    return j == 0 ? (slot ? kQB : kQA) : (slot ? kK1 : kK0);
 }
 __device__ __forceinline__ int free_bar(int slot, int j) {
-    return slot == 0 ? (j == 0 ? bFreeK0 : bFreeQB) : (j == 0 ? bFreeQA : bFreeK1);
+    return j == 0 ? (slot ? bFreeQB : bFreeQA) : (slot ? bFreeK1 : bFreeK0);
 }
 __device__ __forceinline__ float warp_max(float v) {
     float m;
@@ -604,12 +599,12 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
     const int mA = 2 * grp, mB = 2 * grp + 1;
     const bool hasA = mA < p.n_mt, hasB = mB < p.n_mt;
     const bool hasT = grp == p.n_groups - 1 && p.tail_rows > 0;
-    const bool shareX1 = hasT && hasB && nj == 2;   // S(B,1) waits for S(A,1) to leave column block 256
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kNumBars; ++i) {
-            const bool by_wg = (i >= bP0 && i < bP0 + 4) || i == bPt0 || i == bPt0 + 1 || i == bX1;
-            mbar_init(&bars[i], by_wg ? 128 : 1);
+            uint32_t count = (i >= bP0 && i < bP0 + 4) ? 128 : 1;
+            if ((i == bFreeK0 || (i == bFreeK1 && nj > 1)) && hasT) count += 128;   // the tail reads K too
+            mbar_init(&bars[i], count);
         }
         fence_mbar_init();
     }
@@ -682,23 +677,12 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
                     mma_commit(&bars[bS0 + 2 * sl + j]);
                 }
             };
-            auto s_tail = [&](int j) {
-                if (leader) {
-                    mma8<1024, 2, 128, 2>(tmem + kColT + 16 * j, desc(j ? kK1 : kK0, 16), desc(kQT, 16), kIdescQKt, 0u);
-                    mma_commit(&bars[bSt0 + j]);
-                }
-            };
             auto pv_main = [&](int sl, int j) {
                 if (leader) {
                     mma8<1024, 2, 512, 128>(tmem + (sl ? kColB : kColA), desc(p_slot(sl, j), 16), desc(j ? kV1 : kV0, kHalf),
                                             kIdescPVs, j > 0 ? 1u : 0u);
                     mma_commit(&bars[bPV0 + 2 * sl + j]);
                 }
-            };
-            auto pv_tail = [&](int j) {
-                if (leader)
-                    mma8<512, 128, 128, 2>(tmem + kColT + 32 + 16 * j, desc(j ? kV1 : kV0, kHalf), desc(kPT + j * 4096, 16),
-                                           kIdescPVt, 0u);
             };
             auto commit = [&](int b) {
                 if (leader) mma_commit(&bars[b]);
@@ -712,7 +696,6 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
             if (ok) {
                 if (hasA) s_main(0, 0, kColA);
                 if (hasB) s_main(1, 0, kColB);
-                if (hasT) s_tail(0);
                 commit(bFreeK0);
                 if (nj == 1) {
                     commit(bFreeQA);
@@ -724,12 +707,9 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
                 if (ok) {
                     if (hasA) s_main(0, 1, kCol1);
                     commit(bFreeQA);
-                    if (hasT) s_tail(1);
-                    if (!shareX1) {
-                        if (hasB) s_main(1, 1, hasT ? kCol1 : kColT);
-                        commit(bFreeQB);
-                        commit(bFreeK1);
-                    }
+                    if (hasB) s_main(1, 1, kColT);
+                    commit(bFreeQB);
+                    commit(bFreeK1);
                 }
             }
             if (ok) ok = wait(bV0);
@@ -737,21 +717,9 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
                 ok = wait(bP0 + 0);
                 if (ok) pv_main(0, 0);
             }
-            if (ok && shareX1) {
-                ok = wait(bX1);
-                if (ok) {
-                    s_main(1, 1, kCol1);
-                    commit(bFreeQB);
-                    commit(bFreeK1);
-                }
-            }
             if (ok && hasB) {
                 ok = wait(bP0 + 2);
                 if (ok) pv_main(1, 0);
-            }
-            if (ok && hasT) {
-                ok = wait(bPt0);
-                if (ok) pv_tail(0);
             }
             if (ok && nj > 1) {
                 ok = wait(bV0 + 1);
@@ -763,12 +731,7 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
                     ok = wait(bP0 + 3);
                     if (ok) pv_main(1, 1);
                 }
-                if (ok && hasT) {
-                    ok = wait(bPt0 + 1);
-                    if (ok) pv_tail(1);
-                }
             }
-            if (ok && hasT) commit(bPVt);
             __syncwarp();
             if (!ok && leader) flag_error(p.status, 2);
             // drain: nothing this warp issued may still be in flight when the CTA exits
@@ -802,7 +765,7 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
             const float sl2 = p.scale_log2;
             for (int j = 0; j < nj; ++j) {
                 const uint32_t s_col =
-                    tmem + lane_addr + (j == 0 ? (slot ? kColB : kColA) : (slot == 0 || hasT ? kCol1 : kColT));
+                    tmem + lane_addr + (j == 0 ? (slot ? kColB : kColA) : (slot == 0 ? kCol1 : kColT));
                 ok = ok && mbar_wait(&bars[bS0 + 2 * slot + j], 0);
                 tc_fence_after();
                 const int u0 = (kt0 + j) * BN - p.past;
@@ -816,10 +779,6 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
                     for (int q = 0; q < 4; ++q)
                         vb[q] = masked ? vis_bits(vrow, p.vis_words, u0 + q * 32, p.n_tokens, valid) : 0xffffffffu;
                     tmem_wait_ld();
-                }
-                if (slot == 0 && j == 1 && shareX1) {
-                    tc_fence_before();
-                    mbar_arrive(&bars[bX1]);
                 }
                 if (!ok) break;
                 float mk[8];
@@ -907,76 +866,162 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
         }
     } else {
         asm volatile("setmaxnreg.dec.sync.aligned.u32 72;\n" ::: "memory");
-        // ---------------------------------------------------------------- tail (transposed), warps 8-11
+        // ---------------------------------------------------------------- tail on CUDA cores, warps 8-11
+        // The <= 4 tail rows (one token of a group of <= 4 heads) against this
+        // CTA's key tiles, straight from the K/V tiles in shared memory, in
+        // fp32.  Scores: thread k owns key k of the tile.  P.V: thread t owns
+        // dims 2(t % 64) and 2(t % 64) + 1 over keys 64(t / 64) .. +63; the two
+        // key halves add through shared memory.  Column max and sum reduce
+        // with warp-wide redux instructions; the tiles merge at the end.
         const int tw = warp - 8;
-        const int k = tw * 32 + lane;               // key lane (S_t^T), then dim lane (O_t^T)
-        const uint32_t lane_addr = (uint32_t)(tw * 32) << 16;
+        const int k = tw * 32 + lane;
         if (hasT) {
             const int nt = p.tail_rows;
             const float sl2 = p.scale_log2;
-            bool ok = true;
-            for (int j = 0; j < nj; ++j) {
-                ok = ok && mbar_wait(&bars[bSt0 + j], 0);
-                tc_fence_after();
-                uint32_t r[16];
-                if (ok) {
-                    tmem_ld16(tmem + lane_addr + kColT + 16 * j, r);
-                    tmem_wait_ld();
-                }
-                const int u = (kt0 + j) * BN + k - p.past;
-                float s[16];
+            float* qf = reinterpret_cast<float*>(smem + kPT);     // [128 dims][4 rows]
+            float* xo = reinterpret_cast<float*>(smem + kRed + 1536);   // [64 dim pairs][4 rows][2]
+            bool ok = mbar_wait(&bars[bQ], 0);
+            for (int i = k; i < 128 * 4; i += 128) {
+                const int d = i >> 2, r = i & 3, dd = d & 63;
+                const __nv_bfloat16 v = *reinterpret_cast<const __nv_bfloat16*>(
+                    smem + kQT + (d >> 6) * kTHalf + r * 128 + (((dd >> 3) ^ (r & 7)) << 4) + (dd & 7) * 2);
+                qf[i] = (ok && r < nt) ? __bfloat162float(v) : 0.f;
+            }
+            named_bar_sync(1, 128);
+            const int dp = k & 63, kh = k >> 6;
+            float ot0[4][2], ot1[4][2];   // P.V of key tile 0 / 1 for this thread's dims (t < 64)
 #pragma unroll
-                for (int c = 0; c < 16; ++c) {
+            for (int r = 0; r < 4; ++r) ot0[r][0] = ot0[r][1] = ot1[r][0] = ot1[r][1] = 0.f;
+            // scores of every key tile first (both tiles in one pass, sharing the
+            // q loads), so both K slots are released as early as possible
+            float sc0[4] = {0.f, 0.f, 0.f, 0.f}, sc1[4] = {0.f, 0.f, 0.f, 0.f};
+            ok = ok && mbar_wait(&bars[bK0], 0) && (nj < 2 || mbar_wait(&bars[bK0 + 1], 0));
+            if (ok) {
+                const unsigned char* krow0 = smem + kK0 + (k >> 3) * 1024 + (k & 7) * 128;
+                const unsigned char* krow1 = smem + kK1 + (k >> 3) * 1024 + (k & 7) * 128;
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+#pragma unroll 2
+                    for (int c = 0; c < 8; ++c) {
+                        const int off = h * kHalf + ((c ^ (k & 7)) << 4);
+                        const uint4 ka = *reinterpret_cast<const uint4*>(krow0 + off);
+                        const uint4 kb = nj > 1 ? *reinterpret_cast<const uint4*>(krow1 + off) : make_uint4(0, 0, 0, 0);
+                        const uint32_t wa[4] = {ka.x, ka.y, ka.z, ka.w};
+                        const uint32_t wb[4] = {kb.x, kb.y, kb.z, kb.w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const int d = h * 64 + c * 8 + 2 * e;
+                            const float4 q0 = *reinterpret_cast<const float4*>(qf + d * 4);
+                            const float4 q1 = *reinterpret_cast<const float4*>(qf + d * 4 + 4);
+                            const float a0 = __uint_as_float(wa[e] << 16), a1 = __uint_as_float(wa[e] & 0xffff0000u);
+                            const float b0 = __uint_as_float(wb[e] << 16), b1 = __uint_as_float(wb[e] & 0xffff0000u);
+                            sc0[0] = fmaf(a1, q1.x, fmaf(a0, q0.x, sc0[0]));
+                            sc0[1] = fmaf(a1, q1.y, fmaf(a0, q0.y, sc0[1]));
+                            sc0[2] = fmaf(a1, q1.z, fmaf(a0, q0.z, sc0[2]));
+                            sc0[3] = fmaf(a1, q1.w, fmaf(a0, q0.w, sc0[3]));
+                            sc1[0] = fmaf(b1, q1.x, fmaf(b0, q0.x, sc1[0]));
+                            sc1[1] = fmaf(b1, q1.y, fmaf(b0, q0.y, sc1[1]));
+                            sc1[2] = fmaf(b1, q1.z, fmaf(b0, q0.z, sc1[2]));
+                            sc1[3] = fmaf(b1, q1.w, fmaf(b0, q0.w, sc1[3]));
+                        }
+                    }
+                }
+            }
+            mbar_arrive(&bars[bFreeK0]);   // the tail is done with the K slots
+            if (nj > 1) mbar_arrive(&bars[bFreeK1]);
+            for (int j = 0; j < nj; ++j) {
+                float sc[4];
+#pragma unroll
+                for (int r = 0; r < 4; ++r) sc[r] = j ? sc1[r] : sc0[r];
+                const int u = (kt0 + j) * BN + k - p.past;
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
                     bool vis = false;
-                    if (c < nt) {
-                        const int token = p.tail_token0 + c / p.group;
+                    if (r < nt && ok) {
+                        const int token = p.tail_token0 + r / p.group;
                         if (u < 0)
                             vis = true;
                         else if (u < p.n_tokens)
                             vis = (__ldg(p.vis + (int64_t)token * p.vis_words + (u >> 5)) >> (u & 31)) & 1u;
                     }
-                    s[c] = (vis && ok) ? __uint_as_float(r[c]) * sl2 : -INFINITY;
+                    sc[r] = vis ? sc[r] * sl2 : -INFINITY;
                 }
-                // column max: one redux per warp, then one exchange across the 4 warps
+                // column max: one redux per warp, one exchange across the 4 warps
                 float* wm = wmax + j * 64;
 #pragma unroll
-                for (int c = 0; c < 16; ++c) {
-                    if (c < nt) {
-                        const float v = warp_max(s[c]);
-                        if (lane == 0) wm[tw * 16 + c] = v;
+                for (int r = 0; r < 4; ++r) {
+                    if (r < nt) {
+                        const float v = warp_max(sc[r]);
+                        if (lane == 0) wm[tw * 16 + r] = v;
                     }
                 }
                 named_bar_sync(1, 128);
                 float* ws = wsum + j * 64;
+                float pr[4];
 #pragma unroll
-                for (int c = 0; c < 16; ++c) {
-                    if (c < nt) {
-                        const float mt = fmaxf(fmaxf(wm[c], wm[16 + c]), fmaxf(wm[32 + c], wm[48 + c]));
-                        const float pc = ex2_approx(s[c] - (mt == -INFINITY ? 0.f : mt));   // s = -inf gives 0
-                        s[c] = pc;
+                for (int r = 0; r < 4; ++r) {
+                    pr[r] = 0.f;
+                    if (r < nt) {
+                        const float mt = fmaxf(fmaxf(wm[r], wm[16 + r]), fmaxf(wm[32 + r], wm[48 + r]));
+                        pr[r] = ex2_approx(sc[r] - (mt == -INFINITY ? 0.f : mt));   // -inf gives 0
                         // column sum in 2^-24 fixed point: every p <= 1, so a warp's sum fits 32 bits
-                        const uint32_t sum = warp_sum_u32(__float2uint_rn(pc * kFix));
-                        if (lane == 0) ws[tw * 16 + c] = (float)sum * (1.f / kFix);
-                        if (k == 0) tmax[j * 16 + c] = mt;
-                    } else {
-                        s[c] = 0.f;
+                        const uint32_t sum = warp_sum_u32(__float2uint_rn(pr[r] * kFix));
+                        if (lane == 0) ws[tw * 16 + r] = (float)sum * (1.f / kFix);
+                        if (k == 0) tmax[j * 16 + r] = mt;
                     }
                 }
-                // P_t(j) as the [16 rows x 128 keys] K-major, 128-byte-swizzled B operand
-                unsigned char* ptb = smem + kPT + j * 4096 + (k >> 6) * kTHalf;
-                const int kk = k & 63;
+                float* pf = reinterpret_cast<float*>(smem + kPT + 2048 + j * 2048);   // [128 keys][4 rows]
+                *reinterpret_cast<float4*>(pf + k * 4) = make_float4(pr[0], pr[1], pr[2], pr[3]);
+                named_bar_sync(1, 128);
+                ok = ok && mbar_wait(&bars[bV0 + j], 0);
+                float o[4][2];
 #pragma unroll
-                for (int c = 0; c < 16; ++c) {
-                    const uint32_t off = c * 128 + ((((kk >> 3) ^ (c & 7)) & 7) << 4) + (kk & 7) * 2;
-                    *reinterpret_cast<__nv_bfloat16*>(ptb + off) = __float2bfloat16_rn(s[c]);
+                for (int r = 0; r < 4; ++r) o[r][0] = o[r][1] = 0.f;
+                if (ok) {
+                    const int d = 2 * dp, dd = d & 63;
+                    const unsigned char* vcol = smem + (j ? kV1 : kV0) + (d >> 6) * kHalf + (dd & 7) * 2;
+#pragma unroll 4
+                    for (int kk = 0; kk < 64; ++kk) {
+                        const int kr = kh * 64 + kk;
+                        const uint32_t vv = *reinterpret_cast<const uint32_t*>(
+                            vcol + (kr >> 3) * 1024 + (kr & 7) * 128 + (((dd >> 3) ^ (kr & 7)) << 4));
+                        const float v0 = __uint_as_float(vv << 16), v1 = __uint_as_float(vv & 0xffff0000u);
+                        const float4 pq = *reinterpret_cast<const float4*>(pf + kr * 4);
+                        o[0][0] = fmaf(pq.x, v0, o[0][0]);
+                        o[0][1] = fmaf(pq.x, v1, o[0][1]);
+                        o[1][0] = fmaf(pq.y, v0, o[1][0]);
+                        o[1][1] = fmaf(pq.y, v1, o[1][1]);
+                        o[2][0] = fmaf(pq.z, v0, o[2][0]);
+                        o[2][1] = fmaf(pq.z, v1, o[2][1]);
+                        o[3][0] = fmaf(pq.w, v0, o[3][0]);
+                        o[3][1] = fmaf(pq.w, v1, o[3][1]);
+                    }
                 }
-                fence_proxy_async_smem();
-                mbar_arrive(&bars[bPt0 + j]);
+                if (kh == 1) {
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) {
+                        xo[dp * 8 + r * 2] = o[r][0];
+                        xo[dp * 8 + r * 2 + 1] = o[r][1];
+                    }
+                }
+                named_bar_sync(1, 128);
+                if (kh == 0) {
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) {
+                        const float x0 = o[r][0] + xo[dp * 8 + r * 2], x1 = o[r][1] + xo[dp * 8 + r * 2 + 1];
+                        if (j == 0) {
+                            ot0[r][0] = x0;
+                            ot0[r][1] = x1;
+                        } else {
+                            ot1[r][0] = x0;
+                            ot1[r][1] = x1;
+                        }
+                    }
+                }
             }
-            if (ok) ok = mbar_wait(&bars[bPVt], 0);
-            named_bar_sync(1, 128);   // every tile's statistics are visible
-            // thread c < nt merges column c's per-tile statistics into the
-            // weights of O_t(j) and the column's log-sum-exp
+            // thread r < nt merges row r's per-tile statistics into the weights of
+            // each tile's P.V and the row's log-sum-exp
+            named_bar_sync(1, 128);
             if (k < nt) {
                 const float m0 = tmax[k], m1 = nj > 1 ? tmax[16 + k] : -INFINITY;
                 const float l0 = wsum[k] + wsum[16 + k] + wsum[32 + k] + wsum[48 + k];
@@ -992,36 +1037,28 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
             }
             named_bar_sync(1, 128);
             if (!ok) {
-                flag_error(p.status, 4);
-            } else {
-                tc_fence_after();
-                float acc[16];
-#pragma unroll
-                for (int c = 0; c < 16; ++c) acc[c] = 0.f;
-                for (int j = 0; j < nj; ++j) {
-                    uint32_t o[16];
-                    tmem_ld16(tmem + lane_addr + kColT + 32 + 16 * j, o);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int c = 0; c < 16; ++c) acc[c] = fmaf(wts[16 * j + c], __uint_as_float(o[c]), acc[c]);
-                }
-                const int d = k;
+                if (k == 0) flag_error(p.status, 4);
+            } else if (kh == 0) {
                 const int rows_head = p.group * p.n_tokens;
 #pragma unroll
-                for (int c = 0; c < 16; ++c) {
-                    if (c < nt) {
-                        const int token = p.tail_token0 + c / p.group;
-                        const int head = g * p.group + c % p.group;
+                for (int r = 0; r < 4; ++r) {
+                    if (r < nt) {
+                        const int token = p.tail_token0 + r / p.group;
+                        const int head = g * p.group + r % p.group;
                         if (token < p.n_tokens) {
+                            const float w0 = wts[r], w1 = nj > 1 ? wts[16 + r] : 0.f;
+                            const __nv_bfloat162 h = __floats2bfloat162_rn(w0 * ot0[r][0] + w1 * ot1[r][0],
+                                                                           w0 * ot0[r][1] + w1 * ot1[r][1]);
+                            __nv_bfloat16* dst;
                             if (p.splits == 1) {
-                                p.out[(int64_t)token * p.o_stride_tok + (int64_t)head * p.o_stride_head + d] =
-                                    __float2bfloat16_rn(acc[c]);
+                                dst = p.out + (int64_t)token * p.o_stride_tok + (int64_t)head * p.o_stride_head;
                             } else {
                                 const int64_t prow =
-                                    ((int64_t)split * p.hkv + g) * rows_head + p.tail_token0 * p.group + c;
-                                p.part_o[prow * HD + d] = __float2bfloat16_rn(acc[c]);
-                                if (d == 0) p.part_lse[prow] = wts[32 + c];
+                                    ((int64_t)split * p.hkv + g) * rows_head + p.tail_token0 * p.group + r;
+                                dst = p.part_o + prow * HD;
+                                if (dp == 0) p.part_lse[prow] = wts[32 + r];
                             }
+                            *reinterpret_cast<__nv_bfloat162*>(dst + 2 * dp) = h;
                         }
                     }
                 }
@@ -1131,7 +1168,7 @@ static SplitPlan plan_split(int64_t n_tokens, int64_t hq, int64_t hkv, int64_t p
     pl.tpt = BM / pl.group;
     const int64_t rows = (int64_t)pl.group * n_tokens;
     int64_t n_mt = rows / BM, rem = rows % BM, tail = 0;
-    if (rem > 16 || (rem > 0 && 16 % pl.group != 0))
+    if (rem > 4 || (rem > 0 && 16 % pl.group != 0))
         n_mt += 1;
     else
         tail = rem;

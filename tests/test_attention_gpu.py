@@ -70,6 +70,8 @@ def test_matches_hf_sdpa_fixtures(golden_attention):
     (1000, 9, 32, 2),       # group 16: one M tile + 16-row tail
     (20000, 65, 32, 8),     # long context: several waves of key splits
     (64, 600, 32, 8),       # many M tiles: unsplit kernel
+    (100, 131, 8, 8),       # no GQA: 3-row tail (three tokens)
+    (200, 65, 16, 8),       # group 2: 2-row tail
 ])
 def test_random_trees_vs_float64(past, n, hq, hkv):
     from ddtree_eagle3_patch_b200.synthetic import tree_attention_inputs
