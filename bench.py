@@ -252,7 +252,7 @@ def run_ours(args, rank, world, local):
     alg_bytes = kv_bytes + qo_bytes
     peaks = _peaks()
     achieved = alg_bytes / (attn_us * 1e-6) / 1e9
-    roofline = {"bound": "hbm", "kernel": "tree_attn_kernel + attn_combine_kernel (one layer)",
+    roofline = {"bound": "hbm", "kernel": "tree_attn_split_kernel + combine_kernel (one layer)",
                 "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "peak_source": peaks["source"],
                 "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
                 "traffic": _profiled_traffic(), "algorithmic_bytes": alg_bytes, "us_per_launch": round(attn_us, 3)}
@@ -368,7 +368,7 @@ def _peaks():
 
 def _profiled_traffic():
     """DRAM bytes per attention launch from the committed ncu summary, or None."""
-    f = ROOT / "profiles" / "tree_attn_kernel_qwen3_4b_verify.md"
+    f = ROOT / "profiles" / "tree_attn_split_kernel_qwen3_4b_verify.md"
     if not f.exists():
         return None
     for line in f.read_text().splitlines():

@@ -1,0 +1,87 @@
+"""Data-parallel plumbing on two CPU processes (gloo): prompt sharding,
+gather / all_gather conventions and counter merging, as the reference's
+harness uses them (benchmark.py:175, 237-241; distributed.py:55-72)."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+WORLD = 2
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank: int, world: int, port: int, n_prompts: int, out):
+    os.environ.update({"RANK": str(rank), "WORLD_SIZE": str(world), "LOCAL_RANK": str(rank),
+                       "LOCAL_WORLD_SIZE": str(world), "MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port)})
+    from datetime import timedelta
+    from ddtree_eagle3_patch_b200 import distributed as dist
+    dist.init(backend="gloo", timeout=timedelta(seconds=60))
+    try:
+        mine = list(dist.shard_indices(n_prompts))
+        # per-prompt "results": accepted lengths derived from the prompt index
+        responses = [{"idx": i, "accepted": (i % 5) + 1} for i in mine]
+        counters = {"prompts": len(mine), "accepted": sum(r["accepted"] for r in responses), "steps": len(mine) * 3}
+        gathered = dist.gather(responses, dst=0)
+        everyone = dist.all_gather(counters)
+        dist.barrier()
+        out.put((rank, mine, gathered, everyone, dist.is_main()))
+    finally:
+        torch.distributed.destroy_process_group()
+
+
+@pytest.mark.parametrize("n_prompts", [0, 1, 7, 80])
+def test_sharding_gather_and_counters(n_prompts):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, WORLD, port, n_prompts, q)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    results = {}
+    for _ in range(WORLD):
+        rank, mine, gathered, everyone, main = q.get(timeout=120)
+        results[rank] = (mine, gathered, everyone, main)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    # every prompt is decoded by exactly one rank, rank r taking r, r + W, ...
+    shards = [results[r][0] for r in range(WORLD)]
+    assert sorted(i for s in shards for i in s) == list(range(n_prompts))
+    for r in range(WORLD):
+        assert shards[r] == list(range(r, n_prompts, WORLD))
+    # gather: rank-ordered lists on rank 0, None elsewhere
+    assert results[0][3] and not results[1][3]
+    assert results[1][1] is None
+    gathered = results[0][1]
+    assert [[x["idx"] for x in part] for part in gathered] == shards
+    # all_gather: the same rank-ordered counters everywhere, merged to totals
+    from ddtree_eagle3_patch_b200.distributed import merge_counters
+    assert results[0][2] == results[1][2]
+    total = merge_counters(results[0][2])
+    assert total["prompts"] == n_prompts
+    assert total["accepted"] == sum((i % 5) + 1 for i in range(n_prompts))
+    assert total["steps"] == 3 * n_prompts
+
+
+def test_single_process_fallbacks(monkeypatch):
+    """Without RANK the reference warns and runs alone: gather returns [obj]."""
+    from ddtree_eagle3_patch_b200 import distributed as dist
+    monkeypatch.delenv("RANK", raising=False)
+    monkeypatch.delenv("WORLD_SIZE", raising=False)
+    with pytest.warns(UserWarning):
+        dist.init(backend="gloo")
+    assert not dist.is_initialized()
+    assert dist.size() == 1 and dist.rank() == 0 and dist.is_main()
+    assert dist.gather({"a": 1}) == [{"a": 1}]
+    assert dist.all_gather(3) == [3]
+    dist.barrier()
+    assert list(dist.shard_indices(5)) == [0, 1, 2, 3, 4]
+    with pytest.raises(ValueError):
+        dist.shard_indices(5, rank_=2, size_=2)
