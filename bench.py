@@ -283,7 +283,12 @@ def run_ours(args, rank, world, local):
 
 def run_e2e(args, w: Workload, device, stream, tree_out, table, world, dist):
     """Per step: pinned host draft logits, per-layer queries and new tree K/V
-    rows, and verify logits are copied in; the accept result is copied out."""
+    rows, and verify logits are copied in; the accept result is copied out.
+    The copies run on a copy stream in the order the step needs them, and
+    the compute stream waits on a per-layer event just before each use, so
+    the host-to-device traffic overlaps the kernels (a step still contains
+    all of its own copies: the next step starts after this one's result is
+    back on the host)."""
     from ddtree_eagle3_patch_b200 import kernels
     h_draft = [t.cpu().pin_memory() for t in w.draft]
     h_verify = [t.cpu().pin_memory() for t in w.verify]
@@ -299,18 +304,37 @@ def run_e2e(args, w: Workload, device, stream, tree_out, table, world, dist):
                 torch.empty(N_VERIFY, dtype=torch.int64, device=device))
     h2d = (h_draft[0].numel() * 4 + h_verify[0].numel() * 2 + h_q.numel() * 2 + h_kt.numel() * 2 + h_vt.numel() * 2)
     d2h = h_result.numel() * 8
+    from cuda.bindings import runtime as cudart
+    h2d_kind = cudart.cudaMemcpyKind.cudaMemcpyHostToDevice
+    row_bytes = N_VERIFY * HD * 2
+    copy_stream = torch.cuda.Stream(device)
+    ev_draft, ev_verify = torch.cuda.Event(), torch.cuda.Event()
+    ev_layer = [torch.cuda.Event() for _ in range(LAYERS)]
 
     def step(i):
-        with torch.cuda.stream(stream):
+        with torch.cuda.stream(copy_stream):
             d_draft.copy_(h_draft[i % 2], non_blocking=True)
-            tree = kernels.tree_build(d_draft, BUDGET, out=tree_out)
-            d_q.copy_(h_q, non_blocking=True)
+            ev_draft.record(copy_stream)
             for layer in range(LAYERS):
-                w.ks[layer][:, PAST:].copy_(h_kt[layer], non_blocking=True)
-                w.vs[layer][:, PAST:].copy_(h_vt[layer], non_blocking=True)
+                d_q[layer].copy_(h_q[layer], non_blocking=True)
+                # the new tree rows of every head in one 2D copy per tensor
+                for src, dst in ((h_kt[layer], w.ks[layer]), (h_vt[layer], w.vs[layer])):
+                    err, = cudart.cudaMemcpy2DAsync(dst[:, PAST:].data_ptr(), dst.stride(0) * 2, src.data_ptr(),
+                                                    row_bytes, row_bytes, dst.shape[0], h2d_kind,
+                                                    copy_stream.cuda_stream)
+                    if err != cudart.cudaError_t.cudaSuccess:
+                        raise RuntimeError(f"cudaMemcpy2DAsync: {err}")
+                ev_layer[layer].record(copy_stream)
+            d_verify.copy_(h_verify[i % 2], non_blocking=True)
+            ev_verify.record(copy_stream)
+        with torch.cuda.stream(stream):
+            stream.wait_event(ev_draft)
+            tree = kernels.tree_build(d_draft, BUDGET, out=tree_out)
+            for layer in range(LAYERS):
+                stream.wait_event(ev_layer[layer])
                 kernels.tree_attention(d_q[layer], w.ks[layer], w.vs[layer], PAST, tree.visibility, w.scale,
                                        out=w.outs[layer])
-            d_verify.copy_(h_verify[i % 2], non_blocking=True)
+            stream.wait_event(ev_verify)
             acc, info, _ = kernels.tree_accept(d_verify, tree.parents, tree.node_token_ids, tree.info,
                                                max_accept=ROWS + 1, accepted=acc_bufs[0], accept_info=acc_bufs[1],
                                                posterior=acc_bufs[2])
@@ -338,7 +362,7 @@ def run_e2e(args, w: Workload, device, stream, tree_out, table, world, dist):
     el = float(ms.item())
     return {"value": round(world * args.steps / (el / 1e3), 2), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
             "d2h_bytes_per_step": int(d2h), "ms_per_step": round(el / args.steps, 4),
-            "api": "ddtree_eagle3_patch_b200.kernels (C-ABI via ctypes), eager launches"}
+            "api": "ddtree_eagle3_patch_b200.kernels (C-ABI via ctypes), eager launches, copies on a copy stream"}
 
 
 def _attention_splits() -> int:

@@ -617,6 +617,9 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     const uint32_t s_addr = smem_u32(smem);
+    // every CTA of this grid is resident: the next kernel in the stream may be
+    // scheduled as SMs free up (it waits for this grid before reading our output)
+    griddep_launch_dependents();
 
     // 512 threads x 128 registers at launch: warpgroup 3 gives 88 per thread,
     // warpgroup 2 gives 56, the two softmax warpgroups take 72 each.  Each
@@ -630,40 +633,56 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
             // each TMA copy, MMA and commit.
             const bool leader = elect_one_sync();
             // ------------------------------------------------------------ loads
-            if (leader) {
-            prefetch_tmap(&tq);
-            prefetch_tmap(&tk);
-            prefetch_tmap(&tv);
+            // K/V tiles that hold only prefix keys were written before this
+            // step, so they load before the preceding kernel in the stream has
+            // finished; Q and the tile holding the tree's own keys load after.
             const uint64_t kv_policy = policy_evict_first();
-            const uint32_t qbytes = (hasA ? kSlot : 0) + (hasB ? kSlot : 0) + (hasT ? 2 * kTHalf : 0);
-            mbar_arrive_expect_tx(&bars[bQ], qbytes);
-            if (hasA) {
-                tma_load_3d(smem + kQA, &tq, 0, g * p.group, mA * p.tpt, &bars[bQ]);
-                tma_load_3d(smem + kQA + kHalf, &tq, 64, g * p.group, mA * p.tpt, &bars[bQ]);
-            }
-            if (hasB) {
-                tma_load_3d(smem + kQB, &tq, 0, g * p.group, mB * p.tpt, &bars[bQ]);
-                tma_load_3d(smem + kQB + kHalf, &tq, 64, g * p.group, mB * p.tpt, &bars[bQ]);
-            }
-            if (hasT) {
-                prefetch_tmap(&tqt);
-                tma_load_3d(smem + kQT, &tqt, 0, g * p.group, p.tail_token0, &bars[bQ]);
-                tma_load_3d(smem + kQT + kTHalf, &tqt, 64, g * p.group, p.tail_token0, &bars[bQ]);
-            }
-            for (int j = 0; j < nj; ++j) {
+            auto load_k = [&](int j) {
                 const int key0 = (kt0 + j) * BN;
                 unsigned char* kb = smem + (j ? kK1 : kK0);
                 mbar_arrive_expect_tx(&bars[bK0 + j], kSlot);
                 tma_load_3d_hint(kb, &tk, 0, key0, g, &bars[bK0 + j], kv_policy);
                 tma_load_3d_hint(kb + kHalf, &tk, 64, key0, g, &bars[bK0 + j], kv_policy);
-            }
-            for (int j = 0; j < nj; ++j) {
+            };
+            auto load_v = [&](int j) {
                 const int key0 = (kt0 + j) * BN;
                 unsigned char* vb = smem + (j ? kV1 : kV0);
                 mbar_arrive_expect_tx(&bars[bV0 + j], kSlot);
                 tma_load_3d_hint(vb, &tv, 0, key0, g, &bars[bV0 + j], kv_policy);
                 tma_load_3d_hint(vb + kHalf, &tv, 64, key0, g, &bars[bV0 + j], kv_policy);
+            };
+            auto prefix_only = [&](int j) { return (kt0 + j + 1) * BN <= p.past; };
+            if (leader) {
+                prefetch_tmap(&tk);
+                prefetch_tmap(&tv);
+                for (int j = 0; j < nj; ++j)
+                    if (prefix_only(j)) load_k(j);
+                for (int j = 0; j < nj; ++j)
+                    if (prefix_only(j)) load_v(j);
             }
+            __syncwarp();
+            griddep_wait();
+            if (leader) {
+                prefetch_tmap(&tq);
+                const uint32_t qbytes = (hasA ? kSlot : 0) + (hasB ? kSlot : 0) + (hasT ? 2 * kTHalf : 0);
+                mbar_arrive_expect_tx(&bars[bQ], qbytes);
+                if (hasA) {
+                    tma_load_3d(smem + kQA, &tq, 0, g * p.group, mA * p.tpt, &bars[bQ]);
+                    tma_load_3d(smem + kQA + kHalf, &tq, 64, g * p.group, mA * p.tpt, &bars[bQ]);
+                }
+                if (hasB) {
+                    tma_load_3d(smem + kQB, &tq, 0, g * p.group, mB * p.tpt, &bars[bQ]);
+                    tma_load_3d(smem + kQB + kHalf, &tq, 64, g * p.group, mB * p.tpt, &bars[bQ]);
+                }
+                if (hasT) {
+                    prefetch_tmap(&tqt);
+                    tma_load_3d(smem + kQT, &tqt, 0, g * p.group, p.tail_token0, &bars[bQ]);
+                    tma_load_3d(smem + kQT + kTHalf, &tqt, 64, g * p.group, p.tail_token0, &bars[bQ]);
+                }
+                for (int j = 0; j < nj; ++j)
+                    if (!prefix_only(j)) load_k(j);
+                for (int j = 0; j < nj; ++j)
+                    if (!prefix_only(j)) load_v(j);
             }
             __syncwarp();
             // ------------------------------------------------------------ MMA issue
@@ -746,6 +765,7 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
         }
     } else if (warp < 8) {
         asm volatile("setmaxnreg.inc.sync.aligned.u32 200;\n" ::: "memory");
+        griddep_wait();   // nothing global is read or written before the preceding kernel is done
         // ---------------------------------------------------------------- softmax of M tile A / B
         const int slot = warp >> 2;
         const bool has = slot == 0 ? hasA : hasB;
@@ -866,6 +886,7 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
         }
     } else {
         asm volatile("setmaxnreg.dec.sync.aligned.u32 72;\n" ::: "memory");
+        griddep_wait();
         // ---------------------------------------------------------------- tail on CUDA cores, warps 8-11
         // The <= 4 tail rows (one token of a group of <= 4 heads) against this
         // CTA's key tiles, straight from the K/V tiles in shared memory, in
@@ -1077,6 +1098,8 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
 __global__ void __launch_bounds__(128)
 combine_kernel(const __nv_bfloat16* __restrict__ part_o, const float* __restrict__ part_lse, int splits, int hkv,
                int group, int n_tokens, __nv_bfloat16* out, int64_t o_stride_tok, int64_t o_stride_head) {
+    griddep_launch_dependents();
+    griddep_wait();   // the partials come from the split kernel just before
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int rows_head = group * n_tokens;
     const int64_t row = (int64_t)blockIdx.x * 4 + warp;
@@ -1260,14 +1283,32 @@ static int launch_split(const ddt_attention_args* a, const SplitPlan& sp, void* 
     }
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     dim3 grid((unsigned)sp.splits, (unsigned)sp.n_groups, (unsigned)a->hkv);
-    split::tree_attn_split_kernel<<<grid, split::kThreads, split::kSmemBytes, st>>>(tq, tqt, tk, tv, q);
+    // Both kernels are launched as programmatic dependents of whatever precedes
+    // them in the stream: their prologues (and the prefix K/V loads) overlap
+    // the previous kernel's tail; each waits for it before touching its data.
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(split::kThreads);
+    cfg.dynamicSmemBytes = split::kSmemBytes;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t le = cudaLaunchKernelEx(&cfg, split::tree_attn_split_kernel, tq, tqt, tk, tv, q);
+    if (le != cudaSuccess) return set_error(DDT_ECUDA, "tree_attn_split_kernel: %s", cudaGetErrorString(le));
     rc = check_launch("tree_attn_split_kernel");
     if (rc) return rc;
     if (sp.splits > 1) {
         const int64_t rows = a->n_tokens * a->hq;
-        split::combine_kernel<<<(unsigned)ceil_div(rows, 4), 128, 0, st>>>(q.part_o, q.part_lse, sp.splits,
-                                                                          (int)a->hkv, sp.group, (int)a->n_tokens,
-                                                                          q.out, a->o_stride_tok, a->o_stride_head);
+        cfg.gridDim = dim3((unsigned)ceil_div(rows, 4));
+        cfg.blockDim = dim3(128);
+        cfg.dynamicSmemBytes = 0;
+        le = cudaLaunchKernelEx(&cfg, split::combine_kernel, (const __nv_bfloat16*)q.part_o, (const float*)q.part_lse,
+                                sp.splits, (int)a->hkv, sp.group, (int)a->n_tokens, q.out, a->o_stride_tok,
+                                a->o_stride_head);
+        if (le != cudaSuccess) return set_error(DDT_ECUDA, "split_combine_kernel: %s", cudaGetErrorString(le));
         rc = check_launch("split_combine_kernel");
     }
     return rc;
