@@ -304,6 +304,291 @@ __device__ bool slot_tuple_less(const ExpandSmem& e, int a, int b) {
     return na < nb;
 }
 
+// Frontier in shared memory, any budget: one warp, lane-strided scan of the
+// slots each step.
+__device__ int expand_smem(const ExpandSmem& e, int rows, int topk, int budget, int lane) {
+    int fsize = 1;
+    if (lane == 0) {
+        e.f_logw[0] = (double)e.lp[0];
+        e.f_parent[0] = 0;
+        e.f_dr[0] = (1 << 16) | 0;
+        e.n_parent[0] = -1;
+        e.n_dr[0] = 0;
+    }
+    __syncwarp();
+    int count = 0;
+    while (count < budget && fsize > 0) {
+        // lane-local minimum of (-logw, ranks tuple)
+        unsigned long long best_u = ~0ull;
+        int best_s = -1;
+        for (int s = lane; s < fsize; s += 32) {
+            const unsigned long long u = ord_f64(-e.f_logw[s]);
+            if (u < best_u || (u == best_u && best_s >= 0 && slot_tuple_less(e, s, best_s))) {
+                best_u = u;
+                best_s = s;
+            }
+        }
+        const uint32_t hi = __reduce_min_sync(DDT_FULL_MASK, (uint32_t)(best_u >> 32));
+        const uint32_t lo =
+            __reduce_min_sync(DDT_FULL_MASK, ((uint32_t)(best_u >> 32) == hi) ? (uint32_t)best_u : 0xffffffffu);
+        const unsigned long long umin = ((unsigned long long)hi << 32) | lo;
+        const uint32_t tied = __ballot_sync(DDT_FULL_MASK, best_s >= 0 && best_u == umin);
+        int w;
+        if (__popc(tied) == 1) {
+            w = __shfl_sync(DDT_FULL_MASK, best_s, __ffs(tied) - 1);
+        } else {
+            // exact float64 tie across lanes: decide by the ranks tuples
+            int pick = -1;
+            if (lane == 0) {
+                for (int s = 0; s < fsize; ++s) {
+                    if (ord_f64(-e.f_logw[s]) != umin) continue;
+                    if (pick < 0 || slot_tuple_less(e, s, pick)) pick = s;
+                }
+            }
+            w = __shfl_sync(DDT_FULL_MASK, pick, 0);
+        }
+        if (lane == 0) {
+            const double logw = e.f_logw[w];
+            const int parent = e.f_parent[w];
+            const int dr = e.f_dr[w];
+            const int depth = dr >> 16, rank = dr & 0xffff;
+            const int cur = count + 1;
+            e.n_parent[cur] = parent;
+            e.n_dr[cur] = dr;
+            const bool sib = rank + 1 < topk;
+            const bool child = depth < rows;
+            int nf = fsize;
+            if (sib) {
+                const double a = (double)e.lp[(depth - 1) * topk + rank];
+                const double b = (double)e.lp[(depth - 1) * topk + rank + 1];
+                const double s = __dadd_rn(__dadd_rn(logw, -a), b);
+                e.f_logw[w] = s;
+                e.f_parent[w] = parent;
+                e.f_dr[w] = (depth << 16) | (rank + 1);
+            }
+            if (child) {
+                const double c = __dadd_rn(logw, (double)e.lp[depth * topk]);
+                const int slot = sib ? nf++ : w;
+                e.f_logw[slot] = c;
+                e.f_parent[slot] = cur;
+                e.f_dr[slot] = (depth + 1) << 16;
+            }
+            if (!sib && !child) {
+                nf -= 1;
+                if (w != nf) {
+                    e.f_logw[w] = e.f_logw[nf];
+                    e.f_parent[w] = e.f_parent[nf];
+                    e.f_dr[w] = e.f_dr[nf];
+                }
+            }
+            e.scalars[0] = nf;
+        }
+        __syncwarp();
+        fsize = *(volatile int32_t*)&e.scalars[0];
+        count += 1;
+    }
+    return count;
+}
+
+// Ranks tuple of a frontier entry packed as parent << 17 | depth << 11 | rank.
+__device__ int packed_path(const ExpandSmem& e, uint32_t pk, int* out) {
+    const int depth = (pk >> 11) & 63;
+    out[depth - 1] = pk & 2047;
+    int node = (int)(pk >> 17);
+    for (int k = depth - 2; k >= 0; --k) {
+        out[k] = e.n_dr[node] & 0xffff;
+        node = e.n_parent[node];
+    }
+    return depth;
+}
+__device__ bool packed_tuple_less(const ExpandSmem& e, uint32_t a, uint32_t b) {
+    int pa[kMaxRows], pb[kMaxRows];
+    const int na = packed_path(e, a, pa), nb = packed_path(e, b, pb);
+    const int n = na < nb ? na : nb;
+    for (int k = 0; k < n; ++k)
+        if (pa[k] != pb[k]) return pa[k] < pb[k];
+    return na < nb;
+}
+
+// Frontier in registers for budgets below 32 * S: slot i lives in lane i % 32,
+// register i / 32, as (path score, parent << 17 | depth << 11 | rank).  A step
+// is a register min per lane, a warp min of the 64-bit order key, and a
+// broadcast of the winner; every lane computes the sibling and child scores
+// (same fp64 operations and order as the reference, ddtree.py:171, 176) and
+// the owning lanes update their registers.  Exact fp64 ties between slots go
+// through shared memory and are decided by the ranks tuples.
+template <int S>
+__device__ int expand_regs(const ExpandSmem& e, int rows, int topk, int budget, int lane) {
+    double lw[S];
+    uint32_t pk[S];
+    unsigned long long key[S];   // ord_f64(-lw): smaller key = higher score; ~0 marks an empty slot
+#pragma unroll
+    for (int s = 0; s < S; ++s) {
+        lw[s] = 0.0;
+        pk[s] = 0u;
+        key[s] = ~0ull;
+    }
+    if (lane == 0) {
+        lw[0] = (double)e.lp[0];
+        pk[0] = (0u << 17) | (1u << 11) | 0u;
+        key[0] = ord_f64(-lw[0]);
+        e.n_parent[0] = -1;
+        e.n_dr[0] = 0;
+    }
+    int* tie_buf = reinterpret_cast<int*>(e.f_logw);   // tie candidates: (slot, packed) pairs
+    int fsize = 1, count = 0;
+    while (count < budget && fsize > 0) {
+        // lane minimum, then the warp minimum of the high word; the low word
+        // is only reduced when high words tie
+        unsigned long long best = key[0];
+        int bs = 0;
+#pragma unroll
+        for (int s = 1; s < S; ++s)
+            if (key[s] < best) {
+                best = key[s];
+                bs = s;
+            }
+        const uint32_t bhi = (uint32_t)(best >> 32);
+        const uint32_t hi = __reduce_min_sync(DDT_FULL_MASK, bhi);
+        uint32_t cand = __ballot_sync(DDT_FULL_MASK, bhi == hi);
+        unsigned long long umin = best;
+        if (__popc(cand) != 1) {
+            const uint32_t lo = __reduce_min_sync(DDT_FULL_MASK, bhi == hi ? (uint32_t)best : 0xffffffffu);
+            umin = ((unsigned long long)hi << 32) | lo;
+            cand = __ballot_sync(DDT_FULL_MASK, best == umin);
+        } else {
+            umin = __shfl_sync(DDT_FULL_MASK, best, __ffs(cand) - 1);
+        }
+        // a slot tie inside a lane also needs the tuple rule
+        int mine = 0;
+#pragma unroll
+        for (int s = 0; s < S; ++s) mine += key[s] == umin ? 1 : 0;
+        const bool unique = __popc(cand) == 1 && __ballot_sync(DDT_FULL_MASK, mine > 1) == 0;
+        int wl, ws;
+        if (unique) {
+            wl = __ffs(cand) - 1;
+            ws = __shfl_sync(DDT_FULL_MASK, bs, wl);
+        } else {
+            int pre = mine;   // inclusive prefix of the per-lane tie counts
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(DDT_FULL_MASK, pre, o);
+                if (lane >= o) pre += v;
+            }
+            const int total = __shfl_sync(DDT_FULL_MASK, pre, 31);
+            int k = pre - mine;
+#pragma unroll
+            for (int s = 0; s < S; ++s) {
+                if (key[s] == umin) {
+                    tie_buf[2 * k] = s * 32 + lane;
+                    tie_buf[2 * k + 1] = (int)pk[s];
+                    ++k;
+                }
+            }
+            __syncwarp();
+            if (lane == 0) {
+                int pick = 0;
+                for (int c = 1; c < total; ++c)
+                    if (packed_tuple_less(e, (uint32_t)tie_buf[2 * c + 1], (uint32_t)tie_buf[2 * pick + 1])) pick = c;
+                e.scalars[3] = tie_buf[2 * pick];
+            }
+            __syncwarp();
+            const int widx = *(volatile int32_t*)&e.scalars[3];
+            __syncwarp();
+            wl = widx & 31;
+            ws = widx >> 5;
+        }
+        double wlw = 0.0;
+        uint32_t wpk = 0u;
+#pragma unroll
+        for (int s = 0; s < S; ++s)
+            if (s == ws) {
+                wlw = lw[s];
+                wpk = pk[s];
+            }
+        wlw = __shfl_sync(DDT_FULL_MASK, wlw, wl);
+        wpk = __shfl_sync(DDT_FULL_MASK, wpk, wl);
+        const uint32_t parent = wpk >> 17;
+        const int depth = (int)((wpk >> 11) & 63), rank = (int)(wpk & 2047);
+        const int cur = count + 1;
+        if (lane == 0) {
+            e.n_parent[cur] = (int)parent;
+            e.n_dr[cur] = (depth << 16) | rank;
+        }
+        const bool sib = rank + 1 < topk;
+        const bool child = depth < rows;
+        double sv = 0.0, cv = 0.0;
+        if (sib) {
+            const double a = (double)e.lp[(depth - 1) * topk + rank];
+            const double b = (double)e.lp[(depth - 1) * topk + rank + 1];
+            sv = __dadd_rn(__dadd_rn(wlw, -a), b);
+        }
+        if (child) cv = __dadd_rn(wlw, (double)e.lp[depth * topk]);
+        const uint32_t spk = (parent << 17) | ((uint32_t)depth << 11) | (uint32_t)(rank + 1);
+        const uint32_t cpk = ((uint32_t)cur << 17) | ((uint32_t)(depth + 1) << 11);
+        double nv = sv;
+        uint32_t npk = spk;
+        unsigned long long nkey;
+        if (sib) {
+            nkey = ord_f64(-sv);
+        } else if (child) {
+            nv = cv;
+            npk = cpk;
+            nkey = ord_f64(-cv);
+        } else {
+            // remove the winner: the last slot moves into its place
+            const int li = fsize - 1, ll = li & 31, ls = li >> 5;
+            double lv = 0.0;
+            uint32_t lpk = 0u;
+            unsigned long long lk = ~0ull;
+#pragma unroll
+            for (int s = 0; s < S; ++s)
+                if (s == ls) {
+                    lv = lw[s];
+                    lpk = pk[s];
+                    lk = key[s];
+                }
+            nv = __shfl_sync(DDT_FULL_MASK, lv, ll);
+            npk = __shfl_sync(DDT_FULL_MASK, lpk, ll);
+            nkey = __shfl_sync(DDT_FULL_MASK, lk, ll);
+        }
+        if (lane == wl) {
+#pragma unroll
+            for (int s = 0; s < S; ++s)
+                if (s == ws) {
+                    lw[s] = nv;
+                    pk[s] = npk;
+                    key[s] = nkey;
+                }
+        }
+        if (!sib && !child) {   // the last slot empties (after the move, which it may be the source of)
+            const int li = fsize - 1;
+            if (lane == (li & 31)) {
+#pragma unroll
+                for (int s = 0; s < S; ++s)
+                    if (s == (li >> 5)) key[s] = ~0ull;
+            }
+        }
+        if (sib && child) {
+            const int al = fsize & 31, as = fsize >> 5;
+            const unsigned long long ckey = ord_f64(-cv);
+            if (lane == al) {
+#pragma unroll
+                for (int s = 0; s < S; ++s)
+                    if (s == as) {
+                        lw[s] = cv;
+                        pk[s] = cpk;
+                        key[s] = ckey;
+                    }
+            }
+            fsize += 1;
+        } else if (!sib && !child) {
+            fsize -= 1;
+        }
+        ++count;
+    }
+    return count;
+}
+
 // Runs on all threads of one CTA.  lp / ids: [rows, topk] in global memory.
 __device__ void expand_tree(const float* lp_g, const int64_t* ids_g, int rows, int topk, int budget,
                             const int64_t* root_token, int64_t start, const ddt_tree_outputs out, ExpandSmem e) {
@@ -312,86 +597,17 @@ __device__ void expand_tree(const float* lp_g, const int64_t* ids_g, int rows, i
     __syncthreads();
 
     if (warp == 0) {
-        int fsize = 1;
-        if (lane == 0) {
-            e.f_logw[0] = (double)e.lp[0];
-            e.f_parent[0] = 0;
-            e.f_dr[0] = (1 << 16) | 0;
-            e.n_parent[0] = -1;
-            e.n_dr[0] = 0;
-        }
-        __syncwarp();
-        int count = 0;
-        while (count < budget && fsize > 0) {
-            // lane-local minimum of (-logw, ranks tuple)
-            unsigned long long best_u = ~0ull;
-            int best_s = -1;
-            for (int s = lane; s < fsize; s += 32) {
-                const unsigned long long u = ord_f64(-e.f_logw[s]);
-                if (u < best_u || (u == best_u && best_s >= 0 && slot_tuple_less(e, s, best_s))) {
-                    best_u = u;
-                    best_s = s;
-                }
-            }
-            const uint32_t hi = __reduce_min_sync(DDT_FULL_MASK, (uint32_t)(best_u >> 32));
-            const uint32_t lo =
-                __reduce_min_sync(DDT_FULL_MASK, ((uint32_t)(best_u >> 32) == hi) ? (uint32_t)best_u : 0xffffffffu);
-            const unsigned long long umin = ((unsigned long long)hi << 32) | lo;
-            const uint32_t tied = __ballot_sync(DDT_FULL_MASK, best_s >= 0 && best_u == umin);
-            int w;
-            if (__popc(tied) == 1) {
-                w = __shfl_sync(DDT_FULL_MASK, best_s, __ffs(tied) - 1);
-            } else {
-                // exact float64 tie across lanes: decide by the ranks tuples
-                int pick = -1;
-                if (lane == 0) {
-                    for (int s = 0; s < fsize; ++s) {
-                        if (ord_f64(-e.f_logw[s]) != umin) continue;
-                        if (pick < 0 || slot_tuple_less(e, s, pick)) pick = s;
-                    }
-                }
-                w = __shfl_sync(DDT_FULL_MASK, pick, 0);
-            }
-            if (lane == 0) {
-                const double logw = e.f_logw[w];
-                const int parent = e.f_parent[w];
-                const int dr = e.f_dr[w];
-                const int depth = dr >> 16, rank = dr & 0xffff;
-                const int cur = count + 1;
-                e.n_parent[cur] = parent;
-                e.n_dr[cur] = dr;
-                const bool sib = rank + 1 < topk;
-                const bool child = depth < rows;
-                int nf = fsize;
-                if (sib) {
-                    const double a = (double)e.lp[(depth - 1) * topk + rank];
-                    const double b = (double)e.lp[(depth - 1) * topk + rank + 1];
-                    const double s = __dadd_rn(__dadd_rn(logw, -a), b);
-                    e.f_logw[w] = s;
-                    e.f_parent[w] = parent;
-                    e.f_dr[w] = (depth << 16) | (rank + 1);
-                }
-                if (child) {
-                    const double c = __dadd_rn(logw, (double)e.lp[depth * topk]);
-                    const int slot = sib ? nf++ : w;
-                    e.f_logw[slot] = c;
-                    e.f_parent[slot] = cur;
-                    e.f_dr[slot] = (depth + 1) << 16;
-                }
-                if (!sib && !child) {
-                    nf -= 1;
-                    if (w != nf) {
-                        e.f_logw[w] = e.f_logw[nf];
-                        e.f_parent[w] = e.f_parent[nf];
-                        e.f_dr[w] = e.f_dr[nf];
-                    }
-                }
-                e.scalars[0] = nf;
-            }
-            __syncwarp();
-            fsize = *(volatile int32_t*)&e.scalars[0];
-            count += 1;
-        }
+        int count;
+        if (budget < 32)
+            count = expand_regs<1>(e, rows, topk, budget, lane);
+        else if (budget < 64)
+            count = expand_regs<2>(e, rows, topk, budget, lane);
+        else if (budget < 96)
+            count = expand_regs<3>(e, rows, topk, budget, lane);
+        else if (budget < 128)
+            count = expand_regs<4>(e, rows, topk, budget, lane);
+        else
+            count = expand_smem(e, rows, topk, budget, lane);
         if (lane == 0) e.scalars[1] = count;
     }
     __syncthreads();
