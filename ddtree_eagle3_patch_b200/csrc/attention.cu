@@ -399,13 +399,14 @@ constexpr int kThreads = 512;
 constexpr uint32_t kSlot = 2 * kHalf;                 // 32 KB
 constexpr uint32_t kQA = 0, kQB = kSlot, kK0 = 2 * kSlot, kK1 = 3 * kSlot, kV0 = 4 * kSlot, kV1 = 5 * kSlot;
 constexpr uint32_t kQT = 6 * kSlot;                   // tail Q tile, 16 rows x 128 dims: two 2 KB halves
-constexpr uint32_t kPT = kQT + 4096;                  // tail Q in fp32 [128 dims][4 rows], then P(j) [128 keys][4 rows]
-constexpr uint32_t kRed = kPT + 8192;                 // tail reductions, per-tile statistics, P.V exchange
+constexpr uint32_t kPT = kQT + 4096;                  // tail P(j): 16 rows x 128 keys bf16 (K-major, 128-byte swizzle), 4 KB each
+constexpr uint32_t kRed = kPT + 8192;                 // tail reductions and per-tile statistics, then tail Q in fp32
 constexpr uint32_t kBar = kRed + 4096;
 constexpr uint32_t kSmemBytes = kBar + 512 + 1024;
 constexpr uint32_t kTHalf = 16 * 128;
 constexpr uint32_t kColA = 0, kColB = 128, kCol1 = 256, kColT = 384;
 constexpr uint32_t kIdescPVs = idesc_bf16_f32(BM, HD, false, true);   // P K-major from shared memory
+constexpr uint32_t kIdescPVt = idesc_bf16_f32(128, 16, true, false);  // tail: O_t^T = V^T P_t^T (V^T MN-major)
 constexpr float kFix = 16777216.f;                    // 2^24: fixed-point scale of tail probabilities
 
 struct Params {
@@ -434,7 +435,10 @@ enum : int {
     bP0 = 13,      // + 2 * slot + j      (P in shared memory)
     bPV0 = 17,     // + 2 * slot + j      (P.V complete)
     bDrain = 21,
-    kNumBars = 22
+    bX1 = 22,      // S(A,1) loaded: its TMEM block may take the tail's P.V
+    bPt0 = 23,     // + j                 (tail P in shared memory)
+    bPVt = 25,     // the tail's P.V products complete
+    kNumBars = 26
 };
 
 // P(slot, j) goes to the slot freed earliest for it: tile 0's P to the
@@ -602,7 +606,7 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kNumBars; ++i) {
-            uint32_t count = (i >= bP0 && i < bP0 + 4) ? 128 : 1;
+            uint32_t count = ((i >= bP0 && i < bP0 + 4) || i == bX1 || i == bPt0 || i == bPt0 + 1) ? 128 : 1;
             if ((i == bFreeK0 || (i == bFreeK1 && nj > 1)) && hasT) count += 128;   // the tail reads K too
             mbar_init(&bars[i], count);
         }
@@ -740,6 +744,17 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
                 ok = wait(bP0 + 2);
                 if (ok) pv_main(1, 0);
             }
+            if (ok && hasT) {
+                // the tail's O_t^T = V^T P_t^T into S(A,1)'s TMEM block, once free
+                if (hasA && nj > 1) ok = wait(bX1);
+                for (int j = 0; j < nj && ok; ++j) {
+                    ok = wait(bV0 + j) && wait(bPt0 + j);
+                    if (ok && leader)
+                        mma8<512, 128, 128, 2>(tmem + kCol1 + 16 * j, desc(j ? kV1 : kV0, kHalf), desc(kPT + j * 4096, 16),
+                                               kIdescPVt, 0u);
+                }
+                if (ok) commit(bPVt);
+            }
             if (ok && nj > 1) {
                 ok = wait(bV0 + 1);
                 if (ok && hasA) {
@@ -799,6 +814,10 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
                     for (int q = 0; q < 4; ++q)
                         vb[q] = masked ? vis_bits(vrow, p.vis_words, u0 + q * 32, p.n_tokens, valid) : 0xffffffffu;
                     tmem_wait_ld();
+                }
+                if (slot == 0 && j == 1 && hasT) {   // S(A,1)'s TMEM block may now take the tail's P.V
+                    tc_fence_before();
+                    mbar_arrive(&bars[bX1]);
                 }
                 if (!ok) break;
                 float mk[8];
@@ -899,8 +918,7 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
         if (hasT) {
             const int nt = p.tail_rows;
             const float sl2 = p.scale_log2;
-            float* qf = reinterpret_cast<float*>(smem + kPT);     // [128 dims][4 rows]
-            float* xo = reinterpret_cast<float*>(smem + kRed + 1536);   // [64 dim pairs][4 rows][2]
+            float* qf = reinterpret_cast<float*>(smem + kRed + 2048);   // [128 dims][4 rows]
             bool ok = mbar_wait(&bars[bQ], 0);
             for (int i = k; i < 128 * 4; i += 128) {
                 const int d = i >> 2, r = i & 3, dd = d & 63;
@@ -908,11 +926,12 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
                     smem + kQT + (d >> 6) * kTHalf + r * 128 + (((dd >> 3) ^ (r & 7)) << 4) + (dd & 7) * 2);
                 qf[i] = (ok && r < nt) ? __bfloat162float(v) : 0.f;
             }
+            // rows 4..15 of both P_t tiles are zero (the product runs on 16 rows)
+            for (int i = k; i < 2 * 4096 / 16; i += 128) {
+                const int row = (i >> 3) & 15;
+                if (row >= 4) reinterpret_cast<uint4*>(smem + kPT)[i] = make_uint4(0u, 0u, 0u, 0u);
+            }
             named_bar_sync(1, 128);
-            const int dp = k & 63, kh = k >> 6;
-            float ot0[4][2], ot1[4][2];   // P.V of key tile 0 / 1 for this thread's dims (t < 64)
-#pragma unroll
-            for (int r = 0; r < 4; ++r) ot0[r][0] = ot0[r][1] = ot1[r][0] = ot1[r][1] = 0.f;
             // scores of every key tile first (both tiles in one pass, sharing the
             // q loads), so both K slots are released as early as possible
             float sc0[4] = {0.f, 0.f, 0.f, 0.f}, sc1[4] = {0.f, 0.f, 0.f, 0.f};
@@ -991,54 +1010,16 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
                         if (k == 0) tmax[j * 16 + r] = mt;
                     }
                 }
-                float* pf = reinterpret_cast<float*>(smem + kPT + 2048 + j * 2048);   // [128 keys][4 rows]
-                *reinterpret_cast<float4*>(pf + k * 4) = make_float4(pr[0], pr[1], pr[2], pr[3]);
-                named_bar_sync(1, 128);
-                ok = ok && mbar_wait(&bars[bV0 + j], 0);
-                float o[4][2];
+                // P_t(j) as the [16 rows x 128 keys] K-major, 128-byte-swizzled B
+                // operand of the transposed P.V product (rows >= 4 stay zero)
+                unsigned char* ptb = smem + kPT + j * 4096 + (k >> 6) * kTHalf;
+                const int kk = k & 63;
 #pragma unroll
-                for (int r = 0; r < 4; ++r) o[r][0] = o[r][1] = 0.f;
-                if (ok) {
-                    const int d = 2 * dp, dd = d & 63;
-                    const unsigned char* vcol = smem + (j ? kV1 : kV0) + (d >> 6) * kHalf + (dd & 7) * 2;
-#pragma unroll 4
-                    for (int kk = 0; kk < 64; ++kk) {
-                        const int kr = kh * 64 + kk;
-                        const uint32_t vv = *reinterpret_cast<const uint32_t*>(
-                            vcol + (kr >> 3) * 1024 + (kr & 7) * 128 + (((dd >> 3) ^ (kr & 7)) << 4));
-                        const float v0 = __uint_as_float(vv << 16), v1 = __uint_as_float(vv & 0xffff0000u);
-                        const float4 pq = *reinterpret_cast<const float4*>(pf + kr * 4);
-                        o[0][0] = fmaf(pq.x, v0, o[0][0]);
-                        o[0][1] = fmaf(pq.x, v1, o[0][1]);
-                        o[1][0] = fmaf(pq.y, v0, o[1][0]);
-                        o[1][1] = fmaf(pq.y, v1, o[1][1]);
-                        o[2][0] = fmaf(pq.z, v0, o[2][0]);
-                        o[2][1] = fmaf(pq.z, v1, o[2][1]);
-                        o[3][0] = fmaf(pq.w, v0, o[3][0]);
-                        o[3][1] = fmaf(pq.w, v1, o[3][1]);
-                    }
-                }
-                if (kh == 1) {
-#pragma unroll
-                    for (int r = 0; r < 4; ++r) {
-                        xo[dp * 8 + r * 2] = o[r][0];
-                        xo[dp * 8 + r * 2 + 1] = o[r][1];
-                    }
-                }
-                named_bar_sync(1, 128);
-                if (kh == 0) {
-#pragma unroll
-                    for (int r = 0; r < 4; ++r) {
-                        const float x0 = o[r][0] + xo[dp * 8 + r * 2], x1 = o[r][1] + xo[dp * 8 + r * 2 + 1];
-                        if (j == 0) {
-                            ot0[r][0] = x0;
-                            ot0[r][1] = x1;
-                        } else {
-                            ot1[r][0] = x0;
-                            ot1[r][1] = x1;
-                        }
-                    }
-                }
+                for (int r = 0; r < 4; ++r)
+                    *reinterpret_cast<__nv_bfloat16*>(ptb + r * 128 + ((((kk >> 3) ^ r) & 7) << 4) + (kk & 7) * 2) =
+                        __float2bfloat16_rn(pr[r]);
+                fence_proxy_async_smem();
+                mbar_arrive(&bars[bPt0 + j]);
             }
             // thread r < nt merges row r's per-tile statistics into the weights of
             // each tile's P.V and the row's log-sum-exp
@@ -1057,10 +1038,29 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
                 wts[32 + k] = L > 0.f ? mm + log2f(L) : -INFINITY;
             }
             named_bar_sync(1, 128);
+            // O_t^T(j) in TMEM: lane = dim k, column = tail row
+            ok = ok && mbar_wait(&bars[bPVt], 0);
+            tc_fence_after();
+            float o0[16], o1[16];
+            {
+                const uint32_t lane_addr = (uint32_t)(tw * 32) << 16;
+                uint32_t r0[16], r1[16];
+                if (ok) {
+                    tmem_ld16(tmem + lane_addr + kCol1, r0);
+                    if (nj > 1) tmem_ld16(tmem + lane_addr + kCol1 + 16, r1);
+                    tmem_wait_ld();
+                }
+#pragma unroll
+                for (int c = 0; c < 16; ++c) {
+                    o0[c] = ok ? __uint_as_float(r0[c]) : 0.f;
+                    o1[c] = (ok && nj > 1) ? __uint_as_float(r1[c]) : 0.f;
+                }
+            }
             if (!ok) {
                 if (k == 0) flag_error(p.status, 4);
-            } else if (kh == 0) {
+            } else {
                 const int rows_head = p.group * p.n_tokens;
+                const int d = k;
 #pragma unroll
                 for (int r = 0; r < 4; ++r) {
                     if (r < nt) {
@@ -1068,8 +1068,7 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
                         const int head = g * p.group + r % p.group;
                         if (token < p.n_tokens) {
                             const float w0 = wts[r], w1 = nj > 1 ? wts[16 + r] : 0.f;
-                            const __nv_bfloat162 h = __floats2bfloat162_rn(w0 * ot0[r][0] + w1 * ot1[r][0],
-                                                                           w0 * ot0[r][1] + w1 * ot1[r][1]);
+                            const __nv_bfloat16 h = __float2bfloat16_rn(w0 * o0[r] + w1 * o1[r]);
                             __nv_bfloat16* dst;
                             if (p.splits == 1) {
                                 dst = p.out + (int64_t)token * p.o_stride_tok + (int64_t)head * p.o_stride_head;
@@ -1077,9 +1076,9 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
                                 const int64_t prow =
                                     ((int64_t)split * p.hkv + g) * rows_head + p.tail_token0 * p.group + r;
                                 dst = p.part_o + prow * HD;
-                                if (dp == 0) p.part_lse[prow] = wts[32 + r];
+                                if (d == 0) p.part_lse[prow] = wts[32 + r];
                             }
-                            *reinterpret_cast<__nv_bfloat162*>(dst + 2 * dp) = h;
+                            dst[d] = h;
                         }
                     }
                 }
