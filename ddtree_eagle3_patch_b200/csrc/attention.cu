@@ -369,8 +369,10 @@ attn_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ 
 //
 // The rows of a KV head are cut into 128-row M tiles, taken two at a time
 // (tiles A and B, one softmax warpgroup each), plus a tail of <= 4 rows (one
-// token of a group of <= 4 heads) that its own warpgroup computes on CUDA
-// cores in fp32 from the K/V tiles already in shared memory.  Every load is
+// token of a group of <= 4 heads) with its own warpgroup.  The tail's two
+// products run transposed on the tensor core with N = 16 rows (S_t^T = K Q_t^T,
+// O_t^T = V^T P_t^T), so each of its threads owns one key, then one dim;
+// its softmax is column-wise on CUDA cores.  Every load is
 // issued when the CTA starts; the MMA warp then issues the products in the
 // order their operands become ready, and every barrier completes exactly
 // once, so each wait is on parity 0.
@@ -383,15 +385,17 @@ attn_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ 
 //                (warps 13-15 only complete the warpgroup so registers can
 //                move to the softmax warpgroups)
 //
-// Shared memory: Q_A, Q_B, K_0, K_1, V_0, V_1 (32 KB each) and the tail's Q
-// tile, fp32 Q and P.  P of a main tile goes to shared memory (the P.V
-// product reads it as an SS operand) into a slot whose last reader is done:
-// P(A,0) -> Q_A, P(B,0) -> Q_B, P(A,1) -> K_0, P(B,1) -> K_1 (K slots wait
-// for the tail as well).  Since P does not stay in TMEM, an S buffer is free
-// as soon as its softmax has loaded it.
+// Shared memory: Q_A, Q_B, K_0, K_1, V_0, V_1 (32 KB each), the tail's Q and
+// P tiles and its reductions.  P of a main tile goes to shared memory (the
+// P.V product reads it as an SS operand) into a slot whose last reader is
+// done: P(A,0) -> Q_A, P(B,0) -> Q_B, P(A,1) -> K_0, P(B,1) -> K_1.  Since P
+// does not stay in TMEM, an S buffer is free as soon as its softmax has
+// loaded it.
 // TMEM columns: S(A,0) then O_A at 0, S(B,0) then O_B at 128, S(A,1) at 256,
-// S(B,1) at 384.  The two key tiles of a main row merge online (lazy
-// rescaling of O); the tail's tiles merge at the end.
+// S(B,1) at 384.  S_t^T of the tail's key tiles takes columns 128 + 16 j
+// between B's load of S(B,0) and P.V(B,0), issued after the four main S
+// products; O_t^T takes 256 + 16 j once S(A,1) is loaded.  The two key tiles of a main row merge
+// online (lazy rescaling of O); the tail's tiles merge at the end.
 // ---------------------------------------------------------------------------
 namespace split {
 
@@ -400,12 +404,13 @@ constexpr uint32_t kSlot = 2 * kHalf;                 // 32 KB
 constexpr uint32_t kQA = 0, kQB = kSlot, kK0 = 2 * kSlot, kK1 = 3 * kSlot, kV0 = 4 * kSlot, kV1 = 5 * kSlot;
 constexpr uint32_t kQT = 6 * kSlot;                   // tail Q tile, 16 rows x 128 dims: two 2 KB halves
 constexpr uint32_t kPT = kQT + 4096;                  // tail P(j): 16 rows x 128 keys bf16 (K-major, 128-byte swizzle), 4 KB each
-constexpr uint32_t kRed = kPT + 8192;                 // tail reductions and per-tile statistics, then tail Q in fp32
+constexpr uint32_t kRed = kPT + 8192;                 // tail reductions and per-tile statistics
 constexpr uint32_t kBar = kRed + 4096;
 constexpr uint32_t kSmemBytes = kBar + 512 + 1024;
 constexpr uint32_t kTHalf = 16 * 128;
 constexpr uint32_t kColA = 0, kColB = 128, kCol1 = 256, kColT = 384;
 constexpr uint32_t kIdescPVs = idesc_bf16_f32(BM, HD, false, true);   // P K-major from shared memory
+constexpr uint32_t kIdescQKt = idesc_bf16_f32(128, 16, false, false); // tail: S_t^T = K Q_t^T
 constexpr uint32_t kIdescPVt = idesc_bf16_f32(128, 16, true, false);  // tail: O_t^T = V^T P_t^T (V^T MN-major)
 constexpr float kFix = 16777216.f;                    // 2^24: fixed-point scale of tail probabilities
 
@@ -429,7 +434,7 @@ enum : int {
     bV0 = 3,       // + j
     bS0 = 5,       // + 2 * slot + j      (S ready)
     bFreeQA = 9,   // every reader of Q_A done (MMA commit)
-    bFreeK0 = 10,  // every reader of K_0 done (MMA commit, plus the tail's 128 threads)
+    bFreeK0 = 10,  // every reader of K_0 done (MMA commit)
     bFreeQB = 11,
     bFreeK1 = 12,
     bP0 = 13,      // + 2 * slot + j      (P in shared memory)
@@ -438,12 +443,15 @@ enum : int {
     bX1 = 22,      // S(A,1) loaded: its TMEM block may take the tail's P.V
     bPt0 = 23,     // + j                 (tail P in shared memory)
     bPVt = 25,     // the tail's P.V products complete
-    kNumBars = 26
+    bSt = 26,      // the tail's S products complete
+    bStLd = 27,    // the tail has loaded S_t: P.V(B,0) may take its TMEM block
+    bX0B = 28,     // S(B,0) loaded: its TMEM block may take the tail's S products
+    kNumBars = 29
 };
 
 // P(slot, j) goes to the slot freed earliest for it: tile 0's P to the
 // M tile's own Q slot (free once both its S products completed), tile 1's
-// P to a K slot (free once both M tiles' S products and the tail read it).
+// P to a K slot (free once every S product reading it completed).
 __device__ __forceinline__ uint32_t p_slot(int slot, int j) {
     return j == 0 ? (slot ? kQB : kQA) : (slot ? kK1 : kK0);
 }
@@ -606,8 +614,8 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kNumBars; ++i) {
-            uint32_t count = ((i >= bP0 && i < bP0 + 4) || i == bX1 || i == bPt0 || i == bPt0 + 1) ? 128 : 1;
-            if ((i == bFreeK0 || (i == bFreeK1 && nj > 1)) && hasT) count += 128;   // the tail reads K too
+            const uint32_t count =
+                ((i >= bP0 && i < bP0 + 4) || i == bX1 || i == bX0B || i == bPt0 || i == bPt0 + 1 || i == bStLd) ? 128 : 1;
             mbar_init(&bars[i], count);
         }
         fence_mbar_init();
@@ -625,8 +633,9 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
     // scheduled as SMs free up (it waits for this grid before reading our output)
     griddep_launch_dependents();
 
-    // 512 threads x 128 registers at launch: warpgroup 3 gives 88 per thread,
-    // warpgroup 2 gives 56, the two softmax warpgroups take 72 each.  Each
+    // 512 threads x 128 registers at launch: warpgroups 2 and 3 give 88 per
+    // thread each, the two softmax warpgroups take 88 each (216: the softmax
+    // holds a whole 128-column row of S without spilling).  Each
     // role's setmaxnreg sits in its own branch so the compiler sizes that
     // role's code to the new limit; the code after the branches is trivial.
     if (warp >= 12) {
@@ -637,9 +646,13 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
             // each TMA copy, MMA and commit.
             const bool leader = elect_one_sync();
             // ------------------------------------------------------------ loads
-            // K/V tiles that hold only prefix keys were written before this
-            // step, so they load before the preceding kernel in the stream has
-            // finished; Q and the tile holding the tree's own keys load after.
+            // K tiles that hold only prefix keys were written before this step,
+            // so they load before the preceding kernel in the stream has
+            // finished; Q and a K tile holding the tree's own keys load after.
+            // V is not needed before the first softmax ends: its tiles load
+            // once Q and K_0 have landed and the first S products are queued,
+            // so the S products' operands are not queued behind V in the
+            // memory system.
             const uint64_t kv_policy = policy_evict_first();
             auto load_k = [&](int j) {
                 const int key0 = (kt0 + j) * BN;
@@ -661,8 +674,6 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
                 prefetch_tmap(&tv);
                 for (int j = 0; j < nj; ++j)
                     if (prefix_only(j)) load_k(j);
-                for (int j = 0; j < nj; ++j)
-                    if (prefix_only(j)) load_v(j);
             }
             __syncwarp();
             griddep_wait();
@@ -685,8 +696,6 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
                 }
                 for (int j = 0; j < nj; ++j)
                     if (!prefix_only(j)) load_k(j);
-                for (int j = 0; j < nj; ++j)
-                    if (!prefix_only(j)) load_v(j);
             }
             __syncwarp();
             // ------------------------------------------------------------ MMA issue
@@ -715,15 +724,21 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
                 tc_fence_after();
                 return __all_sync(DDT_FULL_MASK, r);
             };
+            // the tail's S_t^T(j) = K_j Q_t^T into S(B,0)'s TMEM block
+            auto s_tail = [&](int j) {
+                if (leader)
+                    mma8<1024, 2, 128, 2>(tmem + kColB + 16 * j, desc(j ? kK1 : kK0, 16), desc(kQT, 16), kIdescQKt, 0u);
+            };
             bool ok = wait(bQ) && wait(bK0);
             if (ok) {
                 if (hasA) s_main(0, 0, kColA);
                 if (hasB) s_main(1, 0, kColB);
-                commit(bFreeK0);
-                if (nj == 1) {
-                    commit(bFreeQA);
-                    commit(bFreeQB);
-                }
+            }
+            if (leader)   // issued even after a failed wait, so the drain below completes
+                for (int j = 0; j < nj; ++j) load_v(j);
+            if (ok && nj == 1) {
+                commit(bFreeQA);
+                commit(bFreeQB);
             }
             if (ok && nj > 1) {
                 ok = wait(bK0 + 1);
@@ -732,8 +747,21 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
                     commit(bFreeQA);
                     if (hasB) s_main(1, 1, kColT);
                     commit(bFreeQB);
-                    commit(bFreeK1);
                 }
+            }
+            // the tail's scores last: they are needed last, and every main S
+            // product they would delay gates a softmax
+            if (ok && hasT) {
+                if (hasB) ok = wait(bX0B);
+                if (ok) {
+                    s_tail(0);
+                    if (nj > 1) s_tail(1);
+                    commit(bSt);
+                }
+            }
+            if (ok) {
+                commit(bFreeK0);
+                if (nj > 1) commit(bFreeK1);
             }
             if (ok) ok = wait(bV0);
             if (ok && hasA) {
@@ -741,7 +769,7 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
                 if (ok) pv_main(0, 0);
             }
             if (ok && hasB) {
-                ok = wait(bP0 + 2);
+                ok = wait(bP0 + 2) && (!hasT || wait(bStLd));   // the tail has loaded S_t from O_B's columns
                 if (ok) pv_main(1, 0);
             }
             if (ok && hasT) {
@@ -779,7 +807,7 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
             mbar_wait(&bars[bQ], 0);
         }
     } else if (warp < 8) {
-        asm volatile("setmaxnreg.inc.sync.aligned.u32 200;\n" ::: "memory");
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 216;\n" ::: "memory");
         griddep_wait();   // nothing global is read or written before the preceding kernel is done
         // ---------------------------------------------------------------- softmax of M tile A / B
         const int slot = warp >> 2;
@@ -815,9 +843,13 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
                         vb[q] = masked ? vis_bits(vrow, p.vis_words, u0 + q * 32, p.n_tokens, valid) : 0xffffffffu;
                     tmem_wait_ld();
                 }
-                if (slot == 0 && j == 1 && hasT) {   // S(A,1)'s TMEM block may now take the tail's P.V
+                if (hasT && slot == 0 && j == 1) {   // S(A,1)'s TMEM block may now take the tail's P.V
                     tc_fence_before();
                     mbar_arrive(&bars[bX1]);
+                }
+                if (hasT && slot == 1 && j == 0) {   // S(B,0)'s TMEM block may now take the tail's S
+                    tc_fence_before();
+                    mbar_arrive(&bars[bX0B]);
                 }
                 if (!ok) break;
                 float mk[8];
@@ -904,71 +936,44 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
                 named_bar_sync(2 + slot, 128);
         }
     } else {
-        asm volatile("setmaxnreg.dec.sync.aligned.u32 72;\n" ::: "memory");
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 40;\n" ::: "memory");
         griddep_wait();
-        // ---------------------------------------------------------------- tail on CUDA cores, warps 8-11
+        // ---------------------------------------------------------------- tail rows, warps 8-11
         // The <= 4 tail rows (one token of a group of <= 4 heads) against this
-        // CTA's key tiles, straight from the K/V tiles in shared memory, in
-        // fp32.  Scores: thread k owns key k of the tile.  P.V: thread t owns
-        // dims 2(t % 64) and 2(t % 64) + 1 over keys 64(t / 64) .. +63; the two
-        // key halves add through shared memory.  Column max and sum reduce
-        // with warp-wide redux instructions; the tiles merge at the end.
+        // CTA's key tiles.  Both products are transposed tensor-core MMAs with
+        // 16 columns: thread k reads key k's scores of every tail row from
+        // S_t^T, runs the softmax column-wise (column max and sum by warp-wide
+        // redux and one exchange across the 4 warps), writes P_t as the B
+        // operand of O_t^T = V^T P_t^T, and finally reads dim k of every tail
+        // row from O_t^T; the key tiles merge there.
         const int tw = warp - 8;
         const int k = tw * 32 + lane;
         if (hasT) {
             const int nt = p.tail_rows;
             const float sl2 = p.scale_log2;
-            float* qf = reinterpret_cast<float*>(smem + kRed + 2048);   // [128 dims][4 rows]
-            bool ok = mbar_wait(&bars[bQ], 0);
-            for (int i = k; i < 128 * 4; i += 128) {
-                const int d = i >> 2, r = i & 3, dd = d & 63;
-                const __nv_bfloat16 v = *reinterpret_cast<const __nv_bfloat16*>(
-                    smem + kQT + (d >> 6) * kTHalf + r * 128 + (((dd >> 3) ^ (r & 7)) << 4) + (dd & 7) * 2);
-                qf[i] = (ok && r < nt) ? __bfloat162float(v) : 0.f;
-            }
             // rows 4..15 of both P_t tiles are zero (the product runs on 16 rows)
             for (int i = k; i < 2 * 4096 / 16; i += 128) {
                 const int row = (i >> 3) & 15;
                 if (row >= 4) reinterpret_cast<uint4*>(smem + kPT)[i] = make_uint4(0u, 0u, 0u, 0u);
             }
-            named_bar_sync(1, 128);
-            // scores of every key tile first (both tiles in one pass, sharing the
-            // q loads), so both K slots are released as early as possible
+            // S_t^T(j) in TMEM: lane = key k, column 16 j + r = tail row r
             float sc0[4] = {0.f, 0.f, 0.f, 0.f}, sc1[4] = {0.f, 0.f, 0.f, 0.f};
-            ok = ok && mbar_wait(&bars[bK0], 0) && (nj < 2 || mbar_wait(&bars[bK0 + 1], 0));
+            bool ok = __all_sync(DDT_FULL_MASK, mbar_wait(&bars[bSt], 0));
+            tc_fence_after();
             if (ok) {
-                const unsigned char* krow0 = smem + kK0 + (k >> 3) * 1024 + (k & 7) * 128;
-                const unsigned char* krow1 = smem + kK1 + (k >> 3) * 1024 + (k & 7) * 128;
+                const uint32_t lane_addr = (uint32_t)(tw * 32) << 16;
+                uint32_t r0[4], r1[4];
+                tmem_ld4(tmem + lane_addr + kColB, r0);
+                if (nj > 1) tmem_ld4(tmem + lane_addr + kColB + 16, r1);
+                tmem_wait_ld();
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-#pragma unroll 2
-                    for (int c = 0; c < 8; ++c) {
-                        const int off = h * kHalf + ((c ^ (k & 7)) << 4);
-                        const uint4 ka = *reinterpret_cast<const uint4*>(krow0 + off);
-                        const uint4 kb = nj > 1 ? *reinterpret_cast<const uint4*>(krow1 + off) : make_uint4(0, 0, 0, 0);
-                        const uint32_t wa[4] = {ka.x, ka.y, ka.z, ka.w};
-                        const uint32_t wb[4] = {kb.x, kb.y, kb.z, kb.w};
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const int d = h * 64 + c * 8 + 2 * e;
-                            const float4 q0 = *reinterpret_cast<const float4*>(qf + d * 4);
-                            const float4 q1 = *reinterpret_cast<const float4*>(qf + d * 4 + 4);
-                            const float a0 = __uint_as_float(wa[e] << 16), a1 = __uint_as_float(wa[e] & 0xffff0000u);
-                            const float b0 = __uint_as_float(wb[e] << 16), b1 = __uint_as_float(wb[e] & 0xffff0000u);
-                            sc0[0] = fmaf(a1, q1.x, fmaf(a0, q0.x, sc0[0]));
-                            sc0[1] = fmaf(a1, q1.y, fmaf(a0, q0.y, sc0[1]));
-                            sc0[2] = fmaf(a1, q1.z, fmaf(a0, q0.z, sc0[2]));
-                            sc0[3] = fmaf(a1, q1.w, fmaf(a0, q0.w, sc0[3]));
-                            sc1[0] = fmaf(b1, q1.x, fmaf(b0, q0.x, sc1[0]));
-                            sc1[1] = fmaf(b1, q1.y, fmaf(b0, q0.y, sc1[1]));
-                            sc1[2] = fmaf(b1, q1.z, fmaf(b0, q0.z, sc1[2]));
-                            sc1[3] = fmaf(b1, q1.w, fmaf(b0, q0.w, sc1[3]));
-                        }
-                    }
+                for (int r = 0; r < 4; ++r) {
+                    sc0[r] = __uint_as_float(r0[r]);
+                    sc1[r] = nj > 1 ? __uint_as_float(r1[r]) : 0.f;
                 }
             }
-            mbar_arrive(&bars[bFreeK0]);   // the tail is done with the K slots
-            if (nj > 1) mbar_arrive(&bars[bFreeK1]);
+            tc_fence_before();
+            mbar_arrive(&bars[bStLd]);
             for (int j = 0; j < nj; ++j) {
                 float sc[4];
 #pragma unroll
@@ -1039,7 +1044,7 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
             }
             named_bar_sync(1, 128);
             // O_t^T(j) in TMEM: lane = dim k, column = tail row
-            ok = ok && mbar_wait(&bars[bPVt], 0);
+            ok = __all_sync(DDT_FULL_MASK, ok && mbar_wait(&bars[bPVt], 0));
             tc_fence_after();
             float o0[16], o1[16];
             {
