@@ -142,8 +142,13 @@ class Workload:
         self.device = device
         self.draft = [cfg1_logits(seed=seed + i).to(device) for i in range(2)]
         self.kcap = PAST + N_VERIFY
-        self.ks = [torch.empty((HKV, self.kcap, HD), dtype=torch.bfloat16, device=device) for _ in range(LAYERS)]
-        self.vs = [torch.empty((HKV, self.kcap, HD), dtype=torch.bfloat16, device=device) for _ in range(LAYERS)]
+        # one allocation per cache tensor kind, as a static KV cache holds it:
+        # every layer's [HKV, kcap, HD] is a view, so the new tree rows of all
+        # layers are one strided region (one 2D copy in the e2e path)
+        self.k_all = torch.empty((LAYERS, HKV, self.kcap, HD), dtype=torch.bfloat16, device=device)
+        self.v_all = torch.empty((LAYERS, HKV, self.kcap, HD), dtype=torch.bfloat16, device=device)
+        self.ks = list(self.k_all.unbind(0))
+        self.vs = list(self.v_all.unbind(0))
         gd = torch.Generator(device=device).manual_seed(seed)
         for t in self.ks:
             t.normal_(generator=gd).mul_(HD ** -0.5)
@@ -284,11 +289,13 @@ def run_ours(args, rank, world, local):
 def run_e2e(args, w: Workload, device, stream, tree_out, table, world, dist):
     """Per step: pinned host draft logits, per-layer queries and new tree K/V
     rows, and verify logits are copied in; the accept result is copied out.
-    The copies run on a copy stream in the order the step needs them, and
-    the compute stream waits on a per-layer event just before each use, so
-    the host-to-device traffic overlaps the kernels (a step still contains
-    all of its own copies: the next step starts after this one's result is
-    back on the host)."""
+    The copies run on a copy stream in the order the step needs them: draft
+    logits, the new K rows of every layer and head in one 2D copy (the cache
+    is one [layers, heads, rows, dim] allocation), the same for V, each
+    layer's queries, then the verify logits.  The compute stream waits on an
+    event just before each use, so the host-to-device traffic overlaps the
+    kernels (a step still contains all of its own copies: the next step
+    starts after this one's result is back on the host)."""
     from ddtree_eagle3_patch_b200 import kernels
     h_draft = [t.cpu().pin_memory() for t in w.draft]
     h_verify = [t.cpu().pin_memory() for t in w.verify]
@@ -308,28 +315,32 @@ def run_e2e(args, w: Workload, device, stream, tree_out, table, world, dist):
     h2d_kind = cudart.cudaMemcpyKind.cudaMemcpyHostToDevice
     row_bytes = N_VERIFY * HD * 2
     copy_stream = torch.cuda.Stream(device)
-    ev_draft, ev_verify = torch.cuda.Event(), torch.cuda.Event()
+    ev_draft, ev_kv, ev_verify = torch.cuda.Event(), torch.cuda.Event(), torch.cuda.Event()
     ev_layer = [torch.cuda.Event() for _ in range(LAYERS)]
+    # (layer, head) rows of the cache are uniformly strided: one 2D copy per tensor kind
+    kv_rows = LAYERS * HKV
+    kv_pitch = w.k_all.stride(1) * 2
+    assert w.k_all.stride(0) == HKV * w.k_all.stride(1) and w.v_all.stride() == w.k_all.stride()
 
     def step(i):
         with torch.cuda.stream(copy_stream):
             d_draft.copy_(h_draft[i % 2], non_blocking=True)
             ev_draft.record(copy_stream)
+            for src, dst in ((h_kt, w.k_all), (h_vt, w.v_all)):
+                err, = cudart.cudaMemcpy2DAsync(dst[:, :, PAST:].data_ptr(), kv_pitch, src.data_ptr(), row_bytes,
+                                                row_bytes, kv_rows, h2d_kind, copy_stream.cuda_stream)
+                if err != cudart.cudaError_t.cudaSuccess:
+                    raise RuntimeError(f"cudaMemcpy2DAsync: {err}")
+            ev_kv.record(copy_stream)
             for layer in range(LAYERS):
                 d_q[layer].copy_(h_q[layer], non_blocking=True)
-                # the new tree rows of every head in one 2D copy per tensor
-                for src, dst in ((h_kt[layer], w.ks[layer]), (h_vt[layer], w.vs[layer])):
-                    err, = cudart.cudaMemcpy2DAsync(dst[:, PAST:].data_ptr(), dst.stride(0) * 2, src.data_ptr(),
-                                                    row_bytes, row_bytes, dst.shape[0], h2d_kind,
-                                                    copy_stream.cuda_stream)
-                    if err != cudart.cudaError_t.cudaSuccess:
-                        raise RuntimeError(f"cudaMemcpy2DAsync: {err}")
                 ev_layer[layer].record(copy_stream)
             d_verify.copy_(h_verify[i % 2], non_blocking=True)
             ev_verify.record(copy_stream)
         with torch.cuda.stream(stream):
             stream.wait_event(ev_draft)
             tree = kernels.tree_build(d_draft, BUDGET, out=tree_out)
+            stream.wait_event(ev_kv)
             for layer in range(LAYERS):
                 stream.wait_event(ev_layer[layer])
                 kernels.tree_attention(d_q[layer], w.ks[layer], w.vs[layer], PAST, tree.visibility, w.scale,
@@ -478,7 +489,8 @@ def run_kernel_only(args, local):
     w = Workload(device, seed=1000)
     tree = kernels.tree_build(w.draft[0], BUDGET)
     lp, ids = tree.top_lp.clone(), tree.top_ids.clone()
-    acc, info, _ = kernels.tree_accept(w.verify[0], tree.parents, tree.node_token_ids, tree.info, max_accept=ROWS + 1)
+    acc, info, post = kernels.tree_accept(w.verify[0], tree.parents, tree.node_token_ids, tree.info,
+                                          max_accept=ROWS + 1)
     tensors = [t for pair in zip(w.ks, w.vs) for t in pair]
 
     def once(i):
@@ -491,7 +503,9 @@ def run_kernel_only(args, local):
         elif args.kernel == "expand":
             kernels.tree_from_log_probs(lp, ids, BUDGET)
         elif args.kernel == "accept":
-            kernels.tree_accept(w.verify[i % 2], tree.parents, tree.node_token_ids, tree.info, max_accept=ROWS + 1)
+            # the step's own preallocated outputs: no allocation or fill per launch
+            kernels.tree_accept(w.verify[i % 2], tree.parents, tree.node_token_ids, tree.info, max_accept=ROWS + 1,
+                                accepted=acc, accept_info=info, posterior=post)
         else:
             kernels.kv_compact(tensors, PAST, N_VERIFY, acc, info[:1], ROWS + 1)
 

@@ -144,8 +144,19 @@ def dtype_code(dt: torch.dtype) -> int:
     raise TypeError(f"unsupported dtype {dt}")
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_of(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
+
+
+def raw_stream(index: int) -> int:
+    """Current CUDA stream handle of device `index` (the cheap form of
+    stream_of, used on per-layer paths where the wrapper's host time counts)."""
+    if _raw_stream is not None:
+        return _raw_stream(index)
+    return torch.cuda.current_stream(index).cuda_stream
 
 
 def require_cuda(t: torch.Tensor, name: str) -> None:
@@ -169,6 +180,10 @@ class Workspaces:
             buf = torch.zeros(max(int(nbytes), 256), dtype=torch.uint8, device=device)
             self._bufs[key] = buf
         return buf
+
+    def current(self, kind: str, index: int):
+        """The buffer of (kind, device index) as it stands, or None."""
+        return self._bufs.get((kind, index))
 
 
 WORKSPACES = Workspaces()

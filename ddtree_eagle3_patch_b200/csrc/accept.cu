@@ -2,9 +2,10 @@
 //
 // accept:  row-wise argmax of the verify logits (model/utils.py:28-30) with
 //          (rows x chunks) CTAs streaming the logits once with 16-byte
-//          loads; the last CTA of a row reduces the chunk winners, the last
-//          row then walks the tree (ddtree.py:290-301) or evaluates the
-//          EAGLE3 paths (eagle3.py:46-79).
+//          loads; each CTA folds its chunk winner into its row's 64-bit word
+//          (atomicMax), and the last CTA of the launch decodes every row,
+//          then walks the tree (ddtree.py:290-301) or evaluates the EAGLE3
+//          paths (eagle3.py:46-79).
 // compact: one launch moves the accepted rows of every cache tensor
 //          (ddtree.py:61-88, 304-369), staging reads in shared memory before
 //          any write so the in-place gather matches index_select + copy_.
@@ -36,34 +37,51 @@ __device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long k)
     return ((unsigned long long)hi << 32) | lo;
 }
 
-// Workspace layout.  The counters sit at fixed offsets for every shape (a
-// counter word is never data in another call's layout), so a zero-filled
-// workspace stays valid across calls of any shape: every completed call
-// leaves its counters at zero again.
+// Workspace layout.  The per-row winner words and the counter sit at fixed
+// offsets for every shape (never data in another call's layout), so a
+// zero-filled workspace stays valid across calls of any shape: every
+// completed call leaves them at zero again.
 constexpr int64_t kMaxRowsPerLaunch = 4096;
 struct WsLayout {
-    size_t row_cnt, done_cnt, part, post, total;
+    size_t row_best, done_cnt, post, total;
 };
 __host__ __device__ inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
-__host__ __device__ inline WsLayout ws_layout(int64_t rows, int64_t chunks) {
+__host__ __device__ inline WsLayout ws_layout(int64_t rows) {
     WsLayout w;
-    w.row_cnt = 0;
-    w.done_cnt = sizeof(uint32_t) * kMaxRowsPerLaunch;
+    w.row_best = 0;
+    w.done_cnt = sizeof(unsigned long long) * kMaxRowsPerLaunch;
     size_t o = align256(w.done_cnt + sizeof(uint32_t) * 4);
-    w.part = o;
-    o = align256(o + sizeof(unsigned long long) * rows * chunks);
     w.post = o;
     o = align256(o + sizeof(int64_t) * rows);
     w.total = o;
     return w;
 }
 
-__host__ inline int64_t choose_chunks(int64_t rows, int64_t vocab, int sms) {
-    // about four CTAs per SM in total, chunks of at least 4096 elements
-    int64_t want = (4 * (int64_t)sms + rows - 1) / rows;
+// Chunks per row: as many CTAs as fit on the GPU at once (one wave),
+// chunks of at least 4096 elements.
+__host__ inline int64_t choose_chunks(int64_t rows, int64_t vocab, int64_t resident_ctas) {
+    int64_t want = resident_ctas / rows;
     int64_t cap = ceil_div(vocab, 4096);
     int64_t c = want < cap ? want : cap;
     return c < 1 ? 1 : c;
+}
+
+// Shared memory of the walk: node tokens and posterior (int64), parents
+// (int32), one entry per verify row.
+struct WalkSmem {
+    int64_t* tok;
+    int64_t* post;
+    int32_t* par;
+};
+__host__ __device__ inline size_t walk_smem_bytes(int64_t n_rows) {
+    return (2 * sizeof(int64_t) + sizeof(int32_t)) * (size_t)n_rows;
+}
+__device__ inline WalkSmem carve_walk(unsigned char* smem, int64_t n_rows) {
+    WalkSmem w;
+    w.tok = reinterpret_cast<int64_t*>(smem);
+    w.post = w.tok + n_rows;
+    w.par = reinterpret_cast<int32_t*>(w.post + n_rows);
+    return w;
 }
 __host__ inline int64_t chunk_len_for(int64_t vocab, int64_t chunks) {
     int64_t len = ceil_div(vocab, chunks);
@@ -88,21 +106,28 @@ struct TailArgs {
     int64_t* e3_accepted;
 };
 
-__device__ void tree_walk(const int64_t* post, int64_t n_rows, const TailArgs& a, unsigned char* smem) {
-    int32_t* s_par = reinterpret_cast<int32_t*>(smem);
-    int64_t* s_tok = reinterpret_cast<int64_t*>(smem + sizeof(int32_t) * kMaxNodes);
+// The walk (ddtree.py:290-301).  Parents, node tokens and the posterior go
+// to shared memory first (the posterior may already be there), so no step
+// waits on a global load.
+__device__ void tree_walk(const int64_t* post, int64_t n_rows, const TailArgs& a, unsigned char* smem,
+                          bool post_in_smem) {
+    const WalkSmem w = carve_walk(smem, n_rows);
+    int64_t* s_tok = w.tok;
+    int64_t* s_post = w.post;
+    int32_t* s_par = w.par;
     int n = (int)(n_rows - 1);
     if (a.n_nodes_dev) n = min(n, (int)*a.n_nodes_dev);
     n = min(n, kMaxNodes - 1);
     for (int i = threadIdx.x; i <= n; i += kThreads) {
         s_par[i] = i == 0 ? -1 : __ldcg(a.parents + i);
         s_tok[i] = i == 0 ? -1 : __ldcg(a.node_tokens + i - 1);
+        if (!post_in_smem) s_post[i] = __ldcg(post + i);
     }
     __syncthreads();
     if (threadIdx.x < 32) {
         const int lane = threadIdx.x;
         int cur = 0;
-        int64_t nxt = __ldcg(post + 0);
+        int64_t nxt = s_post[0];
         int64_t count = 1;
         if (lane == 0 && a.max_accept > 0) a.accepted[0] = 0;
         for (;;) {
@@ -120,7 +145,7 @@ __device__ void tree_walk(const int64_t* post, int64_t n_rows, const TailArgs& a
             cur = child;
             if (lane == 0 && count < a.max_accept) a.accepted[count] = cur;
             count += 1;
-            nxt = __ldcg(post + cur);
+            nxt = s_post[cur];
         }
         if (lane == 0) {
             a.accept_info[0] = count;
@@ -170,15 +195,14 @@ __device__ void eagle3_eval(const int64_t* post, const TailArgs& a, unsigned cha
 
 template <typename T, bool kVec>
 __global__ void __launch_bounds__(kThreads)
-argmax_kernel(const T* __restrict__ logits, int64_t n_rows, int64_t vocab, int64_t row_stride, int chunks,
-              int64_t chunk_len, int64_t* posterior, unsigned char* ws, int mode, TailArgs tail) {
+argmax_kernel(const T* __restrict__ logits, int64_t n_rows, int64_t vocab, int64_t row_stride, int64_t chunk_len,
+              int64_t* posterior, unsigned char* ws, int mode, TailArgs tail) {
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ unsigned long long s_red[kWarps];
     __shared__ int s_flag;
-    const WsLayout L = ws_layout(n_rows, chunks);
-    uint32_t* row_cnt = reinterpret_cast<uint32_t*>(ws + L.row_cnt);
+    const WsLayout L = ws_layout(n_rows);
+    unsigned long long* row_best = reinterpret_cast<unsigned long long*>(ws + L.row_best);
     uint32_t* done_cnt = reinterpret_cast<uint32_t*>(ws + L.done_cnt);
-    unsigned long long* part = reinterpret_cast<unsigned long long*>(ws + L.part);
     int64_t* post = reinterpret_cast<int64_t*>(ws + L.post);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -190,69 +214,89 @@ argmax_kernel(const T* __restrict__ logits, int64_t n_rows, int64_t vocab, int64
     constexpr int kEpv = 16 / sizeof(T);
 
     unsigned long long best = 0ull;
-    for (int64_t base = c0 + (int64_t)tid * kEpv; base < c1; base += (int64_t)kThreads * kEpv) {
-        if (kVec && base + kEpv <= c1) {
-            const uint4 raw = __ldcs(reinterpret_cast<const uint4*>(rowp + base));
-            const T* pv = reinterpret_cast<const T*>(&raw);
+    const int64_t step = (int64_t)kThreads * kEpv;
+    int64_t base = c0 + (int64_t)tid * kEpv;
+    auto scan_vec = [&](const uint4& raw, int64_t b) {
+        const T* pv = reinterpret_cast<const T*>(&raw);
 #pragma unroll
-            for (int e = 0; e < kEpv; ++e) {
-                const unsigned long long k = argmax_key(to_f32<T>(pv[e]), base + e);
-                best = k > best ? k : best;
+        for (int e = 0; e < kEpv; ++e) {
+            const unsigned long long k = argmax_key(to_f32<T>(pv[e]), b + e);
+            best = k > best ? k : best;
+        }
+    };
+    if (kVec) {
+        // batches of eight independent 16-byte loads per thread (the scan is
+        // bound by memory latency otherwise), then one predicated batch for
+        // the rest of this thread's whole vectors and at most one partial
+        // vector; the max is order-independent
+        constexpr int U = 8;
+        for (; base + (U - 1) * step + kEpv <= c1; base += U * step) {
+            uint4 raw[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) raw[u] = __ldcs(reinterpret_cast<const uint4*>(rowp + base + u * step));
+#pragma unroll
+            for (int u = 0; u < U; ++u) scan_vec(raw[u], base + u * step);
+        }
+        uint4 raw[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int64_t b = base + u * step;
+            raw[u] = b + kEpv <= c1 ? __ldcs(reinterpret_cast<const uint4*>(rowp + b)) : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int64_t b = base + u * step;
+            if (b + kEpv <= c1) {
+                scan_vec(raw[u], b);
+            } else if (b < c1) {
+                for (int64_t i = b; i < c1; ++i) {
+                    const unsigned long long k = argmax_key(to_f32<T>(rowp[i]), i);
+                    best = k > best ? k : best;
+                }
             }
-        } else {
-            for (int e = 0; e < kEpv && base + e < c1; ++e) {
-                const unsigned long long k = argmax_key(to_f32<T>(rowp[base + e]), base + e);
-                best = k > best ? k : best;
-            }
+        }
+    } else {
+        for (int64_t i = c0 + tid; i < c1; i += kThreads) {
+            const unsigned long long k = argmax_key(to_f32<T>(rowp[i]), i);
+            best = k > best ? k : best;
         }
     }
     best = warp_max_u64(best);
     if (lane == 0) s_red[warp] = best;
     __syncthreads();
-    if (warp == 0) {
-        unsigned long long k = lane < kWarps ? s_red[lane] : 0ull;
-        k = warp_max_u64(k);
-        if (lane == 0) part[r * chunks + c] = k;
-    }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) s_flag = (atomicAdd(&row_cnt[r], 1u) == (uint32_t)(chunks - 1)) ? 1 : 0;
-    __syncthreads();
-    if (!s_flag) return;
-    __threadfence();
-    // last CTA of the row: reduce the chunk winners
-    if (warp == 0) {
+    // one hand-off: the CTA's winner goes into its row's word, and the last
+    // CTA of the launch decodes every row
+    if (tid == 0) {
         unsigned long long k = 0ull;
-        for (int q = lane; q < chunks; q += 32) {
-            const unsigned long long v = __ldcg(part + r * chunks + q);
-            k = v > k ? v : k;
-        }
-        k = warp_max_u64(k);
-        if (lane == 0) {
-            const int64_t idx = (int64_t)(0xffffffffu - (uint32_t)(k & 0xffffffffu));
-            post[r] = idx;
-            if (posterior) posterior[r] = idx;
-            row_cnt[r] = 0u;
-        }
+        for (int w = 0; w < kWarps; ++w) k = s_red[w] > k ? s_red[w] : k;
+        atomicMax(&row_best[r], k);
+        __threadfence();
+        s_flag = (atomicAdd(&done_cnt[0], 1u) == gridDim.x * gridDim.y - 1) ? 1 : 0;
     }
-    if (mode == kArgmaxOnly) return;
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) s_flag = (atomicAdd(&done_cnt[0], 1u) == (uint32_t)(n_rows - 1)) ? 1 : 0;
     __syncthreads();
     if (!s_flag) return;
     __threadfence();
+    int64_t* s_post = mode == kTreeWalk ? carve_walk(smem, n_rows).post : nullptr;
+    for (int64_t q = tid; q < n_rows; q += kThreads) {
+        const unsigned long long k = atomicExch(&row_best[q], 0ull);   // read, and reset for the next call
+        const int64_t idx = (int64_t)(0xffffffffu - (uint32_t)(k & 0xffffffffu));
+        post[q] = idx;
+        if (posterior) posterior[q] = idx;
+        if (s_post) s_post[q] = idx;
+    }
+    if (tid == 0) done_cnt[0] = 0u;
+    if (mode == kArgmaxOnly) return;
+    __syncthreads();
     if (mode == kTreeWalk)
-        tree_walk(post, n_rows, tail, smem);
+        tree_walk(post, n_rows, tail, smem, true);
     else
         eagle3_eval(post, tail, smem);
-    if (tid == 0) done_cnt[0] = 0u;
 }
 
 // Walk alone, from a posterior already on the device (ddtree.py:290-301).
 __global__ void __launch_bounds__(kThreads) tree_walk_kernel(const int64_t* posterior, int64_t n_rows, TailArgs tail) {
     extern __shared__ __align__(16) unsigned char smem[];
-    tree_walk(posterior, n_rows, tail, smem);
+    tree_walk(posterior, n_rows, tail, smem, false);
 }
 
 // ---------------------------------------------------------------------------
@@ -314,6 +358,34 @@ kv_compact_kernel(void* const* tensors, int64_t heads, int64_t row_bytes, int64_
 using namespace ddt;
 using namespace ddt::accept;
 
+template <typename T, bool V>
+static int launch_argmax_t(const void* logits, int64_t n_rows, int64_t vocab, int64_t row_stride, size_t esz,
+                           int64_t* posterior, unsigned char* ws, int mode, const TailArgs& tail, cudaStream_t st) {
+    auto k = argmax_kernel<T, V>;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const size_t smem = mode == kTreeWalk ? walk_smem_bytes(n_rows < kMaxRowsPerLaunch ? n_rows : kMaxRowsPerLaunch) : 0;
+    if (smem > 48 * 1024 && cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+        return check_launch("cudaFuncSetAttribute(argmax_kernel)");
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k, kThreads, smem) != cudaSuccess || occ < 1) {
+        cudaGetLastError();
+        occ = 1;
+    }
+    const char* base = static_cast<const char*>(logits);
+    for (int64_t r0 = 0; r0 < n_rows; r0 += kMaxRowsPerLaunch) {
+        const int64_t nr = n_rows - r0 < kMaxRowsPerLaunch ? n_rows - r0 : kMaxRowsPerLaunch;
+        const int64_t chunks = choose_chunks(nr, vocab, (int64_t)occ * ddt_sm_count(dev));
+        const int64_t clen = chunk_len_for(vocab, chunks);
+        const int64_t nchunks = ceil_div(vocab, clen);
+        const T* lg = reinterpret_cast<const T*>(base + r0 * row_stride * (int64_t)esz);
+        int64_t* post_out = posterior ? posterior + r0 : nullptr;
+        k<<<dim3((unsigned)nchunks, (unsigned)nr), kThreads, smem, st>>>(lg, nr, vocab, row_stride, clen, post_out, ws,
+                                                                        mode, tail);
+    }
+    return check_launch("argmax_kernel");
+}
+
 static int launch_argmax(const void* logits, int dtype, int64_t n_rows, int64_t vocab, int64_t row_stride,
                          int64_t* posterior, void* workspace, size_t workspace_bytes, int mode, const TailArgs& tail,
                          cudaStream_t st) {
@@ -321,53 +393,30 @@ static int launch_argmax(const void* logits, int dtype, int64_t n_rows, int64_t 
     if (n_rows <= 0 || vocab <= 0 || vocab >= ((int64_t)1 << 31)) return set_error(DDT_EINVAL, "bad logits shape");
     if (row_stride < vocab) return set_error(DDT_EINVAL, "row_stride < vocab");
     if (dtype != DDT_F32 && dtype != DDT_BF16 && dtype != DDT_F16) return set_error(DDT_EINVAL, "dtype %d", dtype);
-    int dev = 0;
-    cudaGetDevice(&dev);
-    const int64_t chunks = choose_chunks(n_rows, vocab, ddt_sm_count(dev));
-    const int64_t clen = chunk_len_for(vocab, chunks);
-    const int64_t nchunks = ceil_div(vocab, clen);
     if (mode != kArgmaxOnly && n_rows > kMaxRowsPerLaunch)
         return set_error(DDT_EUNSUPPORTED, "n_rows=%lld > %lld", (long long)n_rows, (long long)kMaxRowsPerLaunch);
-    const WsLayout L = ws_layout(n_rows < kMaxRowsPerLaunch ? n_rows : kMaxRowsPerLaunch, nchunks);
+    const WsLayout L = ws_layout(n_rows < kMaxRowsPerLaunch ? n_rows : kMaxRowsPerLaunch);
     if (!workspace || workspace_bytes < L.total)
         return set_error(DDT_EWORKSPACE, "accept workspace needs %zu bytes, got %zu", L.total, workspace_bytes);
     if (reinterpret_cast<uintptr_t>(workspace) % 256) return set_error(DDT_EINVAL, "workspace must be 256-byte aligned");
     const size_t esz = dtype == DDT_F32 ? 4 : 2;
     const bool vec = (reinterpret_cast<uintptr_t>(logits) % 16 == 0) && ((row_stride * esz) % 16 == 0);
-    const size_t smem = mode == kTreeWalk ? (sizeof(int32_t) + sizeof(int64_t)) * kMaxNodes : 0;
     unsigned char* ws = static_cast<unsigned char*>(workspace);
-    const char* base = static_cast<const char*>(logits);
-    for (int64_t r0 = 0; r0 < n_rows; r0 += kMaxRowsPerLaunch) {
-        const int64_t nr = n_rows - r0 < kMaxRowsPerLaunch ? n_rows - r0 : kMaxRowsPerLaunch;
-        const void* lg = base + r0 * row_stride * (int64_t)esz;
-        int64_t* post_out = posterior ? posterior + r0 : nullptr;
-        dim3 grid((unsigned)nchunks, (unsigned)nr);
-#define DDT_LAUNCH_AM(T, V)                                                                                      \
-    do {                                                                                                         \
-        auto k = argmax_kernel<T, V>;                                                                            \
-        if (smem > 48 * 1024 &&                                                                                  \
-            cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)      \
-            return check_launch("cudaFuncSetAttribute(argmax_kernel)");                                          \
-        k<<<grid, kThreads, smem, st>>>(static_cast<const T*>(lg), nr, vocab, row_stride, (int)nchunks, clen,    \
-                                        post_out, ws, mode, tail);                                               \
-    } while (0)
-        if (dtype == DDT_F32) {
-            if (vec) DDT_LAUNCH_AM(float, true); else DDT_LAUNCH_AM(float, false);
-        } else if (dtype == DDT_BF16) {
-            if (vec) DDT_LAUNCH_AM(__nv_bfloat16, true); else DDT_LAUNCH_AM(__nv_bfloat16, false);
-        } else {
-            if (vec) DDT_LAUNCH_AM(__half, true); else DDT_LAUNCH_AM(__half, false);
-        }
-    }
-#undef DDT_LAUNCH_AM
-    return check_launch("argmax_kernel");
+    if (dtype == DDT_F32)
+        return vec ? launch_argmax_t<float, true>(logits, n_rows, vocab, row_stride, esz, posterior, ws, mode, tail, st)
+                   : launch_argmax_t<float, false>(logits, n_rows, vocab, row_stride, esz, posterior, ws, mode, tail, st);
+    if (dtype == DDT_BF16)
+        return vec ? launch_argmax_t<__nv_bfloat16, true>(logits, n_rows, vocab, row_stride, esz, posterior, ws, mode,
+                                                          tail, st)
+                   : launch_argmax_t<__nv_bfloat16, false>(logits, n_rows, vocab, row_stride, esz, posterior, ws, mode,
+                                                           tail, st);
+    return vec ? launch_argmax_t<__half, true>(logits, n_rows, vocab, row_stride, esz, posterior, ws, mode, tail, st)
+               : launch_argmax_t<__half, false>(logits, n_rows, vocab, row_stride, esz, posterior, ws, mode, tail, st);
 }
 
 extern "C" size_t ddt_tree_accept_workspace_size(int64_t n_rows, int64_t vocab) {
     if (n_rows <= 0 || vocab <= 0) return 256;
-    // largest chunk count any device could choose (chunks of >= 4096 elements)
-    const int64_t chunks = ceil_div(vocab, 4096);
-    return ws_layout(n_rows < kMaxRowsPerLaunch ? n_rows : kMaxRowsPerLaunch, chunks).total;
+    return ws_layout(n_rows < kMaxRowsPerLaunch ? n_rows : kMaxRowsPerLaunch).total;
 }
 
 extern "C" int ddt_argmax_rows(const void* logits, int dtype, int64_t n_rows, int64_t vocab, int64_t row_stride,
@@ -411,7 +460,7 @@ extern "C" int ddt_tree_walk(const int64_t* posterior, int64_t n_rows, const int
     tail.accepted = accepted;
     tail.max_accept = max_accept;
     tail.accept_info = accept_info;
-    const size_t smem = (sizeof(int32_t) + sizeof(int64_t)) * kMaxNodes;
+    const size_t smem = walk_smem_bytes(n_rows);
     tree_walk_kernel<<<1, kThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(posterior, n_rows, tail);
     return check_launch("tree_walk_kernel");
 }

@@ -1,11 +1,14 @@
 // Kernel (1): DDTree tree build on sm_100a.
 //
 // Restates build_ddtree_tree (ddtree.py:114-196) as one launch:
-//   phase A  (rows x chunks CTAs)  per chunk of a draft row: max, sum of
-//            exp, and the chunk's top-k candidates by a block radix select on
-//            64-bit keys (value, then lower token id) - ddtree.py:136-138;
-//   phase B  (last CTA of a row)   merge the chunk candidates into the row's
-//            top-k, sort it, log-normaliser, lp = top - log_z  (ddtree.py:139);
+//   phase A  (rows x chunks CTAs)  per chunk of a draft row, staged in shared
+//            memory: max, sum of exp, and the chunk's top-k on 64-bit keys
+//            (value, then lower token id), written sorted - ddtree.py:136-138:
+//            a warp-sorted lower bound gathers a few candidates, ranked by
+//            counting (radix select when there are many);
+//   phase B  (last CTA of a row)   the row's top-k from the sorted chunk
+//            lists: the keys at or above the largest list tail, ranked by
+//            counting; log-normaliser, lp = top - log_z  (ddtree.py:139);
 //   phase C  (last CTA overall)    the best-first expansion, restated exactly
 //            with one warp doing the frontier arg-min each step
 //            (ddtree.py:146-177), then parents / depths / tokens, the packed
@@ -24,12 +27,13 @@ namespace tree {
 
 constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
-constexpr int kValsPerThread = 32;
-constexpr int kMaxChunk = kThreads * kValsPerThread;  // 16384 elements
+constexpr int kValsPerThread = 40;
+constexpr int kMaxChunk = kThreads * kValsPerThread;  // 20480 elements: a 151936-wide row in 8 chunks
 constexpr int kCandCap = 2048;
 constexpr int kMaxRows = 32;
 constexpr int kMaxBudget = 1024;
 constexpr int kMergeCap = 16384;  // chunks * topk keys held by the merging CTA
+constexpr int kRankCap = 256;     // candidate counts ranked directly (rank = number of larger keys)
 
 struct SelectScratch {
     uint32_t hist[256];
@@ -210,26 +214,6 @@ __device__ unsigned long long block_kth_largest_regs(KeyAt key_at, int K, Select
     const unsigned long long t = s->prefix;
     __syncthreads();
     return t;
-}
-
-// Descending bitonic sort of P (power of two) keys in shared memory.
-__device__ void bitonic_sort_desc(unsigned long long* a, int P) {
-    for (int k = 2; k <= P; k <<= 1) {
-        for (int j = k >> 1; j > 0; j >>= 1) {
-            for (int i = threadIdx.x; i < P; i += kThreads) {
-                const int ixj = i ^ j;
-                if (ixj > i) {
-                    const bool desc = (i & k) == 0;
-                    const unsigned long long x = a[i], y = a[ixj];
-                    if (desc ? (x < y) : (x > y)) {
-                        a[i] = y;
-                        a[ixj] = x;
-                    }
-                }
-            }
-            __syncthreads();
-        }
-    }
 }
 
 __device__ __forceinline__ unsigned long long make_key(float v, int64_t idx) {
@@ -665,6 +649,7 @@ tree_build_kernel(const T* __restrict__ logits, int rows, int64_t vocab, int64_t
                   unsigned char* ws) {
     extern __shared__ __align__(256) unsigned char smem[];
     __shared__ SelectScratch sel;
+    __shared__ unsigned long long s_offer[kWarps];
     __shared__ double red_d[kWarps];
     __shared__ float red_f[kWarps];
     __shared__ int s_flag;
@@ -684,95 +669,125 @@ tree_build_kernel(const T* __restrict__ logits, int rows, int64_t vocab, int64_t
     const int64_t c0 = (int64_t)c * chunk_len;
     const int64_t c1 = min(c0 + chunk_len, vocab);
 
-    // ---- load the chunk into registers --------------------------------
+    // ---- load the chunk into shared memory ----------------------------
+    // Thread tid holds the 16-byte vectors tid, tid + kThreads, ... of the
+    // chunk; its values stay in shared memory (chunk-local index) rather
+    // than registers, and each thread only ever reads back its own.
     constexpr int kEpv = 16 / sizeof(T);  // elements per 16-byte vector
-    float vals[kValsPerThread];
-    uint32_t valid = 0;
+    unsigned long long* maxkeys = reinterpret_cast<unsigned long long*>(smem);
+    unsigned long long* cand = maxkeys + kThreads;
+    unsigned long long* top = cand + kCandCap;
+    float* cv = reinterpret_cast<float*>(top + kMaxBudget);
+    const int n_valid = (int)(c1 - c0);
 #pragma unroll
     for (int j = 0; j < kValsPerThread / kEpv; ++j) {
-        const int64_t base = c0 + ((int64_t)j * kThreads + tid) * kEpv;
-        if (kVec && base + kEpv <= c1) {
-            const uint4 raw = __ldcs(reinterpret_cast<const uint4*>(rowp + base));
+        const int loc = (j * kThreads + tid) * kEpv;
+        float v[kEpv];
+        if (kVec && loc + kEpv <= n_valid) {
+            const uint4 raw = __ldcs(reinterpret_cast<const uint4*>(rowp + c0 + loc));
             const T* pv = reinterpret_cast<const T*>(&raw);
 #pragma unroll
-            for (int e = 0; e < kEpv; ++e) {
-                vals[j * kEpv + e] = to_f32<T>(pv[e]);
-                valid |= 1u << (j * kEpv + e);
-            }
+            for (int e = 0; e < kEpv; ++e) v[e] = to_f32<T>(pv[e]);
         } else {
 #pragma unroll
-            for (int e = 0; e < kEpv; ++e) {
-                const int64_t idx = base + e;
-                if (idx < c1) {
-                    vals[j * kEpv + e] = to_f32<T>(rowp[idx]);
-                    valid |= 1u << (j * kEpv + e);
-                } else {
-                    vals[j * kEpv + e] = -INFINITY;
-                }
+            for (int e = 0; e < kEpv; ++e) v[e] = loc + e < n_valid ? to_f32<T>(rowp[c0 + loc + e]) : -INFINITY;
+        }
+#pragma unroll
+        for (int e = 0; e < kEpv; e += 4)
+            *reinterpret_cast<float4*>(cv + loc + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+    }
+    auto loc_of = [&](int j) -> int { return ((j / kEpv) * kThreads + tid) * kEpv + (j % kEpv); };
+    // visits this thread's values in index order with 16-byte shared loads
+    // (a warp reads 512 consecutive bytes: no bank conflicts)
+    auto for_vals = [&](auto&& f) {
+#pragma unroll 2
+        for (int jv = 0; jv < kValsPerThread / kEpv; ++jv) {
+            const int loc = (jv * kThreads + tid) * kEpv;
+#pragma unroll
+            for (int h = 0; h < kEpv; h += 4) {
+                const float4 q = *reinterpret_cast<const float4*>(cv + loc + h);
+                f(q.x, loc + h);
+                f(q.y, loc + h + 1);
+                f(q.z, loc + h + 2);
+                f(q.w, loc + h + 3);
             }
         }
-    }
-    auto elem_index = [&](int j) -> int64_t {
-        return c0 + ((int64_t)(j / kEpv) * kThreads + tid) * kEpv + (j % kEpv);
     };
 
     // ---- max and sum of exp (logsumexp pieces, ddtree.py:138) ----------
     float m = -INFINITY;
     bool nan_seen = false;
-#pragma unroll
-    for (int j = 0; j < kValsPerThread; ++j) {
-        if (valid >> j & 1u) {
-            const float v = vals[j];
+    for_vals([&](float v, int loc) {
+        if (loc < n_valid) {
             nan_seen |= (v != v);
             m = fmaxf(m, v);
         }
-    }
+    });
     if (tid == 0) s_flag = 0;
     __syncthreads();
     if (nan_seen) s_flag = 1;
     m = block_max(m, red_f);
     float sum_t = 0.f;
-    if (m != -INFINITY && m == m) {
-#pragma unroll
-        for (int j = 0; j < kValsPerThread; ++j)
-            if (valid >> j & 1u) sum_t += expf(vals[j] - m);
-    }
+    if (m != -INFINITY && m == m)
+        for_vals([&](float v, int loc) {
+            if (loc < n_valid) sum_t += expf(v - m);
+        });
     const double sum_c = block_sum_d((double)sum_t, red_d);
 
     // ---- chunk top-k candidates ----------------------------------------
-    const int n_valid = (int)(c1 - c0);
+    // Keys are (value order, then lower token id) and distinct.  The chunk's
+    // top kc keys go to part_keys in descending order, padded with zeros.
     const int kc = min(topk, n_valid);
-    uint32_t ov[kValsPerThread];
-    unsigned long long tmax = 0ull;
-#pragma unroll
-    for (int j = 0; j < kValsPerThread; ++j) ov[j] = ord_f32(vals[j]);
-    auto key_at = [&](int j) -> unsigned long long {
-        return (valid >> j & 1u) ? (((unsigned long long)ov[j] << 32) |
-                                    (unsigned long long)(0xffffffffu - (uint32_t)elem_index(j)))
-                                 : 0ull;
+    const int lane = tid & 31, warp = tid >> 5;
+    auto key_of = [&](float v, int loc) -> unsigned long long {
+        return loc < n_valid ? (((unsigned long long)ord_f32(v) << 32) |
+                                (unsigned long long)(0xffffffffu - (uint32_t)(c0 + loc)))
+                             : 0ull;
     };
-#pragma unroll
-    for (int j = 0; j < kValsPerThread; ++j) {
-        const unsigned long long k = key_at(j);
+    auto key_at = [&](int j) -> unsigned long long {
+        const int loc = loc_of(j);
+        return key_of(cv[loc], loc);
+    };
+    unsigned long long tmax = 0ull;
+    for_vals([&](float v, int loc) {
+        const unsigned long long k = key_of(v, loc);
         tmax = k > tmax ? k : tmax;
-    }
-    unsigned long long* maxkeys = reinterpret_cast<unsigned long long*>(smem);
-    unsigned long long* cand = maxkeys + kThreads;
+    });
     unsigned long long* dst = part_keys + ((int64_t)d * chunks + c) * topk;
     maxkeys[tid] = tmax;
     if (tid == 0) sel.count = 0;
     __syncthreads();
+    // A lower bound t0 on the kc-th largest key: each warp sorts its 32
+    // thread maxima (distinct: every thread holds a valid value here) and
+    // offers its q-th largest, q = ceil(kc / kWarps); at least q * kWarps >= kc
+    // keys are >= the smallest offer, so every key of the top kc is too.
     unsigned long long t0 = 0ull;
-    if (n_valid > kCandCap && kc <= kThreads) t0 = block_kth_largest(maxkeys, kThreads, kc, &sel);
-    // gather keys >= t0 (warp-aggregated slots)
+    if (n_valid > kCandCap && kc <= kThreads) {
+        const int q = (kc + kWarps - 1) / kWarps;
+        unsigned long long x = tmax;
 #pragma unroll
-    for (int j = 0; j < kValsPerThread; ++j) {
-        const unsigned long long kj = key_at(j);
+        for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+            for (int jj = k >> 1; jj > 0; jj >>= 1) {
+                const unsigned long long y = __shfl_xor_sync(DDT_FULL_MASK, x, jj);
+                const bool keep_max = ((lane & jj) == 0) == ((lane & k) == 0);
+                x = keep_max ? (x > y ? x : y) : (x < y ? x : y);
+            }
+        }
+        const unsigned long long offer = __shfl_sync(DDT_FULL_MASK, x, q - 1);   // lane i: (i+1)-th largest
+        if (lane == 0) s_offer[warp] = offer;
+        __syncthreads();
+        t0 = s_offer[0];
+#pragma unroll
+        for (int w = 1; w < kWarps; ++w) t0 = s_offer[w] < t0 ? s_offer[w] : t0;
+    }
+    // gather keys >= t0 (warp-aggregated slots)
+    for_vals([&](float v, int loc) {
+        const unsigned long long kj = key_of(v, loc);
         const bool take = kj != 0ull && kj >= t0;
         const uint32_t b = __ballot_sync(DDT_FULL_MASK, take);
         if (b) {
             int base = 0;
-            const int lane = tid & 31;
             if (lane == __ffs(b) - 1) base = atomicAdd(&sel.count, __popc(b));
             base = __shfl_sync(DDT_FULL_MASK, base, __ffs(b) - 1);
             if (take) {
@@ -780,29 +795,47 @@ tree_build_kernel(const T* __restrict__ logits, int rows, int64_t vocab, int64_t
                 if (pos < kCandCap) cand[pos] = kj;
             }
         }
-    }
+    });
     __syncthreads();
     const int ncand = sel.count;
     __syncthreads();
     if (tid == 0) sel.count = 0;
-    if (ncand <= kCandCap) {
-        const unsigned long long t1 = block_kth_largest(cand, ncand, kc, &sel);
+    if (ncand <= kRankCap) {
+        // few candidates: a candidate's rank is the number of larger ones
         for (int i = tid; i < ncand; i += kThreads) {
             const unsigned long long k = cand[i];
-            if (k >= t1) {
-                const int pos = atomicAdd(&sel.count, 1);
-                if (pos < topk) dst[pos] = k;
-            }
+            int r = 0;
+            for (int q = 0; q < ncand; ++q) r += cand[q] > k ? 1 : 0;
+            if (r < kc) dst[r] = k;
         }
     } else {
-        const unsigned long long t1 = block_kth_largest_regs(key_at, kc, &sel);
-#pragma unroll
-        for (int j = 0; j < kValsPerThread; ++j) {
-            const unsigned long long kj = key_at(j);
-            if (kj != 0ull && kj >= t1) {
-                const int pos = atomicAdd(&sel.count, 1);
-                if (pos < topk) dst[pos] = kj;
+        // radix select of the kc-th largest, the selected keys into `top`,
+        // then ranked among themselves
+        if (ncand <= kCandCap) {
+            const unsigned long long t1 = block_kth_largest(cand, ncand, kc, &sel);
+            for (int i = tid; i < ncand; i += kThreads) {
+                const unsigned long long k = cand[i];
+                if (k >= t1) {
+                    const int pos = atomicAdd(&sel.count, 1);
+                    if (pos < kc) top[pos] = k;
+                }
             }
+        } else {
+            const unsigned long long t1 = block_kth_largest_regs(key_at, kc, &sel);
+            for (int j = 0; j < kValsPerThread; ++j) {
+                const unsigned long long kj = key_at(j);
+                if (kj != 0ull && kj >= t1) {
+                    const int pos = atomicAdd(&sel.count, 1);
+                    if (pos < kc) top[pos] = kj;
+                }
+            }
+        }
+        __syncthreads();
+        for (int i = tid; i < kc; i += kThreads) {
+            const unsigned long long k = top[i];
+            int r = 0;
+            for (int q = 0; q < kc; ++q) r += top[q] > k ? 1 : 0;
+            dst[r] = k;
         }
     }
     for (int i = kc + tid; i < topk; i += kThreads) dst[i] = 0ull;
@@ -820,52 +853,102 @@ tree_build_kernel(const T* __restrict__ logits, int rows, int64_t vocab, int64_t
     __threadfence();
 
     // ---- phase B: merge the row ------------------------------------------
+    // Every chunk list is sorted (descending, zero-padded) and the nonzero
+    // keys of a row are distinct.  Each list lies entirely at or above its
+    // last entry, so the largest last entry is at most the row's topk-th
+    // key: the keys at or above it are gathered and ranked by counting (a
+    // radix select first when they are many); the topk best land in order.
     {
         const int n = chunks * topk;
         unsigned long long* mk = reinterpret_cast<unsigned long long*>(smem);
-        int P = 1;
-        while (P < topk) P <<= 1;
         unsigned long long* sk = mk + n;
+        unsigned long long* bc = sk + topk;   // gathered keys (at most n)
         const unsigned long long* src = part_keys + (int64_t)d * chunks * topk;
         for (int i = tid; i < n; i += kThreads) mk[i] = __ldcg(src + i);
-        for (int i = tid; i < P; i += kThreads) sk[i] = 0ull;
+        for (int i = tid; i < topk; i += kThreads) sk[i] = 0ull;
         if (tid == 0) sel.count = 0;
         __syncthreads();
-        const unsigned long long t = block_kth_largest(mk, n, topk, &sel);
-        for (int i = tid; i < n; i += kThreads) {
-            const unsigned long long k = mk[i];
-            if (k != 0ull && k >= t) {
-                const int pos = atomicAdd(&sel.count, 1);
-                if (pos < topk) sk[pos] = k;
+        unsigned long long lb = 0ull;
+        for (int q = 0; q < chunks; ++q) {
+            const unsigned long long e = mk[q * topk + topk - 1];
+            lb = e > lb ? e : lb;
+        }
+        const int lane_b = tid & 31;
+        for (int i0 = 0; i0 < n; i0 += kThreads) {
+            const int i = i0 + tid;
+            const unsigned long long x = i < n ? mk[i] : 0ull;
+            const bool take = x != 0ull && x >= lb;
+            const uint32_t bm = __ballot_sync(DDT_FULL_MASK, take);
+            if (bm) {
+                int base = 0;
+                if (lane_b == __ffs(bm) - 1) base = atomicAdd(&sel.count, __popc(bm));
+                base = __shfl_sync(DDT_FULL_MASK, base, __ffs(bm) - 1);
+                if (take) bc[base + __popc(bm & ((1u << lane_b) - 1u))] = x;
             }
         }
         __syncthreads();
-        bitonic_sort_desc(sk, P);
+        const int nb = sel.count;
+        __syncthreads();
+        if (nb <= kRankCap) {
+            for (int i = tid; i < nb; i += kThreads) {
+                const unsigned long long x = bc[i];
+                int r = 0;
+                for (int q = 0; q < nb; ++q) r += bc[q] > x ? 1 : 0;
+                if (r < topk) sk[r] = x;
+            }
+        } else {
+            if (tid == 0) sel.count = 0;
+            const int kt = min(topk, nb);
+            const unsigned long long t = block_kth_largest(bc, nb, kt, &sel);
+            for (int i = tid; i < nb; i += kThreads) {
+                const unsigned long long x = bc[i];
+                if (x >= t) {
+                    const int pos = atomicAdd(&sel.count, 1);
+                    if (pos < kt) mk[pos] = x;   // the chunk lists are no longer needed
+                }
+            }
+            __syncthreads();
+            for (int i = tid; i < kt; i += kThreads) {
+                const unsigned long long x = mk[i];
+                int r = 0;
+                for (int q = 0; q < kt; ++q) r += mk[q] > x ? 1 : 0;
+                sk[r] = x;
+            }
+        }
+        // log-normaliser: warp 0 combines the chunks' (max, sum of exp)
         __shared__ float s_logz;
-        if (tid == 0) {
+        if (tid < 32) {
             float M = -INFINITY;
             bool nan_row = false;
-            for (int q = 0; q < chunks; ++q) {
+            for (int q = lane_b; q < chunks; q += 32) {
                 const float mq = __ldcg(part_m + d * chunks + q);
                 nan_row |= (mq != mq);
                 M = fmaxf(M, mq);
             }
-            float lz;
-            if (nan_row) {
-                lz = __int_as_float(0x7fc00000);
-            } else if (isinf(M)) {
-                lz = M;
-            } else {
-                double S = 0.0;
-                for (int q = 0; q < chunks; ++q) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(DDT_FULL_MASK, M, o));
+            nan_row = __any_sync(DDT_FULL_MASK, nan_row);
+            double S = 0.0;
+            if (!nan_row && !isinf(M)) {
+                for (int q = lane_b; q < chunks; q += 32) {
                     const float mq = __ldcg(part_m + d * chunks + q);
                     const double sq = __ldcg(part_s + d * chunks + q);
                     if (mq != -INFINITY) S += sq * exp((double)mq - (double)M);
                 }
-                lz = (float)((double)M + log(S));
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) S += __shfl_xor_sync(DDT_FULL_MASK, S, o);
             }
-            s_logz = lz;
-            if (!isfinite(lz)) atomicOr(&done_cnt[1], DDT_INFO_NONFINITE);
+            if (lane_b == 0) {
+                float lz;
+                if (nan_row)
+                    lz = __int_as_float(0x7fc00000);
+                else if (isinf(M))
+                    lz = M;
+                else
+                    lz = (float)((double)M + log(S));
+                s_logz = lz;
+                if (!isfinite(lz)) atomicOr(&done_cnt[1], DDT_INFO_NONFINITE);
+            }
         }
         __syncthreads();
         const float lz = s_logz;
@@ -942,10 +1025,8 @@ using namespace ddt;
 using namespace ddt::tree;
 
 static size_t phase_smem(int64_t rows, int64_t chunks, int64_t topk, int64_t budget) {
-    size_t a = sizeof(uint64_t) * (kThreads + kCandCap);
-    int64_t P = 1;
-    while (P < topk) P <<= 1;
-    size_t b = sizeof(uint64_t) * (chunks * topk + P);
+    size_t a = sizeof(uint64_t) * (kThreads + kCandCap + kMaxBudget) + sizeof(float) * kMaxChunk;
+    size_t b = sizeof(uint64_t) * (2 * chunks * topk + topk);
     size_t c = expand_smem_bytes(rows, topk, budget);
     size_t m = a > b ? a : b;
     return m > c ? m : c;

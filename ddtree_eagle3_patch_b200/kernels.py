@@ -135,37 +135,50 @@ def mask_to_bits(mask2d: torch.Tensor, col_offset: int, n_rows: int, out: torch.
     return out
 
 
+_ATT_WS: dict = {}
+
+
 def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, past_length: int, visibility: torch.Tensor,
                    scale: float, out: torch.Tensor | None = None) -> torch.Tensor:
     """Kernel (2): one layer of tree-masked attention.
 
     q [n_tokens, hq, 128], k / v [hkv, kv_rows, 128] (bf16, last dim
     contiguous, any other strides), visibility [n_tokens, W] int32.
-    Returns out [n_tokens, hq, 128] bf16."""
+    Returns out [n_tokens, hq, 128] bf16.
+
+    Called once per layer, so the host work is kept to one read of each
+    tensor's shape and strides; the C entry point checks the rest."""
     for t, n in ((q, "q"), (k, "k"), (v, "v"), (visibility, "visibility")):
-        require_cuda(t, n)
+        if not isinstance(t, torch.Tensor) or not t.is_cuda:
+            require_cuda(t, n)
     if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
         raise TypeError("q, k, v must be bf16")
-    if q.stride(-1) != 1 or k.stride(-1) != 1 or v.stride(-1) != 1:
+    qs, ks = q.stride(), k.stride()
+    kshape = k.shape
+    if qs[-1] != 1 or ks[-1] != 1:
         raise ValueError("head_dim must be the contiguous dimension")
-    if k.stride() != v.stride() or k.shape != v.shape:
+    if v.stride() != ks or v.shape != kshape:
         raise ValueError("k and v must share shape and strides")
     n_tokens, hq, d = q.shape
-    hkv, kv_rows, _ = k.shape
+    hkv, kv_rows, _ = kshape
     if out is None:
         out = torch.empty((n_tokens, hq, d), dtype=torch.bfloat16, device=q.device)
-    visibility = visibility.contiguous()
+    if not visibility.is_contiguous():
+        visibility = visibility.contiguous()
+    dev_index = q.get_device()
+    key = (n_tokens, hq, hkv, int(past_length), dev_index)
+    ws = _ATT_WS.get(key)
     lib = _lib.load()
-    dev = q.device
-    ws_bytes = lib.ddt_tree_attention_workspace_size(n_tokens, hq, hkv, int(past_length),
-                                                     dev.index if dev.index is not None else 0)
-    ws = WORKSPACES.get("attention", dev, ws_bytes)
-    a = AttentionArgs(
-        q=ptr(q), q_stride_tok=q.stride(0), q_stride_head=q.stride(1), k=ptr(k), v=ptr(v),
-        kv_stride_head=k.stride(0), kv_stride_row=k.stride(1), kv_rows=kv_rows, out=ptr(out),
-        o_stride_tok=out.stride(0), o_stride_head=out.stride(1), n_tokens=n_tokens, hq=hq, hkv=hkv, head_dim=d,
-        past_length=int(past_length), visibility=ptr(visibility), vis_words=visibility.shape[1], scale=float(scale))
-    check(lib.ddt_tree_attention(ctypes.byref(a), ptr(ws), ws.numel(), stream_of(dev)), "ddt_tree_attention")
+    if ws is None or ws[0] is not WORKSPACES.current("attention", dev_index):
+        ws_bytes = lib.ddt_tree_attention_workspace_size(n_tokens, hq, hkv, int(past_length), dev_index)
+        buf = WORKSPACES.get("attention", q.device, ws_bytes)
+        ws = (buf, buf.data_ptr(), buf.numel())
+        _ATT_WS[key] = ws
+    os_ = out.stride()
+    a = AttentionArgs(q.data_ptr(), qs[0], qs[1], k.data_ptr(), v.data_ptr(), ks[0], ks[1], kv_rows, out.data_ptr(),
+                      os_[0], os_[1], n_tokens, hq, hkv, d, int(past_length), visibility.data_ptr(),
+                      visibility.shape[1], float(scale))
+    check(lib.ddt_tree_attention(ctypes.byref(a), ws[1], ws[2], _lib.raw_stream(dev_index)), "ddt_tree_attention")
     return out
 
 
