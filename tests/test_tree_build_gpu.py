@@ -188,3 +188,45 @@ def test_dropin_build_ddtree_tree_matches_reference(golden_trees):
         assert set(sub) == {"tree_build_copy", "tree_build_heap", "tree_build_visibility"}
     out = build_ddtree_tree(torch.randn(15, 100, device="cuda"), 0)
     assert out[2] == [-1] and out[4].shape == (1, 1)
+
+
+def test_candidate_overflow_rows_match_oracle():
+    """Rows built to defeat the chunk pre-filter, so each of the kernel's
+    candidate paths runs (9 chunks of 16888 at this width, 512 threads x
+    16-byte vectors; thread t of warp t // 32 holds chunk-local positions
+    with (position // 4) % 512 == t):
+    - rows 0-2: warp 15's slots at -100 and large values in thread 0's
+      slots, so the lower bound falls to -100 and most of the chunk is a
+      candidate (the radix select over the whole chunk);
+    - rows 3-6: warp 15's slots scaled down, so about 8 % of the chunk is a
+      candidate (the radix select over the candidates);
+    - rows 7-9: large values in thread 0's slots over a normal base (the
+      ranked candidates);
+    - rows 10-11: exact ties; rows 12-14: a fifth of the entries at the max."""
+    K = _kernels()
+    L, V, budget = 15, 151936, 64
+    rs = np.random.RandomState(11)
+    x = rs.randn(L, V).astype(np.float32)
+    local = np.arange(V) % 16888
+    thread = (local // 4) % 512
+    first = thread == 0
+    x[0:3] = np.where(first, 8.0 + rs.rand(3, V), np.where(thread >= 480, -100.0, x[0:3]))
+    x[3:7] = np.where(thread >= 480, 0.6 * x[3:7], x[3:7])
+    x[7:10] = np.where(first, 8.0 + rs.rand(3, V), x[7:10])
+    x[10:12] = 0.5
+    x[10:12, rs.randint(0, V, 40)] = 3.0
+    for r in range(12, 15):
+        x[r, rs.rand(V) < 0.2] = x[r].max()
+    x = x.astype(np.float32)
+    t = K.tree_build(torch.from_numpy(x).cuda(), budget)
+    g = _tree_np(t)
+    k = min(budget, V)
+    ids_g = t.top_ids[:, :k].cpu().numpy()
+    lp_g = t.top_lp[:, :k].cpu().numpy()
+    o_ids, o_vals, o_logz = O.topk_logz(x, k)
+    assert np.array_equal(ids_g, o_ids)
+    o_lp = O.log_probs(o_vals, o_logz)
+    tol = 2 * np.spacing(np.abs(o_logz))[:, None] + np.spacing(np.abs(o_lp))
+    assert np.all(np.abs(lp_g - o_lp) <= tol), np.abs(lp_g - o_lp).max()
+    o = O.tree_from_lp(lp_g, ids_g, budget)
+    _assert_tree_equal(g, o["node_token_ids"], o["node_depths"], o["parents"], o["visibility"], "overflow")
