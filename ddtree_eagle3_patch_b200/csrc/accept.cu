@@ -229,13 +229,41 @@ argmax_kernel(const T* __restrict__ logits, int64_t n_rows, int64_t vocab, int64
         // bound by memory latency otherwise), then one predicated batch for
         // the rest of this thread's whole vectors and at most one partial
         // vector; the max is order-independent
+        // A full batch first takes its float max; v * 0 turns NaN when any
+        // element is NaN or infinite, and such a batch takes the exact key
+        // path.  Otherwise the batch can only win with a larger value (this
+        // thread's earlier batches hold lower indices), and only then is the
+        // lowest index holding the max looked up.
         constexpr int U = 8;
         for (; base + (U - 1) * step + kEpv <= c1; base += U * step) {
             uint4 raw[U];
 #pragma unroll
             for (int u = 0; u < U; ++u) raw[u] = __ldcs(reinterpret_cast<const uint4*>(rowp + base + u * step));
+            float bmax = -INFINITY, inf_nan = 0.f;
 #pragma unroll
-            for (int u = 0; u < U; ++u) scan_vec(raw[u], base + u * step);
+            for (int u = 0; u < U; ++u) {
+                const T* pv = reinterpret_cast<const T*>(&raw[u]);
+#pragma unroll
+                for (int e = 0; e < kEpv; ++e) {
+                    const float v = to_f32<T>(pv[e]);
+                    bmax = fmaxf(bmax, v);
+                    inf_nan = fmaf(v, 0.f, inf_nan);
+                }
+            }
+            if (inf_nan != inf_nan) {
+#pragma unroll
+                for (int u = 0; u < U; ++u) scan_vec(raw[u], base + u * step);
+            } else if (ord_f32(bmax == 0.f ? 0.f : bmax) > (uint32_t)(best >> 32)) {
+                int64_t first = base;
+#pragma unroll
+                for (int u = U - 1; u >= 0; --u) {
+                    const T* pv = reinterpret_cast<const T*>(&raw[u]);
+#pragma unroll
+                    for (int e = kEpv - 1; e >= 0; --e)
+                        if (to_f32<T>(pv[e]) == bmax) first = base + u * step + e;
+                }
+                best = argmax_key(bmax, first);
+            }
         }
         uint4 raw[U];
 #pragma unroll

@@ -31,6 +31,10 @@ def test_argmax_matches_oracle_with_ties_and_nan(rows, V):
             x[2, 1] = float("nan")
             x[1, :] = -0.0
             x[1, 5] = 0.0                        # -0 == +0: first index wins
+        if rows > 4:
+            x[3, V // 2] = float("inf")          # +inf is the max
+            x[3, V - 1] = float("inf")
+            x[4, :] = float("-inf")              # all -inf: first index
     got = K.argmax_rows(x.cuda()).cpu().numpy()
     ref = O.argmax_rows(_bf16_bits(x))
     assert np.array_equal(got, ref)
