@@ -633,13 +633,14 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
     // scheduled as SMs free up (it waits for this grid before reading our output)
     griddep_launch_dependents();
 
-    // 512 threads x 128 registers at launch: warpgroups 2 and 3 give 88 per
-    // thread each, the two softmax warpgroups take 88 each (216: the softmax
-    // holds a whole 128-column row of S without spilling).  Each
+    // 512 threads x 128 registers at launch: warpgroup 2 (tail) gives 88 per
+    // thread, warpgroup 3 (loads and MMA issue) 104, the two softmax
+    // warpgroups take 96 each (224: a whole 128-column row of S without
+    // spilling).  Each
     // role's setmaxnreg sits in its own branch so the compiler sizes that
     // role's code to the new limit; the code after the branches is trivial.
     if (warp >= 12) {
-        asm volatile("setmaxnreg.dec.sync.aligned.u32 40;\n" ::: "memory");
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 24;\n" ::: "memory");
         if (warp == 12) {
             // The whole warp runs this branch in step, so the operand
             // descriptors are warp-uniform values; one elected lane issues
@@ -807,7 +808,7 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
             mbar_wait(&bars[bQ], 0);
         }
     } else if (warp < 8) {
-        asm volatile("setmaxnreg.inc.sync.aligned.u32 216;\n" ::: "memory");
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 224;\n" ::: "memory");
         griddep_wait();   // nothing global is read or written before the preceding kernel is done
         // ---------------------------------------------------------------- softmax of M tile A / B
         const int slot = warp >> 2;
