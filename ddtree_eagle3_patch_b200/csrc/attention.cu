@@ -1099,7 +1099,12 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
     }
 }
 
-// Merge of the split partials: one warp per row over hkv * rows_head rows.
+// Merge of the split partials: one warp per row over hkv * rows_head rows,
+// CHUNK splits per memory round trip.  The host picks the smallest CHUNK of
+// 8, 12 and 17 that covers the splits in one round trip (at most 117
+// registers, so four CTAs fit on an SM and the grid of the verify shapes is
+// one wave), or 16 per pass beyond that.
+template <int CHUNK>
 __global__ void __launch_bounds__(128)
 combine_kernel(const __nv_bfloat16* __restrict__ part_o, const float* __restrict__ part_lse, int splits, int hkv,
                int group, int n_tokens, __nv_bfloat16* out, int64_t o_stride_tok, int64_t o_stride_head) {
@@ -1111,7 +1116,7 @@ combine_kernel(const __nv_bfloat16* __restrict__ part_o, const float* __restrict
     if (row >= (int64_t)hkv * rows_head) return;
     const int g = (int)(row / rows_head), r = (int)(row % rows_head);
     const int token = r / group, head = g * group + r % group;
-    merge_row<16>(part_o, part_lse, splits, (int64_t)hkv * rows_head, (int64_t)g * rows_head + r, lane,
+    merge_row<CHUNK>(part_o, part_lse, splits, (int64_t)hkv * rows_head, (int64_t)g * rows_head + r, lane,
               out + (int64_t)token * o_stride_tok + (int64_t)head * o_stride_head);
 }
 
@@ -1310,9 +1315,12 @@ static int launch_split(const ddt_attention_args* a, const SplitPlan& sp, void* 
         cfg.gridDim = dim3((unsigned)ceil_div(rows, 4));
         cfg.blockDim = dim3(128);
         cfg.dynamicSmemBytes = 0;
-        le = cudaLaunchKernelEx(&cfg, split::combine_kernel, (const __nv_bfloat16*)q.part_o, (const float*)q.part_lse,
-                                sp.splits, (int)a->hkv, sp.group, (int)a->n_tokens, q.out, a->o_stride_tok,
-                                a->o_stride_head);
+        auto ck = sp.splits <= 8 ? split::combine_kernel<8>
+                  : sp.splits <= 12 ? split::combine_kernel<12>
+                  : sp.splits <= 17 ? split::combine_kernel<17>
+                                    : split::combine_kernel<16>;
+        le = cudaLaunchKernelEx(&cfg, ck, (const __nv_bfloat16*)q.part_o, (const float*)q.part_lse, sp.splits,
+                                (int)a->hkv, sp.group, (int)a->n_tokens, q.out, a->o_stride_tok, a->o_stride_head);
         if (le != cudaSuccess) return set_error(DDT_ECUDA, "split_combine_kernel: %s", cudaGetErrorString(le));
         rc = check_launch("split_combine_kernel");
     }
