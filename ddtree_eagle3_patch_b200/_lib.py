@@ -84,6 +84,8 @@ _SIGNATURES = {
     "ddt_tree_walk": (ctypes.c_int, [_c_p, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_p, _c_p]),
     "ddt_argmax_rows": (ctypes.c_int, [_c_p, ctypes.c_int, _c_i64, _c_i64, _c_i64, _c_p, _c_p, ctypes.c_size_t,
                                        _c_p]),
+    "ddt_tree_commit": (ctypes.c_int, [_c_p, _c_i64, _c_p, _c_i64, _c_p, _c_p, _c_i64, _c_i64, _c_p, _c_i64, _c_i64,
+                                       _c_p, _c_i64, _c_p]),
     "ddt_kv_compact": (ctypes.c_int, [_c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_p,
                                       _c_i64, _c_p]),
     "ddt_eagle3_accept": (ctypes.c_int, [_c_p, ctypes.c_int, _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_i64, _c_i64,

@@ -328,6 +328,44 @@ __global__ void __launch_bounds__(kThreads) tree_walk_kernel(const int64_t* post
 }
 
 // ---------------------------------------------------------------------------
+// commit (ddtree.py:534-548)
+// ---------------------------------------------------------------------------
+// CTA i copies hidden row accepted[i] to hidden_out row i (when i is below
+// the accepted count); CTA 0 also writes the accepted tokens and the bonus
+// token into output_ids.  The count and the bonus token are read from
+// accept_info on the device.  Writes at or past output_len and accepted
+// indices outside [0, n_rows) are skipped.
+__global__ void __launch_bounds__(kThreads)
+commit_kernel(const int64_t* __restrict__ verify_ids, int64_t n_rows, const int64_t* __restrict__ accepted,
+              int64_t max_accept, const int64_t* __restrict__ accept_info, int64_t* output_ids, int64_t output_len,
+              int64_t start, const unsigned char* __restrict__ hidden, int64_t hidden_stride, int64_t row_bytes,
+              unsigned char* hidden_out, int64_t out_stride) {
+    int64_t count = accept_info[0];
+    if (count > max_accept) count = max_accept;
+    if (count < 0) count = 0;
+    const int64_t i = blockIdx.x;
+    if (i == 0) {
+        for (int64_t t = threadIdx.x; t < count; t += kThreads) {
+            const int64_t row = accepted[t];
+            if (row >= 0 && row < n_rows && start + t < output_len) output_ids[start + t] = verify_ids[row];
+        }
+        if (threadIdx.x == 0 && start + count < output_len) output_ids[start + count] = accept_info[1];
+    }
+    if (!hidden || i >= count) return;
+    const int64_t row = accepted[i];
+    if (row < 0 || row >= n_rows) return;
+    const unsigned char* src = hidden + row * hidden_stride;
+    unsigned char* dst = hidden_out + i * out_stride;
+    const bool vec = ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst) | (uintptr_t)row_bytes) & 15) == 0;
+    if (vec) {
+        for (int64_t b = (int64_t)threadIdx.x * 16; b < row_bytes; b += (int64_t)kThreads * 16)
+            *reinterpret_cast<uint4*>(dst + b) = __ldg(reinterpret_cast<const uint4*>(src + b));
+    } else {
+        for (int64_t b = threadIdx.x; b < row_bytes; b += kThreads) dst[b] = src[b];
+    }
+}
+
+// ---------------------------------------------------------------------------
 // compaction
 // ---------------------------------------------------------------------------
 constexpr int kCompactThreads = 256;
@@ -509,6 +547,25 @@ extern "C" int ddt_eagle3_accept(const void* logits, int dtype, int64_t n_rows, 
     tail.e3_accepted = accepted;
     return launch_argmax(logits, dtype, n_rows, vocab, row_stride, posterior, workspace, workspace_bytes, kEagle3,
                          tail, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ddt_tree_commit(const int64_t* verify_ids, int64_t n_rows, const int64_t* accepted,
+                               int64_t max_accept, const int64_t* accept_info, int64_t* output_ids, int64_t output_len,
+                               int64_t start, const void* hidden, int64_t hidden_row_stride_bytes, int64_t row_bytes,
+                               void* hidden_out, int64_t out_row_stride_bytes, ddt_stream_t stream) {
+    if (!verify_ids || !accepted || !accept_info || !output_ids) return set_error(DDT_EINVAL, "null argument");
+    if (n_rows <= 0 || max_accept < 1) return set_error(DDT_EINVAL, "n_rows and max_accept must be positive");
+    if (start < 0 || output_len <= start) return set_error(DDT_EINVAL, "start %lld outside output of %lld",
+                                                          (long long)start, (long long)output_len);
+    if ((hidden == nullptr) != (hidden_out == nullptr))
+        return set_error(DDT_EINVAL, "hidden and hidden_out go together");
+    if (hidden && (row_bytes <= 0 || hidden_row_stride_bytes < row_bytes || out_row_stride_bytes < row_bytes))
+        return set_error(DDT_EINVAL, "bad hidden row layout");
+    commit_kernel<<<(unsigned)max_accept, kThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        verify_ids, n_rows, accepted, max_accept, accept_info, output_ids, output_len, start,
+        static_cast<const unsigned char*>(hidden), hidden_row_stride_bytes, hidden ? row_bytes : 0,
+        static_cast<unsigned char*>(hidden_out), out_row_stride_bytes);
+    return check_launch("commit_kernel");
 }
 
 extern "C" int ddt_kv_compact(void* const* tensors, int64_t n_tensors, int64_t heads, int64_t row_bytes,

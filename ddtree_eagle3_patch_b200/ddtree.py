@@ -179,6 +179,17 @@ def accept_verified_tree(logits: torch.Tensor, tree: kernels.DeviceTree, max_acc
     return kernels.tree_accept(logits, tree.parents, tree.node_token_ids, tree.info, max_accept=max_accept)
 
 
+def commit_verified_tree(verify_input_ids: torch.Tensor, accepted: torch.Tensor, accept_info: torch.Tensor,
+                         output_ids: torch.Tensor, start: int, hidden: torch.Tensor | None = None):
+    """The commit step of a round (ddtree.py:534-548) on the device, after
+    accept_verified_tree: the accepted verify tokens go to
+    ``output_ids[:, start:start+n]`` and the bonus token to ``start+n``; with
+    ``hidden`` ([1, N, H] verify hidden features) the accepted rows are
+    returned as [max_accept, H] (the first n are valid).  n stays on the
+    device (``accept_info[0]``), so no host sync happens here."""
+    return kernels.tree_commit(verify_input_ids, accepted, accept_info, output_ids, start, hidden)
+
+
 # ----------------------------------------------------------------------------
 # KV compaction
 # ----------------------------------------------------------------------------

@@ -295,6 +295,48 @@ class PointerTable:
 _PTRS = PointerTable()
 
 
+def tree_commit(verify_ids: torch.Tensor, accepted: torch.Tensor, accept_info: torch.Tensor,
+                output_ids: torch.Tensor, start: int, hidden: torch.Tensor | None = None,
+                hidden_out: torch.Tensor | None = None) -> torch.Tensor | None:
+    """Kernel (3c): the commit step of a round (ddtree.py:534-548) on the device.
+
+    Writes the accepted verify tokens into ``output_ids[start:start+n]`` and
+    the bonus token at ``start+n``, and, with ``hidden`` ([N, H] or [1, N, H],
+    last dim contiguous), returns the accepted rows of the hidden features in
+    ``hidden_out`` ([max_accept, H]; rows past the count are left as they
+    are).  ``n`` and the bonus token come from ``accept_info`` on the device:
+    no host sync."""
+    for t, n in ((verify_ids, "verify_ids"), (accepted, "accepted"), (accept_info, "accept_info"),
+                 (output_ids, "output_ids")):
+        require_cuda(t, n)
+    vid = verify_ids.reshape(-1)
+    if vid.dtype != torch.int64 or not vid.is_contiguous():
+        raise ValueError("verify_ids must be contiguous int64")
+    if output_ids.dtype != torch.int64 or not output_ids.is_contiguous():
+        raise ValueError("output_ids must be contiguous int64")
+    if accepted.dtype != torch.int64 or accept_info.dtype != torch.int64:
+        raise ValueError("accepted / accept_info must be int64")
+    max_accept = accepted.numel()
+    row_stride = row_bytes = out_stride = 0
+    if hidden is not None:
+        require_cuda(hidden, "hidden")
+        h = hidden.reshape(-1, hidden.shape[-1]) if hidden.dim() == 3 and hidden.shape[0] == 1 else hidden
+        if h.dim() != 2 or h.stride(-1) != 1:
+            raise ValueError("hidden must be [N, H] (or [1, N, H]) with a contiguous last dimension")
+        if hidden_out is None:
+            hidden_out = torch.empty((max_accept, h.shape[1]), dtype=h.dtype, device=h.device)
+        if hidden_out.dtype != h.dtype or hidden_out.shape[-1] != h.shape[1] or hidden_out.stride(-1) != 1:
+            raise ValueError("hidden_out must match hidden's dtype and width")
+        esz = h.element_size()
+        row_stride, row_bytes, out_stride = h.stride(0) * esz, h.shape[1] * esz, hidden_out.stride(-2) * esz
+        hidden = h
+    rc = _lib.load().ddt_tree_commit(ptr(vid), vid.numel(), ptr(accepted), max_accept, ptr(accept_info),
+                                     ptr(output_ids), output_ids.numel(), int(start), ptr(hidden), row_stride,
+                                     row_bytes, ptr(hidden_out), out_stride, stream_of(vid.device))
+    check(rc, "ddt_tree_commit")
+    return hidden_out
+
+
 def kv_compact(tensors, past_length: int, cur_len: int, keep: torch.Tensor, keep_count: torch.Tensor,
                max_keep: int, table: PointerTable | None = None) -> None:
     """In-place compaction of many [..., heads, rows, head_dim] cache tensors

@@ -183,6 +183,20 @@ DDT_API int ddt_tree_walk(const int64_t* posterior, int64_t n_rows, const int32_
 DDT_API int ddt_argmax_rows(const void* logits, int dtype, int64_t n_rows, int64_t vocab, int64_t row_stride,
                     int64_t* posterior, void* workspace, size_t workspace_bytes, ddt_stream_t stream);
 
+/* The commit step of a round (ddtree.py:534-548) on the device, after
+ * ddt_tree_accept: output_ids[start + i] = verify_ids[accepted[i]] for
+ * i < count and output_ids[start + count] = the bonus token, where count and
+ * the bonus token are accept_info[0] and accept_info[1] (read on the device,
+ * so the round needs no host sync).  When hidden is given, hidden_out row i
+ * = hidden row accepted[i] for i < count: the accepted rows of the verify
+ * hidden features (index_select(1, accepted_index_tensor)), rows of
+ * row_bytes bytes at the given strides.  Writes at or past output_len and
+ * accepted indices outside [0, n_rows) are skipped. */
+DDT_API int ddt_tree_commit(const int64_t* verify_ids, int64_t n_rows, const int64_t* accepted, int64_t max_accept,
+                            const int64_t* accept_info, int64_t* output_ids, int64_t output_len, int64_t start,
+                            const void* hidden /* nullable */, int64_t hidden_row_stride_bytes, int64_t row_bytes,
+                            void* hidden_out /* nullable */, int64_t out_row_stride_bytes, ddt_stream_t stream);
+
 /* In-place compaction of the appended window of many cache tensors in one
  * launch.  Replaces compact_dynamic_cache's per-layer loop (ddtree.py:323-369)
  * over compact_tail_inplace (ddtree.py:61-88): for every tensor t and head h,

@@ -236,6 +236,20 @@ def compact_tail(cache: np.ndarray, past_length: int, keep) -> np.ndarray:
     return out
 
 
+def commit(verify_ids, accepted, next_token: int, output_ids: np.ndarray, start: int, hidden=None):
+    """The commit step of a round (ddtree.py:534-548), on copies:
+    ``output_ids[..., start:start+n] = verify_ids[..., accepted]``, the bonus
+    token at ``start + n``, and the accepted rows of the verify hidden
+    features (``index_select(1, accepted)``)."""
+    acc = np.asarray(accepted, np.int64)
+    out = np.array(output_ids, copy=True)
+    n = len(acc)
+    out[..., start:start + n] = np.asarray(verify_ids)[..., acc]
+    out[..., start + n] = next_token
+    sel = None if hidden is None else np.asarray(hidden)[..., acc, :].copy()
+    return out, sel
+
+
 # ----------------------------------------------------------------------------
 # verify attention reference (HF sdpa path: softmax(QK^T*scale + mask) V)
 # ----------------------------------------------------------------------------

@@ -187,3 +187,43 @@ def test_workspace_reuse_across_shapes():
         x = torch.randn(rows, V).to(torch.bfloat16)
         got = K.argmax_rows(x.cuda()).cpu()
         assert torch.equal(got, torch.argmax(x.float(), dim=-1)), (rows, V)
+
+
+@pytest.mark.parametrize("width,dtype", [(5 * 2560, torch.bfloat16), (37, torch.bfloat16), (64, torch.float32)])
+def test_commit_matches_oracle(width, dtype):
+    """The commit step after a walk: tokens and bonus into output_ids, the
+    accepted hidden rows, with the count read on the device (ddtree.py:534-548)."""
+    K = _k()
+    g = torch.Generator().manual_seed(width)
+    x = torch.randn(15, 4096, generator=g)
+    x[torch.arange(15), torch.randint(0, 4096, (15,), generator=g)] += 8
+    tree = K.tree_build(x.cuda(), 32)
+    n = int(tree.info[0])
+    N = n + 1
+    ids = tree.verify_ids[:N].clone()
+    # a posterior that follows the tree for a few steps, then leaves it
+    post = np.random.RandomState(width).randint(0, 4096, N).astype(np.int64)
+    toks = tree.node_token_ids[:n].cpu().numpy()
+    par = tree.parents[: n + 1].cpu().numpy()
+    cur = 0
+    for _ in range(3):
+        kids = [i for i in range(1, n + 1) if par[i] == cur]
+        if not kids:
+            break
+        post[cur] = toks[kids[0] - 1]
+        cur = kids[0]
+    acc, info = K.tree_walk(torch.from_numpy(post).cuda(), tree.parents, tree.node_token_ids, tree.info,
+                            max_accept=N)
+    count, nxt = int(info[0]), int(info[1])
+    hidden = torch.randn(1, N, width, generator=g).to(dtype).cuda()
+    out_ids = torch.full((1, 64), -1, dtype=torch.int64, device="cuda")
+    sel = K.tree_commit(ids, acc, info, out_ids, 7, hidden)
+    o_ids, o_sel = O.commit(ids.cpu().numpy(), acc[:count].cpu().numpy(), nxt, np.full((1, 64), -1, np.int64), 7,
+                            hidden[0].float().cpu().numpy())
+    assert np.array_equal(out_ids.cpu().numpy(), o_ids)
+    assert torch.equal(sel[:count].float().cpu(), torch.from_numpy(o_sel))
+    assert count >= 2
+    # without hidden features, and with the output ending right after the tokens
+    short = torch.full((7 + count,), -5, dtype=torch.int64, device="cuda")
+    assert K.tree_commit(ids, acc, info, short, 7) is None
+    assert short[7:].cpu().tolist() == o_ids[0, 7:7 + count].tolist()   # the bonus slot is past the end
