@@ -148,8 +148,12 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, past_lengt
 
     Called once per layer, so the host work is kept to one read of each
     tensor's shape and strides; the C entry point checks the rest."""
-    for t, n in ((q, "q"), (k, "k"), (v, "v"), (visibility, "visibility")):
-        if not isinstance(t, torch.Tensor) or not t.is_cuda:
+    try:
+        on_gpu = q.is_cuda and k.is_cuda and v.is_cuda and visibility.is_cuda
+    except AttributeError:
+        on_gpu = False
+    if not on_gpu:
+        for t, n in ((q, "q"), (k, "k"), (v, "v"), (visibility, "visibility")):
             require_cuda(t, n)
     if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
         raise TypeError("q, k, v must be bf16")
@@ -166,17 +170,18 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, past_lengt
     if not visibility.is_contiguous():
         visibility = visibility.contiguous()
     dev_index = q.get_device()
-    key = (n_tokens, hq, hkv, int(past_length), dev_index)
+    past_length = int(past_length)
+    key = (n_tokens, hq, hkv, past_length, dev_index)
     ws = _ATT_WS.get(key)
     lib = _lib.load()
     if ws is None or ws[0] is not WORKSPACES.current("attention", dev_index):
-        ws_bytes = lib.ddt_tree_attention_workspace_size(n_tokens, hq, hkv, int(past_length), dev_index)
+        ws_bytes = lib.ddt_tree_attention_workspace_size(n_tokens, hq, hkv, past_length, dev_index)
         buf = WORKSPACES.get("attention", q.device, ws_bytes)
         ws = (buf, buf.data_ptr(), buf.numel())
         _ATT_WS[key] = ws
     os_ = out.stride()
     a = AttentionArgs(q.data_ptr(), qs[0], qs[1], k.data_ptr(), v.data_ptr(), ks[0], ks[1], kv_rows, out.data_ptr(),
-                      os_[0], os_[1], n_tokens, hq, hkv, d, int(past_length), visibility.data_ptr(),
+                      os_[0], os_[1], n_tokens, hq, hkv, d, past_length, visibility.data_ptr(),
                       visibility.shape[1], float(scale))
     check(lib.ddt_tree_attention(ctypes.byref(a), ws[1], ws[2], _lib.raw_stream(dev_index)), "ddt_tree_attention")
     return out
