@@ -582,13 +582,16 @@ __device__ void expand_tree(const float* lp_g, const int64_t* ids_g, int rows, i
 
     if (warp == 0) {
         int count;
-        if (budget < 32)
+        // before pop t the frontier holds at most t + 1 <= budget entries, so
+        // 32 * S >= budget slots suffice; the last pop's appended entry may
+        // fall past them and is dropped, as nothing is popped after it
+        if (budget <= 32)
             count = expand_regs<1>(e, rows, topk, budget, lane);
-        else if (budget < 64)
+        else if (budget <= 64)
             count = expand_regs<2>(e, rows, topk, budget, lane);
-        else if (budget < 96)
+        else if (budget <= 96)
             count = expand_regs<3>(e, rows, topk, budget, lane);
-        else if (budget < 128)
+        else if (budget <= 128)
             count = expand_regs<4>(e, rows, topk, budget, lane);
         else
             count = expand_smem(e, rows, topk, budget, lane);

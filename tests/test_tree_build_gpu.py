@@ -130,6 +130,34 @@ def test_shapes_and_budgets(L, V, budget):
     _assert_tree_equal(gt, o2["node_token_ids"], o2["node_depths"], o2["parents"], o2["visibility"], (L, V, budget))
 
 
+def _frontier_before_last_pop(o, rows, topk):
+    """Frontier size when the last node is popped: each popped node adds its
+    next sibling (rank + 1 < topk) and its first child (depth < rows) and
+    leaves itself."""
+    f = 1
+    for d, r in zip(o["node_depths"][:-1], o["node_ranks"][:-1]):
+        f += int(r + 1 < topk) + int(d < rows) - 1
+    return f
+
+
+@pytest.mark.parametrize("budget", [32, 64, 96, 128])
+def test_register_frontier_full_at_last_pop(budget):
+    """Flat draft logits make a broad tree in which every pop but the last
+    grows the frontier by one, so the frontier holds exactly ``budget`` entries
+    (every register slot) when the last node is popped."""
+    K = _kernels()
+    L, V = 32, 4096
+    g = torch.Generator().manual_seed(7 + budget)
+    x = torch.randn(L, V, generator=g) * 0.05
+    t = K.tree_build(x.cuda(), budget)
+    o = O.build_tree(x.numpy(), budget)
+    assert _frontier_before_last_pop(o, L, min(budget, V)) == budget
+    assert np.array_equal(t.top_ids[:, :budget].cpu().numpy(), o["ids"])
+    o2 = O.tree_from_lp(t.top_lp[:, :budget].cpu().numpy(), o["ids"], budget)
+    _assert_tree_equal(_tree_np(t), o2["node_token_ids"], o2["node_depths"], o2["parents"], o2["visibility"],
+                       budget)
+
+
 def test_value_ties_break_by_lowest_token_id():
     K = _kernels()
     x = torch.zeros(3, 5000)
