@@ -41,6 +41,8 @@ sys.path.insert(0, str(ROOT))
 LAYERS, HQ, HKV, HD = 36, 32, 8, 128
 ROWS, VOCAB, BUDGET, PAST = 15, 151936, 64, 4096
 N_VERIFY = BUDGET + 1
+QUERY_CHUNK = 9   # layers of queries per host-to-device copy in the e2e leg
+E2E_MIN_STEPS = 300
 METRIC = "tree build+verify steps/s (DDTree hot-path step, Qwen3-4B shape, B=1)"
 UNIT = "steps/s"
 WORKLOAD = (f"tree build [{ROWS}x{VOCAB}] fp32 budget {BUDGET} + tree-verify attention {LAYERS} layers "
@@ -290,18 +292,23 @@ def run_e2e(args, w: Workload, device, stream, tree_out, table, world, dist):
     """Per step: pinned host draft logits, per-layer queries and new tree K/V
     rows, and verify logits are copied in; the accept result is copied out.
     The copies run on a copy stream in the order the step needs them: draft
-    logits, the new K rows of every layer and head in one 2D copy (the cache
-    is one [layers, heads, rows, dim] allocation), the same for V, each
-    layer's queries, then the verify logits.  The compute stream waits on an
-    event just before each use, so the host-to-device traffic overlaps the
-    kernels (a step still contains all of its own copies: the next step
-    starts after this one's result is back on the host)."""
+    logits, the new K and V rows of every layer and head in one contiguous
+    copy to a staging buffer (the compute stream scatters them into the
+    cache rows), the queries in chunks of QUERY_CHUNK layers, then the
+    verify logits.  The compute stream waits on an event just before each
+    use, so the host-to-device traffic overlaps the kernels (a step still
+    contains all of its own copies: the next step starts after this one's
+    result is back on the host).  Few, large copies keep the copy engine at
+    its bandwidth: a 2D copy of the 288 strided (layer, head) rows cost
+    ~1.5 us per row and 36 per-layer query copies ~5 us each on B200."""
     from ddtree_eagle3_patch_b200 import kernels
     h_draft = [t.cpu().pin_memory() for t in w.draft]
     h_verify = [t.cpu().pin_memory() for t in w.verify]
     h_q = torch.stack([q.cpu() for q in w.qs]).pin_memory()
-    h_kt = torch.stack([k[:, PAST:].cpu() for k in w.ks]).pin_memory()
-    h_vt = torch.stack([v[:, PAST:].cpu() for v in w.vs]).pin_memory()
+    # [2, layers, heads, tree rows, dim]: new K rows, then new V rows
+    h_kvt = torch.stack([torch.stack([t[:, PAST:].cpu() for t in w.ks]),
+                         torch.stack([t[:, PAST:].cpu() for t in w.vs])]).pin_memory()
+    d_kvt = torch.empty(h_kvt.shape, dtype=torch.bfloat16, device=device)
     d_draft = torch.empty_like(w.draft[0])
     d_verify = torch.empty_like(w.verify[0])
     d_q = torch.empty((LAYERS, N_VERIFY, HQ, HD), dtype=torch.bfloat16, device=device)
@@ -309,40 +316,33 @@ def run_e2e(args, w: Workload, device, stream, tree_out, table, world, dist):
     acc_bufs = (torch.zeros(ROWS + 1, dtype=torch.int64, device=device),
                 torch.zeros(2, dtype=torch.int64, device=device),
                 torch.empty(N_VERIFY, dtype=torch.int64, device=device))
-    h2d = (h_draft[0].numel() * 4 + h_verify[0].numel() * 2 + h_q.numel() * 2 + h_kt.numel() * 2 + h_vt.numel() * 2)
+    h2d = h_draft[0].numel() * 4 + h_verify[0].numel() * 2 + h_q.numel() * 2 + h_kvt.numel() * 2
     d2h = h_result.numel() * 8
-    from cuda.bindings import runtime as cudart
-    h2d_kind = cudart.cudaMemcpyKind.cudaMemcpyHostToDevice
-    row_bytes = N_VERIFY * HD * 2
     copy_stream = torch.cuda.Stream(device)
     ev_draft, ev_kv, ev_verify = torch.cuda.Event(), torch.cuda.Event(), torch.cuda.Event()
-    ev_layer = [torch.cuda.Event() for _ in range(LAYERS)]
-    # (layer, head) rows of the cache are uniformly strided: one 2D copy per tensor kind
-    kv_rows = LAYERS * HKV
-    kv_pitch = w.k_all.stride(1) * 2
-    assert w.k_all.stride(0) == HKV * w.k_all.stride(1) and w.v_all.stride() == w.k_all.stride()
+    chunks = [(c, min(c + QUERY_CHUNK, LAYERS)) for c in range(0, LAYERS, QUERY_CHUNK)]
+    ev_chunk = [torch.cuda.Event() for _ in chunks]
 
     def step(i):
         with torch.cuda.stream(copy_stream):
             d_draft.copy_(h_draft[i % 2], non_blocking=True)
             ev_draft.record(copy_stream)
-            for src, dst in ((h_kt, w.k_all), (h_vt, w.v_all)):
-                err, = cudart.cudaMemcpy2DAsync(dst[:, :, PAST:].data_ptr(), kv_pitch, src.data_ptr(), row_bytes,
-                                                row_bytes, kv_rows, h2d_kind, copy_stream.cuda_stream)
-                if err != cudart.cudaError_t.cudaSuccess:
-                    raise RuntimeError(f"cudaMemcpy2DAsync: {err}")
+            d_kvt.copy_(h_kvt, non_blocking=True)
             ev_kv.record(copy_stream)
-            for layer in range(LAYERS):
-                d_q[layer].copy_(h_q[layer], non_blocking=True)
-                ev_layer[layer].record(copy_stream)
+            for (c0, c1), ev in zip(chunks, ev_chunk):
+                d_q[c0:c1].copy_(h_q[c0:c1], non_blocking=True)
+                ev.record(copy_stream)
             d_verify.copy_(h_verify[i % 2], non_blocking=True)
             ev_verify.record(copy_stream)
         with torch.cuda.stream(stream):
             stream.wait_event(ev_draft)
             tree = kernels.tree_build(d_draft, BUDGET, out=tree_out)
             stream.wait_event(ev_kv)
+            w.k_all[:, :, PAST:PAST + N_VERIFY].copy_(d_kvt[0])
+            w.v_all[:, :, PAST:PAST + N_VERIFY].copy_(d_kvt[1])
             for layer in range(LAYERS):
-                stream.wait_event(ev_layer[layer])
+                if layer % QUERY_CHUNK == 0:
+                    stream.wait_event(ev_chunk[layer // QUERY_CHUNK])
                 kernels.tree_attention(d_q[layer], w.ks[layer], w.vs[layer], PAST, tree.visibility, w.scale,
                                        out=w.outs[layer])
             stream.wait_event(ev_verify)
@@ -362,8 +362,11 @@ def run_e2e(args, w: Workload, device, stream, tree_out, table, world, dist):
         dist.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # at least E2E_MIN_STEPS steps (~0.35 s): each step waits on the host, so
+    # a short run is dominated by host scheduling noise
+    n_steps = max(args.steps, E2E_MIN_STEPS)
     e0.record(stream)
-    for i in range(args.steps):
+    for i in range(n_steps):
         step(i)
     e1.record(stream)
     torch.cuda.synchronize()
@@ -371,9 +374,10 @@ def run_e2e(args, w: Workload, device, stream, tree_out, table, world, dist):
     if world > 1:
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
     el = float(ms.item())
-    return {"value": round(world * args.steps / (el / 1e3), 2), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
-            "d2h_bytes_per_step": int(d2h), "ms_per_step": round(el / args.steps, 4),
-            "api": "ddtree_eagle3_patch_b200.kernels (C-ABI via ctypes), eager launches, copies on a copy stream"}
+    return {"value": round(world * n_steps / (el / 1e3), 2), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(d2h), "ms_per_step": round(el / n_steps, 4), "steps": n_steps,
+            "api": "ddtree_eagle3_patch_b200.kernels (C-ABI via ctypes), eager launches, copies on a copy stream",
+            "copies_per_step": 4 + len(chunks)}
 
 
 def _attention_splits() -> int:
