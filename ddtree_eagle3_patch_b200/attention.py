@@ -11,6 +11,14 @@ ancestor bitmask of its last ``q_len`` columns (the prefix before them must
 be fully visible, as in the reference's masks).  Causal prefill / decode
 calls (no mask) use the causal bitmask.
 
+Sliding-window layers of hybrid models (the attention function gets
+``sliding_window`` and the reference's ``sliding_attention`` mask,
+ddtree.py:258-287) run ``ddt_tree_attention_window``: each row's first
+visible prefix key comes from the mask (``ddtree_key_lo`` attached by
+``ddtree.compile_ddtree_tree``, else counted from the mask's prefix
+columns, which must hide a leading block of keys per row), or from the row's
+position for causal calls.
+
 Register with ``register()`` and load the target with
 ``attn_implementation="ddtree_b200"``.
 """
@@ -26,11 +34,17 @@ _bits_cache: dict = {}
 _causal_cache: dict = {}
 
 
-def causal_bits(n: int, device: torch.device) -> torch.Tensor:
-    key = (n, device)
+def causal_bits(n: int, device: torch.device, window: int | None = None) -> torch.Tensor:
+    """Packed causal mask of n new rows; with a sliding window shorter than
+    n, row t sees only rows t - window + 1 .. t of them."""
+    if window is not None and window >= n:
+        window = None
+    key = (n, device, window)
     b = _causal_cache.get(key)
     if b is None:
         vis = torch.ones((n, n), dtype=torch.bool, device=device).tril_()
+        if window is not None:
+            vis &= ~torch.ones((n, n), dtype=torch.bool, device=device).tril_(-int(window))
         b = kernels.mask_to_bits(vis, 0, n)
         _causal_cache[key] = b
     return b
@@ -54,26 +68,52 @@ def _mask_bits(mask: torch.Tensor, q_len: int, kv_len: int):
     return bits, past
 
 
+def _mask_key_lo(mask: torch.Tensor, q_len: int, kv_len: int) -> torch.Tensor:
+    """First visible prefix key of each row of a sliding-window mask."""
+    past = kv_len - q_len
+    lo = getattr(mask, "ddtree_key_lo", None)
+    if lo is not None and lo.shape[0] == q_len and getattr(mask, "ddtree_past", None) == past:
+        return lo
+    key = (mask.data_ptr(), tuple(mask.shape), mask.stride(), mask._version, q_len, kv_len)
+    hit = _bits_cache.get("last_key_lo")
+    if hit is not None and hit[0] == key:
+        return hit[1]
+    m2 = mask.reshape(-1, mask.shape[-2], mask.shape[-1])[0][:q_len, :past]
+    visible = m2 if m2.dtype == torch.bool else m2 > torch.finfo(m2.dtype).min / 2
+    lo = (~visible).sum(dim=1, dtype=torch.int64)
+    leading = torch.arange(past, device=m2.device).unsqueeze(0) >= lo.unsqueeze(1)
+    if not torch.equal(visible, leading):
+        raise ValueError("sliding-window mask: each row must hide a leading block of prefix keys")
+    _bits_cache["last_key_lo"] = (key, lo)
+    return lo
+
+
 def tree_verify_attention(module, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
                           attention_mask: torch.Tensor | None, dropout: float = 0.0, scaling: float | None = None,
                           is_causal: bool | None = None, **kwargs):
     """query [1, Hq, T, D], key / value [1, Hkv, S, D] -> ([1, T, Hq, D], None)."""
     if query.shape[0] != 1:
         raise NotImplementedError("the tree-verify attention runs batch 1 (as the reference does)")
-    if kwargs.get("sliding_window") is not None:
-        raise NotImplementedError("sliding-window layers are not supported by the tree-verify kernel")
+    window = kwargs.get("sliding_window")
     if dropout and module.training:
         raise NotImplementedError("dropout is not supported")
     _, hq, T, d = query.shape
     S = key.shape[-2]
     scale = float(scaling) if scaling is not None else d ** -0.5
     if attention_mask is None:
-        bits, past = causal_bits(T, query.device), S - T
+        bits, past = causal_bits(T, query.device, window), S - T
     else:
         bits, past = _mask_bits(attention_mask, T, S)
+    key_lo = None
+    if window is not None:
+        if attention_mask is None:   # causal: row t sits at position past + t
+            key_lo = torch.arange(past - int(window) + 1, past - int(window) + 1 + T, dtype=torch.int64,
+                                  device=query.device)
+        else:
+            key_lo = _mask_key_lo(attention_mask, T, S)
     q = query[0].transpose(0, 1)            # [T, Hq, D]
     out = torch.empty((1, T, hq, d), dtype=query.dtype, device=query.device)
-    kernels.tree_attention(q, key[0], value[0], past, bits, scale, out=out[0])
+    kernels.tree_attention(q, key[0], value[0], past, bits, scale, out=out[0], key_lo=key_lo)
     return out, None
 
 

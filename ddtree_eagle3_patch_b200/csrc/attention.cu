@@ -55,6 +55,7 @@ struct Params {
     float* part_o;
     float* part_lse;
     int* status;
+    const int64_t* key_lo;   // sliding window: first visible prefix key per token, or null
 };
 
 // Visibility of keys u0 .. u0+31 relative to the tree start for one row:
@@ -79,6 +80,26 @@ __device__ __forceinline__ uint32_t vis_bits(const uint32_t* row, int W, int u0,
         if (left < 32) tree &= (1u << left) - 1u;
     }
     return prefix | tree;
+}
+
+// First visible prefix key of a row under a sliding window, clamped to
+// [0, past]: prefix keys before it are hidden (the reference's
+// sliding_attention mask, ddtree.py:276-283).  Without a window, 0.
+__device__ __forceinline__ int row_key_lo(const int64_t* key_lo, int token, bool row_valid, int past) {
+    if (!key_lo || !row_valid) return 0;
+    const int64_t lo = __ldg(key_lo + token);
+    return lo <= 0 ? 0 : (lo >= past ? past : (int)lo);
+}
+
+// Window mask of keys k0 .. k0+31: bit c is clear for a prefix key
+// (k0 + c < past) before `lo`; every other key keeps its bit.
+__device__ __forceinline__ uint32_t window_bits(int k0, int lo, int past) {
+    const int d = lo - k0;
+    uint32_t w = d <= 0 ? 0xffffffffu : (d >= 32 ? 0u : (0xffffffffu << d));
+    const int t = past - k0;
+    if (t <= 0) return 0xffffffffu;
+    if (t < 32) w |= 0xffffffffu << t;
+    return w;
 }
 
 __device__ __forceinline__ void flag_error(int* status, int code) {
@@ -211,6 +232,7 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
         const int head = g * p.group + hl;
         const bool valid = token < p.n_tokens;
         const uint32_t* vrow = valid ? p.vis + (int64_t)token * p.vis_words : p.vis;
+        const int lo = row_key_lo(p.key_lo, token, valid, p.past);
         float m_ref = -INFINITY, l = 0.f;
         bool ok = true;
         for (int jj = 0; jj < nj && ok; ++jj) {
@@ -228,7 +250,8 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
             float mx = -INFINITY;
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                const uint32_t vb = vis_bits(vrow, p.vis_words, u_base + q * 32, p.n_tokens, valid);
+                uint32_t vb = vis_bits(vrow, p.vis_words, u_base + q * 32, p.n_tokens, valid);
+                if (lo > 0) vb &= window_bits(p.past + u_base + q * 32, lo, p.past);
 #pragma unroll
                 for (int c = 0; c < 32; ++c) {
                     float s = __uint_as_float(sr[q][c]) * p.scale_log2;
@@ -238,10 +261,14 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
                 }
             }
             const float m_new = fmaxf(m_ref, mx);
+            // the O rescale reads and writes TMEM with warp-collective
+            // tcgen05.ld / st, so the warp takes it together when any of its
+            // rows needs it; the other rows scale by exactly 1
+            const bool grow = jj > 0 && m_new > m_ref + 8.0f;
             if (jj == 0) {
                 m_ref = m_new;
-            } else if (m_new > m_ref + 8.0f) {
-                const float alpha = exp2f(m_ref - m_new);
+            } else if (__any_sync(__activemask(), grow)) {
+                const float alpha = grow ? exp2f(m_ref - m_new) : 1.f;
                 if (!mbar_wait(&pv_done[(jj - 1) & 1], ((jj - 1) >> 1) & 1)) {
                     ok = false;
                     break;
@@ -257,8 +284,10 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
                     tmem_st32(tmem + lane_addr + 256 + q * 32, o);
                 }
                 tmem_wait_st();
-                l *= alpha;
-                m_ref = m_new;
+                if (grow) {
+                    l *= alpha;
+                    m_ref = m_new;
+                }
             }
             const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
             uint32_t pk[2][32];
@@ -425,6 +454,7 @@ struct Params {
     __nv_bfloat16* part_o;
     float* part_lse;
     int* status;
+    const int64_t* key_lo;   // sliding window: first visible prefix key per token, or null
 };
 
 // Barriers; each completes exactly once per CTA.
@@ -591,6 +621,10 @@ __device__ __forceinline__ void tile_epilogue(const Params& p, uint32_t o_col, u
     }
 }
 
+// kWindow: sliding-window layer (p.key_lo set).  A separate instance, so the
+// ordinary layers' code, the transposed tail's above all, carries no window
+// test.
+template <bool kWindow>
 __global__ void __launch_bounds__(kThreads, 1)
 tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tqt,
                        const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
@@ -826,6 +860,7 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
         bool ok = true;
         if (has) {
             const uint32_t* vrow = valid ? p.vis + (int64_t)token * p.vis_words : p.vis;
+            const int lo = kWindow ? row_key_lo(p.key_lo, token, valid, p.past) : 0;
             const float sl2 = p.scale_log2;
             for (int j = 0; j < nj; ++j) {
                 const uint32_t s_col =
@@ -833,7 +868,9 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
                 ok = ok && mbar_wait(&bars[bS0 + 2 * slot + j], 0);
                 tc_fence_after();
                 const int u0 = (kt0 + j) * BN - p.past;
-                const bool masked = u0 + BN > 0;
+                // tiles reaching into the tree, and under a sliding window the
+                // tiles holding prefix keys before this row's first visible one
+                const bool masked = u0 + BN > 0 || (kWindow && u0 + p.past < lo);
                 uint32_t r[4][32];
                 uint32_t vb[4];
                 if (ok) {
@@ -841,7 +878,10 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
                     for (int q = 0; q < 4; ++q) tmem_ld32(s_col + q * 32, r[q]);
 #pragma unroll
                     for (int q = 0; q < 4; ++q)
-                        vb[q] = masked ? vis_bits(vrow, p.vis_words, u0 + q * 32, p.n_tokens, valid) : 0xffffffffu;
+                        vb[q] = !masked ? 0xffffffffu
+                                : kWindow ? vis_bits(vrow, p.vis_words, u0 + q * 32, p.n_tokens, valid) &
+                                                window_bits(p.past + u0 + q * 32, lo, p.past)
+                                          : vis_bits(vrow, p.vis_words, u0 + q * 32, p.n_tokens, valid);
                     tmem_wait_ld();
                 }
                 if (hasT && slot == 0 && j == 1) {   // S(A,1)'s TMEM block may now take the tail's P.V
@@ -871,11 +911,15 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
                 const float mx = fmaxf(fmaxf(fmaxf(mk[0], mk[1]), fmaxf(mk[2], mk[3])),
                                        fmaxf(fmaxf(mk[4], mk[5]), fmaxf(mk[6], mk[7])));
                 const float m_new = fmaxf(m_ref, mx * sl2);
+                // rare: a row's running max grew by more than 2^8; O is
+                // rescaled once P.V of tile 0 is done.  tcgen05.ld / st are
+                // warp-collective, so the warp takes the rescale together when
+                // any of its rows needs it; the other rows scale by exactly 1
+                const bool grow = j > 0 && m_new > m_ref + 8.0f;
                 if (j == 0) {
                     m_ref = m_new;
-                } else if (m_new > m_ref + 8.0f) {
-                    // rare: the running max grew by more than 2^8; rescale O once P.V of tile 0 is done
-                    const float alpha = ex2_approx(m_ref - m_new);
+                } else if (__any_sync(__activemask(), grow)) {
+                    const float alpha = grow ? ex2_approx(m_ref - m_new) : 1.f;
                     ok = mbar_wait(&bars[bPV0 + 2 * slot], 0);
                     if (!ok) break;
                     tc_fence_after();
@@ -890,8 +934,10 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
                     }
                     tmem_wait_st();
                     tc_fence_before();
-                    l *= alpha;
-                    m_ref = m_new;
+                    if (grow) {
+                        l *= alpha;
+                        m_ref = m_new;
+                    }
                 }
                 const float neg_m = m_ref == -INFINITY ? 0.f : -m_ref;
                 ok = mbar_wait(&bars[free_bar(slot, j)], 0);
@@ -986,7 +1032,7 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
                     if (r < nt && ok) {
                         const int token = p.tail_token0 + r / p.group;
                         if (u < 0)
-                            vis = true;
+                            vis = !kWindow || (int64_t)(u + p.past) >= __ldg(p.key_lo + token);
                         else if (u < p.n_tokens)
                             vis = (__ldg(p.vis + (int64_t)token * p.vis_words + (u >> 5)) >> (u & 31)) & 1u;
                     }
@@ -1233,8 +1279,8 @@ using namespace ddt;
 using namespace ddt::attn;
 
 // Launch of the split kernel (and, with several key splits, the merge).
-static int launch_split(const ddt_attention_args* a, const SplitPlan& sp, void* workspace, size_t workspace_bytes,
-                        ddt_stream_t stream) {
+static int launch_split(const ddt_attention_args* a, const int64_t* key_lo, const SplitPlan& sp, void* workspace,
+                        size_t workspace_bytes, ddt_stream_t stream) {
     if (!workspace || workspace_bytes < sp.ws_bytes || reinterpret_cast<uintptr_t>(workspace) % 256)
         return set_error(DDT_EWORKSPACE, "attention workspace needs %zu bytes (256-aligned), got %zu", sp.ws_bytes,
                          workspace_bytes);
@@ -1256,8 +1302,11 @@ static int launch_split(const ddt_attention_args* a, const SplitPlan& sp, void* 
     static std::once_flag once;
     static cudaError_t attr_err = cudaSuccess;
     std::call_once(once, [] {
-        attr_err = cudaFuncSetAttribute(split::tree_attn_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)split::kSmemBytes);
+        attr_err = cudaFuncSetAttribute(split::tree_attn_split_kernel<false>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)split::kSmemBytes);
+        if (attr_err == cudaSuccess)
+            attr_err = cudaFuncSetAttribute(split::tree_attn_split_kernel<true>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)split::kSmemBytes);
     });
     if (attr_err != cudaSuccess) return set_error(DDT_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(attr_err));
     unsigned char* ws = static_cast<unsigned char*>(workspace);
@@ -1276,6 +1325,7 @@ static int launch_split(const ddt_attention_args* a, const SplitPlan& sp, void* 
     q.tail_rows = sp.tail_rows;
     q.tail_token0 = sp.tail_token0;
     q.vis = a->visibility;
+    q.key_lo = key_lo;
     q.vis_words = (int)a->vis_words;
     q.scale_log2 = a->scale * 1.4426950408889634f;
     q.out = static_cast<__nv_bfloat16*>(a->out);
@@ -1306,7 +1356,8 @@ static int launch_split(const ddt_attention_args* a, const SplitPlan& sp, void* 
     cfg.stream = st;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t le = cudaLaunchKernelEx(&cfg, split::tree_attn_split_kernel, tq, tqt, tk, tv, q);
+    cudaError_t le = key_lo ? cudaLaunchKernelEx(&cfg, split::tree_attn_split_kernel<true>, tq, tqt, tk, tv, q)
+                            : cudaLaunchKernelEx(&cfg, split::tree_attn_split_kernel<false>, tq, tqt, tk, tv, q);
     if (le != cudaSuccess) return set_error(DDT_ECUDA, "tree_attn_split_kernel: %s", cudaGetErrorString(le));
     rc = check_launch("tree_attn_split_kernel");
     if (rc) return rc;
@@ -1336,8 +1387,8 @@ extern "C" size_t ddt_tree_attention_workspace_size(int64_t n_tokens, int64_t hq
     return sp.usable && sp.ws_bytes > a ? sp.ws_bytes : a;
 }
 
-extern "C" int ddt_tree_attention(const ddt_attention_args* a, void* workspace, size_t workspace_bytes,
-                                  ddt_stream_t stream) {
+static int tree_attention_impl(const ddt_attention_args* a, const int64_t* key_lo, void* workspace,
+                               size_t workspace_bytes, ddt_stream_t stream) {
     if (!a) return set_error(DDT_EINVAL, "args is null");
     if (!a->q || !a->k || !a->v || !a->out || !a->visibility) return set_error(DDT_EINVAL, "null tensor pointer");
     if (a->head_dim != HD) return set_error(DDT_EUNSUPPORTED, "head_dim %lld (only 128)", (long long)a->head_dim);
@@ -1364,7 +1415,7 @@ extern "C" int ddt_tree_attention(const ddt_attention_args* a, void* workspace, 
         return set_error(DDT_EWORKSPACE, "attention workspace needs %zu bytes (256-aligned), got %zu", pl.ws_bytes,
                          workspace_bytes);
     const SplitPlan sp = plan_split(a->n_tokens, a->hq, a->hkv, a->past_length, ddt_sm_count(dev));
-    if (sp.usable) return launch_split(a, sp, workspace, workspace_bytes, stream);
+    if (sp.usable) return launch_split(a, key_lo, sp, workspace, workspace_bytes, stream);
     CUtensorMap tq, tk, tv;
     int rc = make_map(&tq, a->q, HD, a->hq, a->n_tokens, a->q_stride_head * 2, a->q_stride_tok * 2, 64,
                       (uint32_t)group, (uint32_t)pl.tpt);
@@ -1391,6 +1442,7 @@ extern "C" int ddt_tree_attention(const ddt_attention_args* a, void* workspace, 
     p.n_kt = pl.n_kt;
     p.splits = pl.splits;
     p.vis = a->visibility;
+    p.key_lo = key_lo;
     p.vis_words = (int)a->vis_words;
     p.scale_log2 = a->scale * 1.4426950408889634f;
     p.out = static_cast<__nv_bfloat16*>(a->out);
@@ -1419,4 +1471,16 @@ extern "C" int ddt_tree_attention(const ddt_attention_args* a, void* workspace, 
         rc = check_launch("attn_combine_kernel");
     }
     return rc;
+}
+
+extern "C" int ddt_tree_attention(const ddt_attention_args* a, void* workspace, size_t workspace_bytes,
+                                  ddt_stream_t stream) {
+    return tree_attention_impl(a, nullptr, workspace, workspace_bytes, stream);
+}
+
+extern "C" int ddt_tree_attention_window(const ddt_attention_args* a, const int64_t* key_lo, void* workspace,
+                                         size_t workspace_bytes, ddt_stream_t stream) {
+    if (!key_lo) return set_error(DDT_EINVAL, "key_lo is null");
+    if (reinterpret_cast<uintptr_t>(key_lo) % alignof(int64_t)) return set_error(DDT_EINVAL, "key_lo must be 8-byte aligned");
+    return tree_attention_impl(a, key_lo, workspace, workspace_bytes, stream);
 }

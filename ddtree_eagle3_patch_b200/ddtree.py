@@ -123,13 +123,25 @@ def compile_ddtree_tree(root_token_id, start: int, node_token_ids: torch.Tensor,
     kernels.tree_mask_fill(smask, past_length, current_length, bits, 0, 0)
     past_block = sliding_attention_mask_buffer[0, 0, :current_length, :past_length]
     past_block.zero_()
+    lower = sliding_key_lo(pos[0], sliding_window)
     if past_length > 0:
-        qpos = pos[0].to(torch.long)
-        lower = qpos - sliding_window + 1
         idx = torch.arange(past_length, device=past_block.device)
         past_block.masked_fill_(idx.unsqueeze(0) < lower.unsqueeze(1), torch.finfo(dtype).min)
     sliding = sliding_attention_mask_buffer[:, :, :current_length, : past_length + current_length]
+    _attach_bits(sliding, bits, past_length)
+    try:
+        sliding.ddtree_key_lo = lower
+    except (AttributeError, RuntimeError):
+        pass
     return ids, pos, {"full_attention": full, "sliding_attention": sliding}, past_length, current_length
+
+
+def sliding_key_lo(position_ids: torch.Tensor, sliding_window: int) -> torch.Tensor:
+    """First visible prefix key of each verify row of a sliding-window layer:
+    query position - window + 1, the lower bound of the reference's
+    ``sliding_attention`` mask (ddtree.py:276-283).  int64, on the device of
+    ``position_ids``; pass it as ``key_lo`` to ``kernels.tree_attention``."""
+    return position_ids.reshape(-1).to(torch.int64) - (int(sliding_window) - 1)
 
 
 def _attach_bits(mask: torch.Tensor, bits: torch.Tensor, past_length: int) -> None:

@@ -139,12 +139,16 @@ _ATT_WS: dict = {}
 
 
 def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, past_length: int, visibility: torch.Tensor,
-                   scale: float, out: torch.Tensor | None = None) -> torch.Tensor:
+                   scale: float, out: torch.Tensor | None = None, key_lo: torch.Tensor | None = None) -> torch.Tensor:
     """Kernel (2): one layer of tree-masked attention.
 
     q [n_tokens, hq, 128], k / v [hkv, kv_rows, 128] (bf16, last dim
     contiguous, any other strides), visibility [n_tokens, W] int32.
     Returns out [n_tokens, hq, 128] bf16.
+
+    ``key_lo`` (int64 [n_tokens] on the device) makes it a sliding-window
+    layer: row t then sees prefix key j only if j >= key_lo[t]
+    (``ddt_tree_attention_window``; see ``ddtree.sliding_key_lo``).
 
     Called once per layer, so the host work is kept to one read of each
     tensor's shape and strides; the C entry point checks the rest."""
@@ -183,7 +187,13 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, past_lengt
     a = AttentionArgs(q.data_ptr(), qs[0], qs[1], k.data_ptr(), v.data_ptr(), ks[0], ks[1], kv_rows, out.data_ptr(),
                       os_[0], os_[1], n_tokens, hq, hkv, d, past_length, visibility.data_ptr(),
                       visibility.shape[1], float(scale))
-    check(lib.ddt_tree_attention(ctypes.byref(a), ws[1], ws[2], _lib.raw_stream(dev_index)), "ddt_tree_attention")
+    if key_lo is None:
+        check(lib.ddt_tree_attention(ctypes.byref(a), ws[1], ws[2], _lib.raw_stream(dev_index)), "ddt_tree_attention")
+        return out
+    if not key_lo.is_cuda or key_lo.dtype != torch.int64 or not key_lo.is_contiguous() or key_lo.numel() < n_tokens:
+        raise ValueError("key_lo must be a contiguous int64 CUDA tensor with one entry per token")
+    check(lib.ddt_tree_attention_window(ctypes.byref(a), key_lo.data_ptr(), ws[1], ws[2], _lib.raw_stream(dev_index)),
+          "ddt_tree_attention_window")
     return out
 
 

@@ -155,6 +155,16 @@ DDT_API size_t ddt_tree_attention_workspace_size(int64_t n_tokens, int64_t hq, i
 DDT_API int ddt_tree_attention(const ddt_attention_args* args, void* workspace, size_t workspace_bytes,
                        ddt_stream_t stream);
 
+/* Sliding-window layers of a hybrid model (Gemma 3/4).  Replaces the same
+ * attention call when the layer gets the reference's "sliding_attention"
+ * mask (ddtree.py:258-287): key_lo [n_tokens] int64 on the device gives
+ * each tree row its first visible prefix key, so row t sees prefix key j
+ * iff j >= key_lo[t] (the reference's query_position - window + 1; values
+ * below 0 or above past_length are clamped).  Tree keys follow `visibility`
+ * as in ddt_tree_attention.  Same workspace. */
+DDT_API int ddt_tree_attention_window(const ddt_attention_args* args, const int64_t* key_lo, void* workspace,
+                              size_t workspace_bytes, ddt_stream_t stream);
+
 /* ---------------------------------------------------------------------------
  * (3) Greedy acceptance and KV compaction.
  * ddt_tree_accept replaces sample(logits, 0) (model/utils.py:28-30) plus

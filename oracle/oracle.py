@@ -163,6 +163,12 @@ def unpack_visibility(words: np.ndarray, N: int) -> np.ndarray:
 # ----------------------------------------------------------------------------
 # compile (ddtree.py:199-256)
 # ----------------------------------------------------------------------------
+def sliding_key_lo(positions, window: int) -> np.ndarray:
+    """Lower bound of each row's visible prefix keys under a sliding window:
+    query position - window + 1 (ddtree.py:276-281)."""
+    return np.asarray(positions, np.int64) - (int(window) - 1)
+
+
 def compile_tree(root_token: int, start: int, node_token_ids, node_depths, visibility, past_length: int,
                  mask_min: float):
     """Verify ids, position ids and the dense additive mask rows [N, past+N]."""
@@ -253,10 +259,12 @@ def commit(verify_ids, accepted, next_token: int, output_ids: np.ndarray, start:
 # ----------------------------------------------------------------------------
 # verify attention reference (HF sdpa path: softmax(QK^T*scale + mask) V)
 # ----------------------------------------------------------------------------
-def tree_attention_ref(q, k, v, past_length: int, visibility, scale: float):
+def tree_attention_ref(q, k, v, past_length: int, visibility, scale: float, key_lo=None):
     """float32/float64 attention with the reference's tree mask.
 
     q: [N, Hq, D]; k, v: [Hkv, S, D] with S = past_length + N; visibility: bool [N, N].
+    key_lo (optional, [N]): the sliding-window layers' mask (ddtree.py:276-283),
+    prefix key j hidden from row t when j < key_lo[t].
     Returns [N, Hq, D] float64.
     """
     q = np.asarray(q, np.float64)
@@ -268,6 +276,8 @@ def tree_attention_ref(q, k, v, past_length: int, visibility, scale: float):
     allowed = np.ones((N, S), bool)
     allowed[:, past_length:past_length + N] = np.asarray(visibility, bool)
     allowed[:, past_length + N:] = False
+    if key_lo is not None:
+        allowed[:, :past_length] &= np.arange(past_length)[None, :] >= np.asarray(key_lo, np.int64)[:, None]
     out = np.zeros((N, Hq, D), np.float64)
     for h in range(Hq):
         kh = k[h // g]

@@ -52,6 +52,8 @@ def test_abi_version_and_validation_errors():
     a.head_dim = 128
     a.hq, a.hkv = 3, 2
     assert lib.ddt_tree_attention(ctypes.byref(a), None, 0, None) == 1   # hq % hkv
+    assert lib.ddt_tree_attention_window(ctypes.byref(a), None, None, 0, None) == 1   # key_lo is null
+    assert b"key_lo" in lib.ddt_last_error()
 
 
 def test_workspace_sizes_are_positive():

@@ -167,3 +167,22 @@ def test_fully_masked_split_rows_are_finite():
     out, ref = _run(q, k, v, past, vis, scale)
     assert np.isfinite(out).all()
     assert_close_bf16(out, ref)
+
+
+@pytest.mark.parametrize("past,n", [(4096, 65), (64, 600)])
+def test_row_max_jump_between_key_tiles(past, n):
+    """One key in a second key tile scores far above everything before it, for
+    the rows of one query head per KV group only: those rows' running max
+    grows by more than 2^8 and O is rescaled, while the other rows of the
+    same warps keep theirs (split kernel, then the unsplit kernel)."""
+    from ddtree_eagle3_patch_b200.synthetic import tree_attention_inputs
+    hq, hkv = 32, 8
+    q, k, v, vis, scale = tree_attention_inputs(seed=21 + n, past=past, n=n, hq=hq, hkv=hkv, d=128)
+    key = 150                       # key tile 1 of the first split
+    k[:, key, :] = 0.0
+    k[:, key, 0] = 16.0
+    q[:, :, 0] = 0.0
+    q[:, ::hq // hkv, 0] = 10.0     # head 0 of each group: score 160 * scale on that key
+    out, ref = _run(q, k, v, past, vis, scale)
+    assert np.isfinite(out).all()
+    assert_close_bf16(out, ref, (past, n))
