@@ -78,6 +78,10 @@ _SIGNATURES = {
     "ddt_mask_to_bits": (ctypes.c_int, [_c_p, ctypes.c_int, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_p]),
     "ddt_tree_attention_workspace_size": (ctypes.c_size_t, [_c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_int]),
     "ddt_tree_attention": (ctypes.c_int, [ctypes.POINTER(AttentionArgs), _c_p, ctypes.c_size_t, _c_p]),
+    "ddt_sample_rows_workspace_size": (ctypes.c_size_t, [ctypes.c_int64, ctypes.c_int64]),
+    "ddt_sample_rows": (ctypes.c_int, [_c_p, ctypes.c_int, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                       ctypes.c_float, ctypes.c_uint64, ctypes.c_uint64, _c_p, _c_p, ctypes.c_size_t,
+                                       _c_p]),
     "ddt_tree_attention_window": (ctypes.c_int, [ctypes.POINTER(AttentionArgs), _c_p, _c_p, ctypes.c_size_t, _c_p]),
     "ddt_tree_accept_workspace_size": (ctypes.c_size_t, [_c_i64, _c_i64]),
     "ddt_tree_accept": (ctypes.c_int, [_c_p, ctypes.c_int, _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_p,

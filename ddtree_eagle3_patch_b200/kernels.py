@@ -251,6 +251,40 @@ def tree_walk(posterior: torch.Tensor, parents: torch.Tensor, node_token_ids: to
     return accepted, accept_info
 
 
+def sample_rows(logits: torch.Tensor, temperature: float, seed: int, offset: int = 0,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """One token per row drawn from softmax(logits / temperature)
+    (``ddt_sample_rows``): int64 of shape ``logits.shape[:-1]``.  The same
+    (seed, offset) gives the same draws."""
+    require_cuda(logits, "logits")
+    shape = logits.shape
+    x = logits.reshape(-1, shape[-1])
+    if x.stride(1) != 1:
+        x = x.contiguous()
+    n_rows, vocab = x.shape
+    if out is None:
+        out = torch.empty((n_rows,), dtype=torch.int64, device=x.device)
+    lib = _lib.load()
+    ws = WORKSPACES.get("sample", x.device, lib.ddt_sample_rows_workspace_size(n_rows, vocab))
+    rc = lib.ddt_sample_rows(ptr(x), dtype_code(x.dtype), n_rows, vocab, x.stride(0), float(temperature),
+                             int(seed) & 0xFFFFFFFFFFFFFFFF, int(offset) & 0xFFFFFFFFFFFFFFFF, ptr(out), ptr(ws),
+                             ws.numel(), stream_of(x.device))
+    check(rc, "ddt_sample_rows")
+    return out.view(shape[:-1])
+
+
+def sample(logits: torch.Tensor, temperature: float = 0.0, generator: torch.Generator | None = None) -> torch.Tensor:
+    """``sample(logits, temperature)`` of model/utils.py:28-35 on the device:
+    row-wise argmax below temperature 1e-5, otherwise one draw per row from
+    softmax(logits / temperature).  The seed of a draw comes from torch's
+    CPU generator (or ``generator``), so ``torch.manual_seed`` makes runs
+    repeat, as it does for the reference's ``torch.multinomial``."""
+    if temperature < 1e-5:
+        return argmax_rows(logits)
+    seed = int(torch.randint(0, 2 ** 62, (1,), generator=generator).item())
+    return sample_rows(logits, temperature, seed)
+
+
 def argmax_rows(logits: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     require_cuda(logits, "logits")
     shape = logits.shape

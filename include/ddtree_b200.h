@@ -193,6 +193,19 @@ DDT_API int ddt_tree_walk(const int64_t* posterior, int64_t n_rows, const int32_
 DDT_API int ddt_argmax_rows(const void* logits, int dtype, int64_t n_rows, int64_t vocab, int64_t row_stride,
                     int64_t* posterior, void* workspace, size_t workspace_bytes, ddt_stream_t stream);
 
+/* Temperature sampling of each row, the temperature > 0 branch of
+ * sample(logits, temperature) (model/utils.py:31-35): one token per row drawn
+ * from softmax(logits / temperature), written to posterior [n_rows] int64.
+ * Drawn by the Gumbel-max rule with Philox4x32-10 uniforms keyed by `seed` and
+ * counted by (element, row, `offset`): the same (seed, offset) gives the same
+ * draws, and the distribution is torch.multinomial's, not its random stream.
+ * NaN logits are never drawn (a row of NaN gives 0).  The posterior feeds
+ * ddt_tree_walk.  n_rows <= 65535; vocab < 2^31. */
+DDT_API size_t ddt_sample_rows_workspace_size(int64_t n_rows, int64_t vocab);
+DDT_API int ddt_sample_rows(const void* logits, int dtype, int64_t n_rows, int64_t vocab, int64_t row_stride,
+                    float temperature, uint64_t seed, uint64_t offset, int64_t* posterior, void* workspace,
+                    size_t workspace_bytes, ddt_stream_t stream);
+
 /* The commit step of a round (ddtree.py:534-548) on the device, after
  * ddt_tree_accept: output_ids[start + i] = verify_ids[accepted[i]] for
  * i < count and output_ids[start + count] = the bonus token, where count and
