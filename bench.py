@@ -57,7 +57,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--kernel", choices=["attention", "tree_build", "expand", "accept", "compact"], default=None,
+    ap.add_argument("--kernel", choices=["attention", "tree_build", "expand", "accept", "compact", "sample"],
+                    default=None,
                     help="launch only this kernel of the step (warmup + steps times, eager) and print its "
                          "average CUDA-event time; used for small profiler captures")
     return ap.parse_args()
@@ -496,6 +497,7 @@ def run_kernel_only(args, local):
     acc, info, post = kernels.tree_accept(w.verify[0], tree.parents, tree.node_token_ids, tree.info,
                                           max_accept=ROWS + 1)
     tensors = [t for pair in zip(w.ks, w.vs) for t in pair]
+    acc_bufs_sample = torch.empty(N_VERIFY, dtype=torch.int64, device=device)
 
     def once(i):
         if args.kernel == "attention":
@@ -504,6 +506,9 @@ def run_kernel_only(args, local):
                                    out=w.outs[layer])
         elif args.kernel == "tree_build":
             kernels.tree_build(w.draft[i % 2], BUDGET, out=tree)
+        elif args.kernel == "sample":
+            # temperature 1 draw of every verify row (the accept path at temperature > 0)
+            kernels.sample_rows(w.verify[i % 2], 1.0, seed=1234, offset=i, out=acc_bufs_sample)
         elif args.kernel == "expand":
             kernels.tree_from_log_probs(lp, ids, BUDGET)
         elif args.kernel == "accept":
