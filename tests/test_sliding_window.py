@@ -56,6 +56,25 @@ def test_oracle_key_lo_equals_reference_dense_mask(golden_misc):
     assert np.allclose(got, ref, rtol=1e-12, atol=1e-12)
 
 
+def test_wrapper_bounds_from_reference_mask(golden_misc):
+    """The HF attention function's bounds, counted from the reference's own
+    sliding mask, are the clamped position - window + 1; a mask whose hidden
+    prefix keys are not a leading block is refused."""
+    from ddtree_eagle3_patch_b200.attention import _mask_key_lo
+    z = golden_misc
+    past = int(z["compile_past"])
+    mask = torch.from_numpy(z["compile_sw_sliding"]).to(torch.bfloat16)
+    N = mask.shape[-2]
+    lo = _mask_key_lo(mask, N, past + N).numpy()
+    expect = np.clip(O.sliding_key_lo(z["compile_pos"].reshape(-1), 8), 0, past)
+    assert np.array_equal(lo, expect)
+    holed = mask.clone()
+    row = int(np.argmax(expect > 1))
+    holed[0, 0, row, 0] = 0.0      # key 0 visible again, after hidden keys
+    with pytest.raises(ValueError):
+        _mask_key_lo(holed, N, past + N)
+
+
 def _inputs(past, n, hq, hkv, seed):
     from ddtree_eagle3_patch_b200.synthetic import tree_attention_inputs
     q, k, v, vis, scale = tree_attention_inputs(seed=seed, past=past, n=n, hq=hq, hkv=hkv, d=128)
