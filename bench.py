@@ -1,7 +1,21 @@
-"""Benchmark of the DDTree per-step draft-tree hot path on B200.
+"""Benchmark of DDTree decoding and its per-step draft-tree hot path on B200.
 
-One step = the device work of one DDTree decoding round outside the model
-GEMMs, at the Qwen3-4B verify shape:
+Two workloads (``--workload``):
+
+decode (default): end-to-end DDTree decoding at the Qwen3-4B shape, B=1.
+One step = one ``ddtree_generate`` call: a random-init Qwen3-4B target
+(36 layers, hidden 2560, intermediate 9728, 32/8 heads, vocab 151936, bf16)
+with a random-init 5-layer DFlash draft of the same width, block size 16,
+node budget 32, a 512-token uniform random prompt, 1024 new tokens, greedy.
+``value`` is whole-job generated tokens/s over the K calls (prefill
+included), prompts resident on the device; ``e2e`` passes the prompt from
+pinned host memory and returns ids to the host inside the timed region.
+With N GPUs every rank decodes its own prompts (the reference shards
+prompts by rank) and one NCCL all-gather of a fixed-size counter tensor
+collects tokens, rounds and times.
+
+step: one step = the device work of one DDTree decoding round outside the
+model GEMMs, at the Qwen3-4B verify shape:
   1. tree build from draft logits [15, 151936] fp32, node budget 64
      (top-k + log-normaliser + best-first expansion + ancestor bitmask);
   2. tree-masked verify attention for 36 layers: 32 query / 8 KV heads,
@@ -43,6 +57,9 @@ ROWS, VOCAB, BUDGET, PAST = 15, 151936, 64, 4096
 N_VERIFY = BUDGET + 1
 QUERY_CHUNK = 9   # layers of queries per host-to-device copy in the e2e leg
 E2E_MIN_STEPS = 300
+DEC_SHAPE, DEC_PROMPT, DEC_NEW_TOKENS, DEC_BUDGET, DEC_BLOCK, DEC_DRAFT_LAYERS = "qwen3-4b", 512, 1024, 32, 16, 5
+DEC_METRIC = "decode tok/s (Qwen3-4B shape, B=1)"
+DEC_UNIT = "tok/s"
 METRIC = "tree build+verify steps/s (DDTree hot-path step, Qwen3-4B shape, B=1)"
 UNIT = "steps/s"
 WORKLOAD = (f"tree build [{ROWS}x{VOCAB}] fp32 budget {BUDGET} + tree-verify attention {LAYERS} layers "
@@ -53,15 +70,22 @@ WORKLOAD = (f"tree build [{ROWS}x{VOCAB}] fp32 budget {BUDGET} + tree-verify att
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", choices=["decode", "step"], default="decode")
+    ap.add_argument("--steps", type=int, default=None, help="timed steps (decode: 3 calls; step: 200)")
+    ap.add_argument("--warmup", type=int, default=None, help="untimed steps (default 3 / 5)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel", choices=["attention", "tree_build", "expand", "accept", "compact", "sample"],
                     default=None,
                     help="launch only this kernel of the step (warmup + steps times, eager) and print its "
                          "average CUDA-event time; used for small profiler captures")
-    return ap.parse_args()
+    ap.add_argument("--new-tokens", type=int, default=DEC_NEW_TOKENS, help="decode: tokens per call")
+    args = ap.parse_args()
+    if args.steps is None:
+        args.steps = 3 if args.workload == "decode" and not args.kernel else 200
+    if args.warmup is None:
+        args.warmup = 3 if args.workload == "decode" and not args.kernel else 5
+    return args
 
 
 def dist_env():
@@ -557,13 +581,250 @@ def run_kernel_only(args, local):
                       "attention_status": kernels.attention_status(device)}))
 
 
+# ----------------------------------------------------------------------------
+# decode workload (end-to-end ddtree_generate)
+# ----------------------------------------------------------------------------
+def _decode_workload(new_tokens: int) -> str:
+    return (f"DDTree decode, random-init {DEC_SHAPE} target (36 layers, hidden 2560, intermediate 9728, 32/8 heads, "
+            f"vocab 151936) + {DEC_DRAFT_LAYERS}-layer DFlash draft, block {DEC_BLOCK}, budget {DEC_BUDGET}, "
+            f"prompt {DEC_PROMPT} random ids, {new_tokens} new tokens, greedy, batch 1")
+
+
+def _decode_prompts(rank: int, count: int, mask_id: int):
+    from ddtree_eagle3_patch_b200.synthetic import random_prompt
+    # rank r decodes prompts r, r + world, ... of one seeded list (benchmark.py:175)
+    return [random_prompt(DEC_PROMPT, seed=7000 + 64 * i + rank, exclude=mask_id) for i in range(count)]
+
+
+def _attention_roofline_at(device, past: int, n: int, reps: int = 20):
+    """The tree-attention op at one verify shape, 36 layers per graph replay
+    (inputs larger than L2 across the 36 layers of K/V at long prefixes)."""
+    from ddtree_eagle3_patch_b200 import kernels
+    from ddtree_eagle3_patch_b200.synthetic import random_tree
+    g = torch.Generator(device=device).manual_seed(3)
+    ks = [torch.randn((HKV, past + n, HD), generator=g, device=device).mul_(HD ** -0.5).to(torch.bfloat16)
+          for _ in range(LAYERS)]
+    vs = [torch.randn((HKV, past + n, HD), generator=g, device=device).to(torch.bfloat16) for _ in range(LAYERS)]
+    qs = [torch.randn((n, HQ, HD), generator=g, device=device).to(torch.bfloat16) for _ in range(LAYERS)]
+    outs = [torch.empty((n, HQ, HD), dtype=torch.bfloat16, device=device) for _ in range(LAYERS)]
+    _, _, vis = random_tree(n - 1, max_depth=16, seed=5)
+    bits = kernels.mask_to_bits(torch.from_numpy(np.ascontiguousarray(vis)).to(device), 0, n)
+    stream = torch.cuda.Stream(device)
+    stream.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(stream):
+        for layer in range(LAYERS):
+            kernels.tree_attention(qs[layer], ks[layer], vs[layer], past, bits, HD ** -0.5, out=outs[layer])
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for layer in range(LAYERS):
+                kernels.tree_attention(qs[layer], ks[layer], vs[layer], past, bits, HD ** -0.5, out=outs[layer])
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (reps * LAYERS)
+    alg = 2 * HKV * (past + n) * HD * 2 + 2 * n * HQ * HD * 2
+    peaks = _peaks()
+    achieved = alg / (us * 1e-6) / 1e9
+    del graph
+    return {"bound": "hbm", "kernel": f"tree attention op (split kernel + combine), prefix {past} + {n} rows",
+            "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "peak_source": peaks["source"],
+            "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4), "algorithmic_bytes": alg,
+            "us_per_launch": round(us, 3)}
+
+
+def run_decode(args, rank, world, local):
+    from ddtree_eagle3_patch_b200 import _lib, kernels
+    from ddtree_eagle3_patch_b200 import distributed as D
+    from ddtree_eagle3_patch_b200.ddtree import ddtree_generate
+    from ddtree_eagle3_patch_b200.synthetic import build_decode_models
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    dist = init_dist(world, "nccl")
+    t_build = time.perf_counter()
+    target, draft = build_decode_models(DEC_SHAPE, device, torch.bfloat16, seed=0, draft_layers=DEC_DRAFT_LAYERS,
+                                        block_size=DEC_BLOCK)
+    t_build = time.perf_counter() - t_build
+    mask_id = draft.mask_token_id
+    n_prompts = args.warmup + 2 * args.steps
+    host_prompts = [p.pin_memory() for p in _decode_prompts(rank, n_prompts, mask_id)]
+    dev_prompts = [p.to(device) for p in host_prompts]
+    lib = _lib.load()
+
+    def gen(ids):
+        return ddtree_generate(draft, target, ids, mask_token_id=mask_id, max_new_tokens=args.new_tokens,
+                               block_size=DEC_BLOCK, stop_token_ids=None, temperature=0.0, tree_budget=DEC_BUDGET)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for i in range(args.warmup):
+        gen(dev_prompts[i])
+    barrier()
+    # timed region: K calls, prompts resident on the device
+    launches0 = lib.ddt_launch_count()
+    with ClockSampler(_physical_index(local)) as clocks:
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        results = [gen(dev_prompts[args.warmup + i]) for i in range(args.steps)]
+        e1.record()
+        barrier()
+    launches = lib.ddt_launch_count() - launches0
+    clock = clocks.summary()
+    elapsed_s = e0.elapsed_time(e1) / 1e3
+    tokens = sum(r.num_output_tokens for r in results)
+    rounds = sum(r.decode_rounds for r in results)
+    decode_s = sum(r.time_per_output_token * r.num_output_tokens for r in results)
+    stage = {k: sum(r.stage_times[k] for r in results) for k in ("draft", "tree_build", "tree_compile", "verify",
+                                                                  "commit")}
+    # the round's counters, one NCCL all-gather of a fixed-size vector
+    counters = D.gather_counters([elapsed_s, tokens, rounds, decode_s, sum(r.time_to_first_token for r in results)],
+                                 device=device)
+    wall = float(counters[:, 0].max())
+    total_tokens = float(counters[:, 1].sum())
+    value = total_tokens / wall
+
+    # e2e: prompt from pinned host memory, ids back on the host, inside the timed region
+    barrier()
+    h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    h0.record()
+    e2e_tokens = 0
+    for i in range(args.steps):
+        ids = host_prompts[args.warmup + args.steps + i].to(device, non_blocking=True)
+        r = gen(ids)
+        e2e_tokens += r.num_output_tokens
+    h1.record()
+    barrier()
+    e2e_c = D.gather_counters([h0.elapsed_time(h1) / 1e3, e2e_tokens], device=device)
+    e2e_value = float(e2e_c[:, 1].sum()) / float(e2e_c[:, 0].max())
+
+    # roofline of this package's dominant kernel in the round: the tree
+    # attention at the verify shape of mid-generation (prefix 512 + 512, 33 rows)
+    roof = _attention_roofline_at(device, DEC_PROMPT + args.new_tokens // 2, DEC_BUDGET + 1)
+    status = kernels.attention_status(device)
+    out = None
+    if rank == 0:
+        acc = [a for r in results for a in r.acceptance_lengths]
+        per_round_ms = {k: round(v / max(rounds, 1) * 1e3, 4) for k, v in stage.items()}
+        out = {
+            "metric": DEC_METRIC, "value": round(value, 2), "unit": DEC_UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(wall / args.steps * 1e3, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random-init weights, seeded uniform random prompt ids)",
+            "config": {"workload": _decode_workload(args.new_tokens), "global_batch": world, "seq_len": DEC_PROMPT,
+                       "parallelism": f"data parallel x{world} (prompts sharded by rank, one stream per GPU)",
+                       "l2": "weights (8.1 GB per verify) larger than L2"},
+            "decode_tok_s_excluding_prefill": round(float(counters[:, 1].sum()) / float(counters[:, 3].max()), 2),
+            "time_to_first_token_ms": round(float(counters[:, 4].max()) / args.steps * 1e3, 2),
+            "tokens_per_round": round(tokens / max(rounds, 1), 4),
+            "acceptance_histogram": {str(k): acc.count(k) for k in sorted(set(acc))},
+            "stage_ms_per_round": per_round_ms,
+            "roofline": roof,
+            "e2e": {"value": round(e2e_value, 2), "unit": DEC_UNIT, "h2d_bytes_per_step": DEC_PROMPT * 8,
+                    "d2h_bytes_per_step": (DEC_PROMPT + args.new_tokens) * 8,
+                    "api": "ddtree_eagle3_patch_b200.ddtree.ddtree_generate (host prompt in, host ids out)"},
+            "gpu_launches": int(launches), "clocks": clock, "attention_status": status,
+            "model_build_s": round(t_build, 1),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            out["cpu_baseline"] = cpu_decode_baseline(rounds=2)
+    if world > 1:
+        dist.barrier()
+    return out
+
+
+def _cpu_decode_models():
+    from ddtree_eagle3_patch_b200.synthetic import dflash_config, target_config
+    from oracle.cpu_decode import build_cpu_models
+    tcfg = target_config(DEC_SHAPE)
+    dcfg = dflash_config(tcfg, DEC_DRAFT_LAYERS, DEC_BLOCK)
+    return build_cpu_models(tcfg, dcfg, torch.bfloat16, seed=0)
+
+
+def _cpu_decode_estimate(prefill_s: float, rounds: list, new_tokens: int):
+    per_round = sum(r["total"] for r in rounds) / len(rounds)
+    tokens_per_round = sum(r["accepted"] for r in rounds) / len(rounds)
+    call_s = prefill_s + new_tokens / tokens_per_round * per_round
+    return new_tokens / call_s, per_round, tokens_per_round
+
+
+def cpu_decode_baseline(rounds: int):
+    """The reference's decode loop on the host (oracle/cpu_decode.py): one
+    prefill of the 512-token prompt, then ``rounds`` decode rounds; the
+    whole-call rate of the 1024-token workload is estimated from them."""
+    from oracle.cpu_decode import CpuDecode
+    torch.set_num_threads(os.cpu_count() or 1)
+    target, draft = _cpu_decode_models()
+    prompt = _decode_prompts(0, 1, draft.mask_token_id)[0]
+    run = CpuDecode(draft, target, prompt, DEC_NEW_TOKENS, DEC_BLOCK, DEC_BUDGET)
+    prefill_s = run.prefill()
+    rec = [run.round() for _ in range(rounds)]
+    value, per_round, tpr = _cpu_decode_estimate(prefill_s, rec, DEC_NEW_TOKENS)
+    return {"value": round(value, 4), "unit": DEC_UNIT, "cores": torch.get_num_threads(), "kind": "port",
+            "sample": (f"prefill of the {DEC_PROMPT}-token prompt plus {rounds} decode rounds of the reference loop; "
+                       f"whole-call rate = {DEC_NEW_TOKENS} / (prefill + {DEC_NEW_TOKENS} / tokens-per-round x "
+                       f"round time)"),
+            "prefill_s": round(prefill_s, 3), "round_s": round(per_round, 3), "tokens_per_round": round(tpr, 3)}
+
+
+def run_decode_reference(args, rank, world, local):
+    """The reference arm of the decode workload: the reference's loop on the
+    host cores (rank 0 only).  A step is one decode round after one shared
+    prefill; ``value`` is the whole-call rate of the configured workload
+    estimated from the measured prefill and the K timed rounds."""
+    if world > 1:
+        init_dist(world, "gloo")
+        import torch.distributed as tdist
+        tdist.barrier()
+        if rank != 0:
+            return None
+    from oracle.cpu_decode import CpuDecode
+    torch.set_num_threads(os.cpu_count() or 1)
+    target, draft = _cpu_decode_models()
+    prompt = _decode_prompts(0, 1, draft.mask_token_id)[0]
+    run = CpuDecode(draft, target, prompt, DEC_NEW_TOKENS, DEC_BLOCK, DEC_BUDGET)
+    prefill_s = run.prefill()
+    for _ in range(args.warmup):
+        run.round()
+    t0 = time.perf_counter()
+    rec = [run.round() for _ in range(args.steps)]
+    wall = time.perf_counter() - t0
+    value, per_round, tpr = _cpu_decode_estimate(prefill_s, rec, args.new_tokens)
+    sample = (f"one prefill of the {DEC_PROMPT}-token prompt ({prefill_s:.2f} s), {args.warmup} untimed and "
+              f"{args.steps} timed decode rounds ({per_round:.3f} s each, {tpr:.2f} tokens per round); value = "
+              f"{args.new_tokens} / (prefill + {args.new_tokens} / tokens-per-round x round time)")
+    return {"metric": DEC_METRIC, "value": round(value, 4), "unit": DEC_UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(per_round * 1e3, 2), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random-init weights, seeded uniform random prompt ids)", "impl": "reference",
+            "config": {"workload": _decode_workload(args.new_tokens), "parallelism": "host CPU, rank 0"},
+            "cpu_baseline": {"value": round(value, 4), "unit": DEC_UNIT, "cores": torch.get_num_threads(),
+                             "kind": "port", "sample": sample},
+            "e2e": {"value": round(value, 4), "unit": DEC_UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "stage_s_per_round": {k: round(sum(r[k] for r in rec) / len(rec), 4)
+                                  for k in ("draft", "tree_build", "tree_compile", "verify", "commit")},
+            "wall_s": round(wall, 2)}
+
+
 def main():
     args = parse()
     rank, world, local = dist_env()
     if args.kernel:
         run_kernel_only(args, local)
         return
-    if args.impl == "reference":
+    if args.workload == "decode":
+        out = run_decode_reference(args, rank, world, local) if args.impl == "reference" else \
+            run_decode(args, rank, world, local)
+    elif args.impl == "reference":
         out = run_reference(args, rank, world, local)
     else:
         out = run_ours(args, rank, world, local)

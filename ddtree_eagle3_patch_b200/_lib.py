@@ -66,6 +66,7 @@ _SIGNATURES = {
     "ddt_last_error": (ctypes.c_char_p, []),
     "ddt_abi_version": (ctypes.c_int, []),
     "ddt_sm_count": (ctypes.c_int, [ctypes.c_int]),
+    "ddt_launch_count": (ctypes.c_uint64, []),
     "ddt_tree_build_workspace_size": (ctypes.c_size_t, [_c_i64, _c_i64, _c_i64]),
     "ddt_tree_build": (ctypes.c_int, [_c_p, ctypes.c_int, _c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_i64,
                                       ctypes.POINTER(TreeOutputs), _c_p, ctypes.c_size_t, _c_p]),
@@ -83,6 +84,7 @@ _SIGNATURES = {
                                        ctypes.c_float, ctypes.c_uint64, ctypes.c_uint64, _c_p, _c_p, ctypes.c_size_t,
                                        _c_p]),
     "ddt_tree_attention_window": (ctypes.c_int, [ctypes.POINTER(AttentionArgs), _c_p, _c_p, ctypes.c_size_t, _c_p]),
+    "ddt_tree_attention_f32": (ctypes.c_int, [ctypes.POINTER(AttentionArgs), _c_p, _c_p, _c_p]),
     "ddt_tree_accept_workspace_size": (ctypes.c_size_t, [_c_i64, _c_i64]),
     "ddt_tree_accept": (ctypes.c_int, [_c_p, ctypes.c_int, _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_p,
                                        _c_i64, _c_p, _c_p, ctypes.c_size_t, _c_p]),

@@ -1,4 +1,5 @@
 // Error reporting and device queries shared by the C-ABI entry points.
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <mutex>
@@ -17,9 +18,14 @@ int set_error(int status, const char* fmt, ...) {
     return status;
 }
 
+// Kernels launched by this library since load (every launch goes through
+// check_launch); read by ddt_launch_count().
+static std::atomic<unsigned long long> g_launches{0};
+
 int check_launch(const char* what) {
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return set_error(DDT_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+    g_launches.fetch_add(1, std::memory_order_relaxed);
     return DDT_OK;
 }
 
@@ -28,6 +34,8 @@ int check_launch(const char* what) {
 extern "C" const char* ddt_last_error(void) { return ddt::g_last_error; }
 
 extern "C" int ddt_abi_version(void) { return 1; }
+
+extern "C" uint64_t ddt_launch_count(void) { return ddt::g_launches.load(std::memory_order_relaxed); }
 
 extern "C" int ddt_sm_count(int device) {
     static std::mutex mu;

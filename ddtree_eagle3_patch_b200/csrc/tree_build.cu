@@ -1136,10 +1136,11 @@ extern "C" int ddt_tree_from_log_probs(const float* lp, const int64_t* ids, int6
 // ---------------------------------------------------------------------------
 // Tree build for callers that cannot allocate device memory.
 //
-// Some callers of this library cannot call cudaMalloc: code running inside a
-// CUDA-graph capture, or a host application whose device memory is owned
-// by another allocator (a serving framework's memory pool, a game engine
-// budget) and that must not grow it behind that allocator's back.  For them
+// Some callers of this library cannot call cudaMalloc: a plugin that is
+// handed only its input and output buffers, or a host application whose
+// device memory is owned by another allocator (a serving framework's memory
+// pool, a game engine budget) and that must not grow it behind that
+// allocator's back.  For them
 // ddt_tree_build_noalloc runs the same kernel as ddt_tree_build, with its
 // scratch in a fixed 1 MiB array that lives in this library's device image.
 // Every GPU that loads the library holds that MiB until the process exits.

@@ -317,3 +317,292 @@ def compact_dynamic_cache(past_key_values, past_length: int, keep_current_indice
         table = _TABLES.setdefault((device, shape, len(group)), kernels.PointerTable())
         kernels.kv_compact(group, past_length, cur, buf[1:], buf[:1], len(keep), table=table)
     past_key_values.crop(past_length + len(keep))
+
+
+# ----------------------------------------------------------------------------
+# The decode loop
+# ----------------------------------------------------------------------------
+def detect_hybrid_attention(target):
+    """``(layer_types, sliding_window)`` when the target interleaves
+    sliding-window and full attention layers (Gemma 3/4), else ``(None,
+    None)`` (ddtree.py:27-49).  The text tower's config is used when the
+    model has one."""
+    cfg = getattr(target, "config", None)
+    if cfg is None:
+        return None, None
+    text_cfg = getattr(cfg, "text_config", None) or cfg
+    layer_types = getattr(text_cfg, "layer_types", None)
+    window = getattr(text_cfg, "sliding_window", None)
+    if not layer_types or window is None or int(window) <= 0:
+        return None, None
+    if "sliding_attention" not in layer_types or "full_attention" not in layer_types:
+        return None, None
+    return list(layer_types), int(window)
+
+
+def tree_node_count(budget: int, rows: int, vocab: int) -> int:
+    """Nodes of the best-first tree, known before it is built.
+
+    The expansion pops until the budget is met or the heap is empty, and
+    the heap empties only after every node of the complete top-k tree of
+    depth ``rows`` has been popped: each pop pushes its next sibling and its
+    first child (ddtree.py:157-177).  So n = min(budget, sum_{d=1..rows}
+    topk^d), topk = min(budget, vocab), and the verify batch size needs no
+    read-back of the tree."""
+    if budget <= 0 or rows <= 0:
+        return 0
+    k = min(budget, vocab)
+    total, level = 0, 1
+    for _ in range(rows):
+        level *= k
+        total += level
+        if total >= budget:
+            return budget
+    return total
+
+
+@torch.inference_mode()
+def ddtree_generate(model, target, input_ids: torch.Tensor, mask_token_id: int, max_new_tokens: int,
+                    block_size: int, stop_token_ids, temperature: float = 0.0, tree_budget: int | None = None,
+                    save_tree_traces: bool = False) -> SimpleNamespace:
+    """DDTree speculative decoding (ddtree.py:372-587), same arguments and
+    same ``SimpleNamespace`` result.
+
+    Each round: the draft predicts ``block_size - 1`` positions; the tree
+    kernel builds the best-first tree, its verify ids and positions and the
+    packed ancestor bits on the device; the target verifies every node in
+    one forward through the tree-attention kernel (the attention layers are
+    routed to it for the call); the accept kernel takes the argmax of every
+    verify row (or a temperature draw) and walks the tree; the commit kernel
+    writes the accepted and bonus tokens into ``output_ids`` and gathers the
+    accepted rows of the target's context features; one launch compacts
+    every layer's K and V.  The accepted count stays on the device until the
+    round's single host read, which also returns the new tokens for the stop
+    check.  Stage times come from CUDA events (``stage_times`` has the
+    reference's keys; the fused tree kernel's time is booked to
+    ``tree_build``, its three sub-stages read 0, and ``tree_compile`` is the
+    host time to describe the tree mask).
+    """
+    if block_size <= 1:
+        return _target_only_generate(model, target, input_ids, mask_token_id, max_new_tokens, block_size,
+                                     stop_token_ids, temperature)
+    from .cache import TreeAppendCache
+    from .model import apply_final_logit_softcapping, extract_context_feature
+    from .runtime import (EventClock, Readback, TreeMask, compact_on_device, device_sample_seed,
+                          tree_attention_for)
+
+    device = model.device
+    num_input_tokens = input_ids.shape[1]
+    max_length = num_input_tokens + max_new_tokens
+    draft_horizon = block_size - 1
+    tree_budget = draft_horizon if tree_budget is None else max(int(tree_budget), 0)
+    max_tree_nodes = 1 + tree_budget
+    vocab = target.lm_head.weight.shape[0] if hasattr(target, "lm_head") else target.config.vocab_size
+
+    output_ids = torch.full((1, max_length + max_tree_nodes), mask_token_id, dtype=torch.long, device=device)
+    position_ids = torch.arange(output_ids.shape[1], device=device).unsqueeze(0)
+    stop_ids = None if stop_token_ids is None else set(int(t) for t in stop_token_ids)
+    layer_types, sliding_window = detect_hybrid_attention(target)
+
+    target_cache = TreeAppendCache(max_length + max_tree_nodes + 1, config=target.config)
+    draft_cache = TreeAppendCache(max_length + max_tree_nodes + block_size + 1, config=model.config)
+    tree = kernels.DeviceTree.allocate(draft_horizon, vocab, tree_budget, device)
+    accepted = torch.zeros((max_tree_nodes,), dtype=torch.int64, device=device)
+    accept_info = torch.zeros((2,), dtype=torch.int64, device=device)
+    posterior = torch.empty((max_tree_nodes,), dtype=torch.int64, device=device)
+    tree_mask = TreeMask(target.dtype, device)
+    readback = Readback(4 + 6 * max_tree_nodes, device)
+    tables: dict = {}
+    seed = device_sample_seed() if temperature >= 1e-5 else 0
+
+    stage_times = empty_stage_times(DDTREE_STAGE_ORDER + DDTREE_TREE_BUILD_STAGE_ORDER)
+    clock = EventClock(device)
+    hidden_buf = None
+
+    with tree_attention_for(target):
+        ev_prefill = clock.mark()
+        output = target(input_ids, position_ids=position_ids[:, :num_input_tokens], past_key_values=target_cache,
+                        use_cache=True, logits_to_keep=1, output_hidden_states=True)
+        output_ids[:, :num_input_tokens] = input_ids
+        output_ids[:, num_input_tokens: num_input_tokens + 1] = kernels.sample(output.logits, temperature)
+        target_hidden = extract_context_feature(output.hidden_states, model.target_layer_ids)
+        ev_first = clock.mark()
+
+        ev_decode = clock.mark()
+        ev_round_clock = ev_decode
+        start = num_input_tokens
+        acceptance_lengths, round_ends = [], []
+        round_trees = [] if save_tree_traces else None
+        draft_prefill = True
+        rnd = 0
+        while start < max_length:
+            ev0 = clock.mark()
+            block = output_ids[:, start: start + block_size]
+            noise_embedding = target.model.embed_tokens(block)
+            draft_hidden = model(target_hidden=target_hidden, noise_embedding=noise_embedding,
+                                 position_ids=position_ids[:, draft_cache.get_seq_length(): start + block_size],
+                                 past_key_values=draft_cache, use_cache=True, is_causal=False)
+            draft_logits = target.lm_head(draft_hidden[:, -draft_horizon:, :])
+            draft_logits = apply_final_logit_softcapping(draft_logits, model.final_logit_softcapping)
+            draft_cache.crop(start)
+            ev1 = clock.mark()
+            if draft_prefill:
+                draft_prefill = False
+                ev_decode = ev1
+            else:
+                clock.span("draft", ev0, ev1)
+
+            rows = draft_logits.shape[1]
+            kernels.tree_build(draft_logits[0], tree_budget, root_token=output_ids[0, start: start + 1],
+                               start=start, out=tree)
+            n_nodes = tree_node_count(tree_budget, rows, draft_logits.shape[-1])
+            N = 1 + n_nodes
+            ev2 = clock.mark()
+            clock.span("tree_build", ev1, ev2)
+
+            bits = tree.visibility[:N]
+            mask = tree_mask(bits, start, N)
+            if sliding_window is not None:
+                key_lo = sliding_key_lo(tree.verify_pos[:N], sliding_window)
+                mask = {"full_attention": mask, "sliding_attention": tree_mask(bits, start, N, key_lo)}
+            ev3 = clock.mark()
+            clock.span("tree_compile", ev2, ev3)
+
+            output = target(tree.verify_ids[:N].unsqueeze(0), position_ids=tree.verify_pos[:N].unsqueeze(0),
+                            attention_mask=mask, past_key_values=target_cache, use_cache=True,
+                            output_hidden_states=True)
+            ev4 = clock.mark()
+            clock.span("verify", ev3, ev4)
+
+            logits = output.logits[0]
+            if temperature < 1e-5:
+                kernels.tree_accept(logits, tree.parents, tree.node_token_ids, tree.info, max_accept=N,
+                                    accepted=accepted[:N], accept_info=accept_info, posterior=posterior[:N])
+            else:
+                post = kernels.sample_rows(logits, temperature, seed, rnd)
+                acc_t, info_t = kernels.tree_walk(post, tree.parents, tree.node_token_ids, tree.info, max_accept=N)
+                accepted[:N].copy_(acc_t)
+                accept_info.copy_(info_t)
+            features = extract_context_feature(output.hidden_states, model.target_layer_ids)
+            if hidden_buf is None or hidden_buf.shape[-1] != features.shape[-1]:
+                hidden_buf = torch.empty((max_tree_nodes, features.shape[-1]), dtype=features.dtype, device=device)
+            kernels.tree_commit(tree.verify_ids[:N], accepted[:N], accept_info, output_ids[0], start,
+                                hidden=features[0], hidden_out=hidden_buf[:N])
+            compact_on_device(target_cache, start, N, accepted, accept_info[:1], N, tables)
+            pieces = [(accept_info, 2), (output_ids[0, start:], N + 1)]
+            if save_tree_traces:
+                pieces += [(accepted, N), (tree.node_token_ids, n_nodes), (tree.node_depths, n_nodes),
+                           (tree.parents.to(torch.int64), N)]
+            got = readback.fetch(pieces)
+            count, new_tokens = int(got[0][0]), got[1][: int(got[0][0]) + 1]
+            target_cache.crop(start + count)
+            target_hidden = hidden_buf[None, :count]
+            acceptance_lengths.append(count)
+            start += count
+            ev5 = clock.mark()
+            clock.span("commit", ev4, ev5)
+            round_ends.append(ev5)
+            if save_tree_traces:
+                parents = [int(p) for p in got[5]]
+                parents[0] = -1
+                round_trees.append({
+                    "accepted_indices": [int(i) for i in got[2][:count]],
+                    "tree": {"node_token_ids": [int(t) for t in got[3]], "node_depths": [int(d) for d in got[4]],
+                             "parents": parents}})
+            rnd += 1
+            if stop_ids is not None and any(t in stop_ids for t in new_tokens):
+                break
+
+        ev_end = clock.mark()
+
+    output_ids = output_ids[:, :max_length]
+    output_ids = output_ids[:, output_ids[0] != mask_token_id]
+    if stop_ids is not None:
+        gen = output_ids[0, num_input_tokens:].tolist()
+        for i, t in enumerate(gen):
+            if t in stop_ids:
+                output_ids = output_ids[:, : num_input_tokens + i + 1]
+                break
+    num_output_tokens = output_ids.shape[1] - num_input_tokens
+    clock.resolve(stage_times)
+    total_decode_time = EventClock.seconds(ev_decode, ev_end)
+    return SimpleNamespace(
+        output_ids=output_ids.cpu(),
+        num_input_tokens=num_input_tokens,
+        num_output_tokens=num_output_tokens,
+        time_to_first_token=EventClock.seconds(ev_prefill, ev_first),
+        time_per_output_token=total_decode_time / max(num_output_tokens, 1),
+        acceptance_lengths=acceptance_lengths,
+        decode_rounds=len(acceptance_lengths),
+        stage_times=stage_times,
+        round_timestamps=[EventClock.seconds(ev_round_clock, e) for e in round_ends],
+        round_trees=round_trees,
+    )
+
+
+DFLASH_STAGE_ORDER = ("draft", "verify", "commit")
+
+
+def _target_only_generate(model, target, input_ids, mask_token_id, max_new_tokens, block_size, stop_token_ids,
+                          temperature):
+    """``ddtree_generate`` with ``block_size <= 1`` hands over to the
+    reference's ``dflash_generate`` (ddtree.py:383-393), which then decodes
+    one target token per round without a draft (dflash.py:18-143 with a
+    one-token block).  That is what this does, with the same result fields."""
+    if block_size < 1:
+        raise ValueError("block_size must be at least 1")
+    from .cache import TreeAppendCache
+    from .runtime import EventClock, Readback, tree_attention_for
+
+    device = model.device
+    num_input_tokens = input_ids.shape[1]
+    max_length = num_input_tokens + max_new_tokens
+    output_ids = torch.full((1, max_length + block_size), mask_token_id, dtype=torch.long, device=device)
+    position_ids = torch.arange(output_ids.shape[1], device=device).unsqueeze(0)
+    stop_ids = None if stop_token_ids is None else set(int(t) for t in stop_token_ids)
+    cache = TreeAppendCache(max_length + 2, config=target.config)
+    stage_times = empty_stage_times(DFLASH_STAGE_ORDER)
+    clock = EventClock(device)
+    readback = Readback(4, device)
+    with tree_attention_for(target):
+        ev_prefill = clock.mark()
+        out = target(input_ids, position_ids=position_ids[:, :num_input_tokens], past_key_values=cache,
+                     use_cache=True, logits_to_keep=1)
+        output_ids[:, :num_input_tokens] = input_ids
+        output_ids[:, num_input_tokens: num_input_tokens + 1] = kernels.sample(out.logits, temperature)
+        ev_first = clock.mark()
+        ev_decode = clock.mark()
+        start = num_input_tokens
+        acceptance_lengths, round_ends = [], []
+        while start < max_length:
+            ev0 = clock.mark()
+            out = target(output_ids[:, start: start + 1], position_ids=position_ids[:, start: start + 1],
+                         past_key_values=cache, use_cache=True)
+            ev1 = clock.mark()
+            clock.span("verify", ev0, ev1)
+            output_ids[:, start + 1] = kernels.sample(out.logits, temperature)[:, 0]
+            got = readback.fetch([(output_ids[0, start:], 2)])
+            acceptance_lengths.append(1)
+            start += 1
+            ev2 = clock.mark()
+            clock.span("commit", ev1, ev2)
+            round_ends.append(ev2)
+            if stop_ids is not None and any(t in stop_ids for t in got[0]):
+                break
+        ev_end = clock.mark()
+    output_ids = output_ids[:, :max_length]
+    output_ids = output_ids[:, output_ids[0] != mask_token_id]
+    if stop_ids is not None:
+        for i, t in enumerate(output_ids[0, num_input_tokens:].tolist()):
+            if t in stop_ids:
+                output_ids = output_ids[:, : num_input_tokens + i + 1]
+                break
+    num_output_tokens = output_ids.shape[1] - num_input_tokens
+    clock.resolve(stage_times)
+    total = EventClock.seconds(ev_decode, ev_end)
+    return SimpleNamespace(
+        output_ids=output_ids.cpu(), num_input_tokens=num_input_tokens, num_output_tokens=num_output_tokens,
+        time_to_first_token=EventClock.seconds(ev_prefill, ev_first),
+        time_per_output_token=total / max(num_output_tokens, 1), acceptance_lengths=acceptance_lengths,
+        decode_rounds=len(acceptance_lengths), stage_times=stage_times,
+        round_timestamps=[EventClock.seconds(ev_decode, e) for e in round_ends])

@@ -31,6 +31,7 @@ __all__ = [
     "gather",
     "all_gather",
     "shard_indices",
+    "gather_counters",
     "merge_counters",
 ]
 
@@ -102,6 +103,27 @@ def shard_indices(n: int, rank_: Optional[int] = None, size_: Optional[int] = No
     if s <= 0 or not 0 <= r < s:
         raise ValueError(f"rank {r} outside world of size {s}")
     return range(r, n, s)
+
+
+def gather_counters(values, device=None):
+    """Every rank's fixed-size counter vector, gathered in one collective.
+
+    The reference gathers pickled response objects to rank 0
+    (distributed.py:55-64, benchmark.py:237-241); the counters its analysis
+    needs (tokens, rounds, accepted lengths, times) are fixed-size numbers,
+    so here each rank contributes one float64 vector and a single
+    ``all_gather_into_tensor`` (NCCL over NVLink for CUDA tensors, gloo on
+    CPU) returns the [world, n] matrix on every rank.  Single-process: the
+    [1, n] matrix of this rank."""
+    import torch
+    vec = torch.as_tensor(values, dtype=torch.float64)
+    if device is not None:
+        vec = vec.to(device)
+    if not is_initialized():
+        return vec.unsqueeze(0)
+    out = torch.empty((dist.get_world_size(), vec.numel()), dtype=torch.float64, device=vec.device)
+    dist.all_gather_into_tensor(out, vec.contiguous())
+    return out
 
 
 def merge_counters(per_rank: Iterable[Dict[str, float]]) -> Dict[str, float]:

@@ -159,8 +159,10 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, past_lengt
     if not on_gpu:
         for t, n in ((q, "q"), (k, "k"), (v, "v"), (visibility, "visibility")):
             require_cuda(t, n)
+    if q.dtype == torch.float32 and k.dtype == torch.float32 and v.dtype == torch.float32:
+        return tree_attention_f32(q, k, v, past_length, visibility, scale, out=out, key_lo=key_lo)
     if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
-        raise TypeError("q, k, v must be bf16")
+        raise TypeError("q, k, v must all be bf16 (tensor-core path) or all float32")
     qs, ks = q.stride(), k.stride()
     kshape = k.shape
     if qs[-1] != 1 or ks[-1] != 1:
@@ -194,6 +196,44 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, past_lengt
         raise ValueError("key_lo must be a contiguous int64 CUDA tensor with one entry per token")
     check(lib.ddt_tree_attention_window(ctypes.byref(a), key_lo.data_ptr(), ws[1], ws[2], _lib.raw_stream(dev_index)),
           "ddt_tree_attention_window")
+    return out
+
+
+def tree_attention_f32(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, past_length: int,
+                       visibility: torch.Tensor, scale: float, out: torch.Tensor | None = None,
+                       key_lo: torch.Tensor | None = None, past_dev: torch.Tensor | None = None) -> torch.Tensor:
+    """Float32 tree attention (``ddt_tree_attention_f32``): the layouts of
+    ``tree_attention`` with float32 tensors.  ``past_dev`` (int32 device
+    scalar) makes the prefix length a run-time value; ``past_length`` is then
+    its upper bound."""
+    for t, n in ((q, "q"), (k, "k"), (v, "v"), (visibility, "visibility")):
+        require_cuda(t, n)
+    if q.dtype != torch.float32 or k.dtype != torch.float32 or v.dtype != torch.float32:
+        raise TypeError("q, k, v must be float32")
+    qs, ks = q.stride(), k.stride()
+    if qs[-1] != 1 or ks[-1] != 1:
+        raise ValueError("head_dim must be the contiguous dimension")
+    if v.stride() != ks or v.shape != k.shape:
+        raise ValueError("k and v must share shape and strides")
+    n_tokens, hq, d = q.shape
+    hkv, kv_rows, _ = k.shape
+    if out is None:
+        out = torch.empty((n_tokens, hq, d), dtype=torch.float32, device=q.device)
+    if out.dtype != torch.float32:
+        raise TypeError("out must be float32")
+    if not visibility.is_contiguous():
+        visibility = visibility.contiguous()
+    if key_lo is not None and (not key_lo.is_cuda or key_lo.dtype != torch.int64 or not key_lo.is_contiguous()
+                               or key_lo.numel() < n_tokens):
+        raise ValueError("key_lo must be a contiguous int64 CUDA tensor with one entry per token")
+    if past_dev is not None and (not past_dev.is_cuda or past_dev.dtype != torch.int32):
+        raise ValueError("past_dev must be an int32 CUDA tensor")
+    os_ = out.stride()
+    a = AttentionArgs(q.data_ptr(), qs[0], qs[1], k.data_ptr(), v.data_ptr(), ks[0], ks[1], kv_rows, out.data_ptr(),
+                      os_[0], os_[1], n_tokens, hq, hkv, d, int(past_length), visibility.data_ptr(),
+                      visibility.shape[1], float(scale))
+    check(_lib.load().ddt_tree_attention_f32(ctypes.byref(a), ptr(key_lo), ptr(past_dev), stream_of(q.device)),
+          "ddt_tree_attention_f32")
     return out
 
 

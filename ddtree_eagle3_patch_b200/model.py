@@ -1,0 +1,203 @@
+"""The DFlash block-diffusion draft model and the model-side helpers that the
+decode loop calls (the reference's ``model`` package: model/dflash.py,
+model/utils.py of kimwin2/ddtree_eagle3_patch).
+
+The draft is not part of the accelerated path: it produces the draft logits
+that the tree build consumes.  It is here so the decode loop can run where
+the reference cannot be imported, and its parameter names, config keys and
+``forward`` signature are the reference's, so a DFlash checkpoint loads
+into it unchanged (``DFlashDraftModel.from_pretrained``) and ``ddtree_generate``
+accepts either class.
+
+What it computes (model/dflash.py:28-197): each layer attends from the
+block's noise rows (queries) to [context rows ; noise rows] (keys/values),
+non-causally; the context rows are the target's hidden features projected
+by ``fc`` and normalised by ``hidden_norm``; K gets ``k_norm`` before the
+rotary embedding and Q takes the last ``q_len`` rotary positions.  The
+attention itself runs on the tree-attention kernel with every key visible,
+over the draft cache's rows in place.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import numpy as np
+import torch
+from torch import nn
+from transformers.models.qwen3.modeling_qwen3 import (
+    Qwen3Config,
+    Qwen3MLP,
+    Qwen3PreTrainedModel,
+    Qwen3RMSNorm,
+    Qwen3RotaryEmbedding,
+    rotate_half,
+)
+
+from . import kernels
+
+__all__ = [
+    "DFlashDraftModel",
+    "build_target_layer_ids",
+    "extract_context_feature",
+    "sample",
+    "get_final_logit_softcapping",
+    "apply_final_logit_softcapping",
+]
+
+
+def build_target_layer_ids(num_target_layers: int, num_draft_layers: int) -> list[int]:
+    """Target layers whose hidden states feed the draft (model/utils.py:5-15):
+    the middle layer for a 1-layer draft, else evenly spaced from layer 1 to
+    layer num_target_layers - 3."""
+    if num_draft_layers == 1:
+        return [num_target_layers // 2]
+    lo, hi = 1, num_target_layers - 3
+    return [int(round(lo + i * (hi - lo) / (num_draft_layers - 1))) for i in range(num_draft_layers)]
+
+
+def extract_context_feature(hidden_states, layer_ids) -> torch.Tensor:
+    """Concatenate the target's hidden states after each listed layer
+    (index + 1 into HF's ``hidden_states``, whose entry 0 is the embedding
+    output; model/utils.py:17-26)."""
+    return torch.cat([hidden_states[i + 1] for i in layer_ids], dim=-1)
+
+
+def sample(logits: torch.Tensor, temperature: float = 0.0) -> torch.Tensor:
+    """``model.utils.sample`` (model/utils.py:28-35) on the device kernels:
+    row argmax below temperature 1e-5, else a draw from softmax(logits / T)."""
+    return kernels.sample(logits, temperature)
+
+
+def get_final_logit_softcapping(config) -> Optional[float]:
+    """``dflash_config['final_logit_softcapping']``, else the config attribute
+    (model/utils.py:37-42)."""
+    dflash_config = getattr(config, "dflash_config", None) or {}
+    value = dflash_config.get("final_logit_softcapping", getattr(config, "final_logit_softcapping", None))
+    return None if value is None else float(value)
+
+
+def apply_final_logit_softcapping(logits: torch.Tensor, final_logit_softcapping: Optional[float]) -> torch.Tensor:
+    """cap * tanh(logits / cap), or the logits unchanged (model/utils.py:44-50)."""
+    if final_logit_softcapping is None:
+        return logits
+    return torch.tanh(logits / final_logit_softcapping) * final_logit_softcapping
+
+
+_ALL_VISIBLE: dict = {}
+
+
+def _all_visible_bits(n: int, device: torch.device) -> torch.Tensor:
+    """Packed mask of n rows that see all n new keys (non-causal)."""
+    key = (n, device)
+    b = _ALL_VISIBLE.get(key)
+    if b is None:
+        words = np.zeros((n, (n + 31) // 32), np.uint32)
+        full, rem = divmod(n, 32)
+        words[:, :full] = 0xFFFFFFFF
+        if rem:
+            words[:, full] = (1 << rem) - 1
+        b = torch.from_numpy(words.view(np.int32)).to(device)
+        _ALL_VISIBLE[key] = b
+    return b
+
+
+class DFlashAttention(nn.Module):
+    """Noise-row queries over [context ; noise] keys (model/dflash.py:36-108)."""
+
+    def __init__(self, config: Qwen3Config, layer_idx: int):
+        super().__init__()
+        self.layer_idx = layer_idx
+        self.head_dim = getattr(config, "head_dim", None) or config.hidden_size // config.num_attention_heads
+        self.num_heads = config.num_attention_heads
+        self.num_kv_heads = config.num_key_value_heads
+        self.scaling = self.head_dim ** -0.5
+        bias = config.attention_bias
+        self.q_proj = nn.Linear(config.hidden_size, self.num_heads * self.head_dim, bias=bias)
+        self.k_proj = nn.Linear(config.hidden_size, self.num_kv_heads * self.head_dim, bias=bias)
+        self.v_proj = nn.Linear(config.hidden_size, self.num_kv_heads * self.head_dim, bias=bias)
+        self.o_proj = nn.Linear(self.num_heads * self.head_dim, config.hidden_size, bias=bias)
+        self.q_norm = Qwen3RMSNorm(self.head_dim, eps=config.rms_norm_eps)
+        self.k_norm = Qwen3RMSNorm(self.head_dim, eps=config.rms_norm_eps)
+
+    def forward(self, hidden_states: torch.Tensor, target_hidden: torch.Tensor, position_embeddings,
+                past_key_values=None) -> torch.Tensor:
+        bsz, q_len, _ = hidden_states.shape
+        if bsz != 1:
+            raise NotImplementedError("the DFlash draft runs batch 1, as the reference's decode loop does")
+        ctx_len = target_hidden.shape[1]
+        hd = self.head_dim
+        q = self.q_norm(self.q_proj(hidden_states).view(1, q_len, self.num_heads, hd))
+        # context and noise rows are projected separately, as in the reference,
+        # so each row sees the same GEMM shapes as there
+        k = torch.cat([self.k_proj(target_hidden), self.k_proj(hidden_states)], dim=1)
+        v = torch.cat([self.v_proj(target_hidden), self.v_proj(hidden_states)], dim=1)
+        k = self.k_norm(k.view(1, ctx_len + q_len, self.num_kv_heads, hd)).transpose(1, 2)
+        v = v.view(1, ctx_len + q_len, self.num_kv_heads, hd).transpose(1, 2)
+        cos, sin = position_embeddings
+        cos_q, sin_q = cos[:, -q_len:].unsqueeze(2), sin[:, -q_len:].unsqueeze(2)
+        q = q * cos_q + rotate_half(q) * sin_q                      # [1, q_len, Hq, D]
+        k = k * cos.unsqueeze(1) + rotate_half(k) * sin.unsqueeze(1)  # [1, Hkv, S, D]
+        if past_key_values is not None:
+            k, v = past_key_values.update(k, v, self.layer_idx)
+        kv_len = k.shape[-2]
+        bits = _all_visible_bits(q_len, q.device)
+        out = kernels.tree_attention(q[0], k[0], v[0], kv_len - q_len, bits, self.scaling)
+        return self.o_proj(out.reshape(1, q_len, self.num_heads * hd))
+
+
+class DFlashDecoderLayer(nn.Module):
+    """Pre-norm attention + MLP block (model/dflash.py:110-150)."""
+
+    def __init__(self, config: Qwen3Config, layer_idx: int):
+        super().__init__()
+        self.self_attn = DFlashAttention(config, layer_idx)
+        self.mlp = Qwen3MLP(config)
+        self.input_layernorm = Qwen3RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
+        self.post_attention_layernorm = Qwen3RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
+
+    def forward(self, hidden_states, target_hidden, position_embeddings, past_key_values=None):
+        h = hidden_states + self.self_attn(self.input_layernorm(hidden_states), target_hidden, position_embeddings,
+                                           past_key_values)
+        return h + self.mlp(self.post_attention_layernorm(h))
+
+
+class DFlashDraftModel(Qwen3PreTrainedModel):
+    """The DFlash block draft (model/dflash.py:153-197): same config keys
+    (``dflash_config.target_layer_ids`` / ``mask_token_id``, ``block_size``,
+    ``num_target_layers``), same parameter names, same ``forward``."""
+
+    config_class = Qwen3Config
+    _no_split_modules = ["DFlashDecoderLayer"]
+
+    def __init__(self, config) -> None:
+        super().__init__(config)
+        self.config = config
+        layer_types = getattr(config, "layer_types", None) or []
+        if "sliding_attention" in layer_types:
+            raise NotImplementedError("sliding-window DFlash draft layers are not supported")
+        self.layers = nn.ModuleList([DFlashDecoderLayer(config, i) for i in range(config.num_hidden_layers)])
+        dflash_config = getattr(config, "dflash_config", None) or {}
+        self.target_layer_ids = dflash_config.get(
+            "target_layer_ids", build_target_layer_ids(config.num_target_layers, config.num_hidden_layers))
+        self.norm = Qwen3RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
+        self.rotary_emb = Qwen3RotaryEmbedding(config)
+        self.fc = nn.Linear(len(self.target_layer_ids) * config.hidden_size, config.hidden_size, bias=False)
+        self.hidden_norm = Qwen3RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
+        self.block_size = config.block_size
+        self.mask_token_id = dflash_config.get("mask_token_id", None)
+        self.final_logit_softcapping = get_final_logit_softcapping(config)
+        self.post_init()
+
+    def forward(self, position_ids: torch.LongTensor, attention_mask: Optional[torch.Tensor] = None,
+                noise_embedding: Optional[torch.Tensor] = None, target_hidden: Optional[torch.Tensor] = None,
+                past_key_values=None, use_cache: bool = False, **kwargs) -> torch.Tensor:
+        """Hidden states of the noise rows, normalised: [1, q_len, hidden]."""
+        if attention_mask is not None:
+            raise NotImplementedError("the DFlash draft attends to every context and block row (no mask)")
+        hidden_states = noise_embedding
+        ctx = self.hidden_norm(self.fc(target_hidden))
+        position_embeddings = self.rotary_emb(hidden_states, position_ids)
+        cache = past_key_values if use_cache else None
+        for layer in self.layers:
+            hidden_states = layer(hidden_states, ctx, position_embeddings, cache)
+        return self.norm(hidden_states)

@@ -102,3 +102,75 @@ def tree_attention_inputs(seed: int, past: int, n: int, hq: int, hkv: int, d: in
     v = torch.randn(hkv, past + n, d, generator=g)
     _, _, vis = random_tree(n - 1, max_depth=max_depth, seed=seed)
     return (q.numpy(), k.numpy(), v.numpy(), vis, float(d) ** -0.5)
+
+
+# ----------------------------------------------------------------------------
+# random-init models of the end-to-end decode configurations
+# ----------------------------------------------------------------------------
+TARGET_SHAPES = {
+    # Qwen3-4B: 36 layers, hidden 2560, intermediate 9728, 32 q / 8 kv heads
+    "qwen3-4b": dict(hidden_size=2560, intermediate_size=9728, num_hidden_layers=36, num_attention_heads=32,
+                     num_key_value_heads=8, head_dim=128, vocab_size=V_QWEN3, tie_word_embeddings=True),
+    # Qwen3-8B: 36 layers, hidden 4096, intermediate 12288, 32 q / 8 kv heads
+    "qwen3-8b": dict(hidden_size=4096, intermediate_size=12288, num_hidden_layers=36, num_attention_heads=32,
+                     num_key_value_heads=8, head_dim=128, vocab_size=V_QWEN3, tie_word_embeddings=False),
+}
+
+
+def target_config(shape: str = "qwen3-4b"):
+    """Qwen3Config of a target shape (rope theta 1e6, 40960 positions)."""
+    from transformers import Qwen3Config
+    return Qwen3Config(max_position_embeddings=40960, rope_theta=1000000.0, rms_norm_eps=1e-6,
+                       **TARGET_SHAPES[shape])
+
+
+def dflash_config(target_cfg, num_layers: int = 5, block_size: int = 16, mask_token_id: int | None = None):
+    """A DFlash block-diffusion draft of the target's width: ``num_layers``
+    Qwen3 layers, context features from build_target_layer_ids(target
+    layers, num_layers), the given block size and mask token (default the
+    last vocabulary id)."""
+    from transformers import Qwen3Config
+    from .model import build_target_layer_ids
+    t = target_cfg
+    rope = dict(getattr(t, "rope_parameters", None) or {"rope_type": "default", "rope_theta": 1000000.0})
+    cfg = Qwen3Config(hidden_size=t.hidden_size, intermediate_size=t.intermediate_size, num_hidden_layers=num_layers,
+                      num_attention_heads=t.num_attention_heads, num_key_value_heads=t.num_key_value_heads,
+                      head_dim=t.head_dim, vocab_size=t.vocab_size, max_position_embeddings=t.max_position_embeddings,
+                      rope_parameters=rope, rms_norm_eps=t.rms_norm_eps)
+    cfg.block_size = block_size
+    cfg.num_target_layers = t.num_hidden_layers
+    cfg.dflash_config = {
+        "target_layer_ids": build_target_layer_ids(t.num_hidden_layers, num_layers),
+        "mask_token_id": t.vocab_size - 1 if mask_token_id is None else mask_token_id,
+    }
+    return cfg
+
+
+def build_decode_models(shape: str, device, dtype=torch.bfloat16, seed: int = 0, draft_layers: int = 5,
+                        block_size: int = 16):
+    """Random-init (HF initialisation, seeded) target and DFlash draft,
+    created directly on ``device`` in ``dtype``."""
+    from transformers import Qwen3ForCausalLM
+    from .model import DFlashDraftModel
+    tcfg = target_config(shape)
+    dcfg = dflash_config(tcfg, draft_layers, block_size)
+    old = torch.get_default_dtype()
+    torch.manual_seed(seed)
+    try:
+        torch.set_default_dtype(dtype)
+        with torch.device(device):
+            target = Qwen3ForCausalLM(tcfg).eval()
+            draft = DFlashDraftModel(dcfg).eval()
+    finally:
+        torch.set_default_dtype(old)
+    return target.to(dtype), draft.to(dtype)
+
+
+def random_prompt(length: int, vocab: int = V_QWEN3, seed: int = 0, exclude: int | None = None) -> torch.Tensor:
+    """[1, length] uniform random token ids (never ``exclude``)."""
+    g = torch.Generator().manual_seed(seed)
+    hi = vocab if exclude is None else vocab - 1
+    ids = torch.randint(0, hi, (1, length), generator=g)
+    if exclude is not None:
+        ids[ids >= exclude] += 1
+    return ids

@@ -48,6 +48,9 @@ enum ddt_dtype { DDT_F32 = 0, DDT_BF16 = 1, DDT_F16 = 2, DDT_BOOL = 3 };
 DDT_API const char* ddt_last_error(void);
 DDT_API int ddt_abi_version(void);
 DDT_API int ddt_sm_count(int device);
+/* Kernels this library has launched since it was loaded (all devices and
+ * threads; a launch recorded into a CUDA graph counts once, at capture). */
+DDT_API uint64_t ddt_launch_count(void);
 
 /* ---------------------------------------------------------------------------
  * (1) Tree build.
@@ -83,20 +86,22 @@ DDT_API int ddt_tree_build(const void* logits, int dtype, int64_t rows, int64_t 
 
 /* ddt_tree_build for callers that cannot allocate device memory.
  * This entry point has no counterpart in the reference.  Some callers of this
- * library cannot call cudaMalloc: code running inside a CUDA-graph capture,
- * or a host application whose device memory is owned by another allocator
- * (a serving framework's pool) and must not grow behind its back.  This call
- * takes the same inputs and outputs as ddt_tree_build but no workspace: its
- * scratch is a fixed 1 MiB array inside the library's device image, held by
- * every GPU that loads the library until the process exits.  1 MiB covers 15
- * draft rows x 151936 vocabulary up to a node budget of 512; larger shapes
- * return DDT_EUNSUPPORTED.  It calls no cudaMalloc / cudaFree.
+ * library cannot call cudaMalloc: a host application whose device memory is
+ * owned by another allocator (a serving framework's pool) that must not grow
+ * behind its back, or a plugin that is handed only its input and output
+ * buffers.  This call takes the same inputs and outputs as ddt_tree_build but
+ * no workspace: its scratch is a fixed 1 MiB array inside the library's
+ * device image, held by every GPU that loads the library until the process
+ * exits.  1 MiB covers 15 draft rows x 151936 vocabulary up to a node budget
+ * of 512; larger shapes return DDT_EUNSUPPORTED.  It calls no cudaMalloc /
+ * cudaFree.
  * The first call on a device looks up the array's device address
- * (cudaGetSymbolAddress, with that device current); make that first call
- * before any stream capture.  All calls share the one array: calls that
- * overlap on the GPU (different streams without ordering) race.  Each call
- * clears the counters at the start of the array on `stream` before its
- * launch. */
+ * (cudaGetSymbolAddress, with that device current) and keeps it for the
+ * process: it assumes the device's primary context and no cudaDeviceReset
+ * afterwards.  Make that first call before any stream capture.  All calls
+ * share the one array: calls that overlap on the GPU (different streams
+ * without ordering) race.  Each call clears the counters at the start of the
+ * array on `stream` before its launch. */
 DDT_API int ddt_tree_build_noalloc(const void* logits, int dtype, int64_t rows, int64_t vocab, int64_t row_stride,
                                    int64_t budget, const int64_t* root_token, int64_t start,
                                    const ddt_tree_outputs* out, ddt_stream_t stream);
@@ -164,6 +169,19 @@ DDT_API int ddt_tree_attention(const ddt_attention_args* args, void* workspace, 
  * as in ddt_tree_attention.  Same workspace. */
 DDT_API int ddt_tree_attention_window(const ddt_attention_args* args, const int64_t* key_lo, void* workspace,
                               size_t workspace_bytes, ddt_stream_t stream);
+
+/* The same attention call for float32 targets (the reference's SDPA in the
+ * target's dtype, ddtree.py:523-531): q, k, v and out are float32 with the
+ * strides of ddt_attention_args counted in float elements (multiples of 4),
+ * computed with fp32 FMAs and accurate exponentials on the CUDA cores (the
+ * tensor cores have no float32 operand form that keeps 1e-5 accuracy).
+ * key_lo (nullable) makes it a sliding-window layer as in
+ * ddt_tree_attention_window.  past_dev (nullable, device int32): the prefix
+ * length is read from it at run time, clamped to [0, args->past_length],
+ * which is then only its upper bound (kv_rows >= past_length + n_tokens).
+ * No workspace. */
+DDT_API int ddt_tree_attention_f32(const ddt_attention_args* args, const int64_t* key_lo, const int32_t* past_dev,
+                                   ddt_stream_t stream);
 
 /* ---------------------------------------------------------------------------
  * (3) Greedy acceptance and KV compaction.

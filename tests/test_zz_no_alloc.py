@@ -1,7 +1,8 @@
 """ddt_tree_build_noalloc: the tree build for callers that cannot allocate.
 
-Some callers cannot call cudaMalloc (a CUDA-graph capture in progress, or an
-application whose device memory belongs to another allocator).  The
+Some callers cannot call cudaMalloc (a plugin handed only its inputs and
+outputs, or an application whose device memory belongs to another
+allocator).  The
 no-alloc entry point runs the tree-build kernel with its scratch in a fixed
 array inside the library instead of a caller workspace.  This test calls it
 through the C ABI twice in a row and checks every output against the
