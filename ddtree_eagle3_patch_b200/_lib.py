@@ -85,6 +85,10 @@ _SIGNATURES = {
                                        _c_p]),
     "ddt_tree_attention_window": (ctypes.c_int, [ctypes.POINTER(AttentionArgs), _c_p, _c_p, ctypes.c_size_t, _c_p]),
     "ddt_tree_attention_f32": (ctypes.c_int, [ctypes.POINTER(AttentionArgs), _c_p, _c_p, _c_p]),
+    "ddt_tree_attention_dev": (ctypes.c_int, [ctypes.POINTER(AttentionArgs), _c_p, _c_p, _c_p, ctypes.c_size_t,
+                                              _c_p]),
+    "ddt_kv_append": (ctypes.c_int, [_c_p, _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
+                                     _c_i64, _c_p, _c_p, _c_p]),
     "ddt_tree_accept_workspace_size": (ctypes.c_size_t, [_c_i64, _c_i64]),
     "ddt_tree_accept": (ctypes.c_int, [_c_p, ctypes.c_int, _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_p,
                                        _c_i64, _c_p, _c_p, ctypes.c_size_t, _c_p]),

@@ -100,6 +100,16 @@ def tree_verify_attention(module, query: torch.Tensor, key: torch.Tensor, value:
     _, hq, T, d = query.shape
     S = key.shape[-2]
     scale = float(scaling) if scaling is not None else d ** -0.5
+    past_dev = getattr(attention_mask, "ddtree_past_dev", None) if attention_mask is not None else None
+    if past_dev is not None:
+        # a captured verify forward: the cache returns its whole buffers and
+        # the prefix length lives on the device (TreeMask.static)
+        q = query[0].transpose(0, 1)
+        out = torch.empty((1, T, hq, d), dtype=query.dtype, device=query.device)
+        kernels.tree_attention(q, key[0], value[0], attention_mask.ddtree_past_max, attention_mask.ddtree_bits, scale,
+                               out=out[0], key_lo=getattr(attention_mask, "ddtree_key_lo", None), past_dev=past_dev,
+                               workspace=attention_mask.ddtree_workspace)
+        return out, None
     if attention_mask is None:
         bits, past = causal_bits(T, query.device, window), S - T
     else:

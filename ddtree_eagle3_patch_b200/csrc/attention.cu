@@ -455,7 +455,23 @@ struct Params {
     float* part_lse;
     int* status;
     const int64_t* key_lo;   // sliding window: first visible prefix key per token, or null
+    // Run-time prefix length, or null.  When set, `past` and `n_kt` above
+    // describe the largest prefix the launch covers (the grid is planned for
+    // it) and the kernel reads the actual prefix here, clamped to [0, past]:
+    // CTAs whose key tiles lie past the actual keys exit at once.
+    const int32_t* past_dev;
 };
+
+// Prefix length and key-tile count of this launch (see Params::past_dev).
+__device__ __forceinline__ void runtime_keys(const Params& p, int& past, int& n_kt) {
+    past = p.past;
+    n_kt = p.n_kt;
+    if (p.past_dev) {
+        const int v = __ldg(p.past_dev);
+        past = v < 0 ? 0 : (v > p.past ? p.past : v);
+        n_kt = (past + p.n_tokens + BN - 1) / BN;
+    }
+}
 
 // Barriers; each completes exactly once per CTA.
 enum : int {
@@ -640,8 +656,11 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int split = blockIdx.x, grp = blockIdx.y, g = blockIdx.z;
+    int past, n_kt;
+    runtime_keys(p, past, n_kt);
     const int kt0 = split * p.tpc;
-    const int nj = min(p.tpc, p.n_kt - kt0);     // 1 or 2
+    const int nj = min(p.tpc, n_kt - kt0);       // 1 or 2
+    if (nj <= 0) return;                         // past the run-time keys (whole CTA, before any barrier)
     const int mA = 2 * grp, mB = 2 * grp + 1;
     const bool hasA = mA < p.n_mt, hasB = mB < p.n_mt;
     const bool hasT = grp == p.n_groups - 1 && p.tail_rows > 0;
@@ -703,7 +722,7 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
                 tma_load_3d_hint(vb, &tv, 0, key0, g, &bars[bV0 + j], kv_policy);
                 tma_load_3d_hint(vb + kHalf, &tv, 64, key0, g, &bars[bV0 + j], kv_policy);
             };
-            auto prefix_only = [&](int j) { return (kt0 + j + 1) * BN <= p.past; };
+            auto prefix_only = [&](int j) { return (kt0 + j + 1) * BN <= past; };
             if (leader) {
                 prefetch_tmap(&tk);
                 prefetch_tmap(&tv);
@@ -860,17 +879,17 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
         bool ok = true;
         if (has) {
             const uint32_t* vrow = valid ? p.vis + (int64_t)token * p.vis_words : p.vis;
-            const int lo = kWindow ? row_key_lo(p.key_lo, token, valid, p.past) : 0;
+            const int lo = kWindow ? row_key_lo(p.key_lo, token, valid, past) : 0;
             const float sl2 = p.scale_log2;
             for (int j = 0; j < nj; ++j) {
                 const uint32_t s_col =
                     tmem + lane_addr + (j == 0 ? (slot ? kColB : kColA) : (slot == 0 ? kCol1 : kColT));
                 ok = ok && mbar_wait(&bars[bS0 + 2 * slot + j], 0);
                 tc_fence_after();
-                const int u0 = (kt0 + j) * BN - p.past;
+                const int u0 = (kt0 + j) * BN - past;
                 // tiles reaching into the tree, and under a sliding window the
                 // tiles holding prefix keys before this row's first visible one
-                const bool masked = u0 + BN > 0 || (kWindow && u0 + p.past < lo);
+                const bool masked = u0 + BN > 0 || (kWindow && u0 + past < lo);
                 uint32_t r[4][32];
                 uint32_t vb[4];
                 if (ok) {
@@ -880,7 +899,7 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
                     for (int q = 0; q < 4; ++q)
                         vb[q] = !masked ? 0xffffffffu
                                 : kWindow ? vis_bits(vrow, p.vis_words, u0 + q * 32, p.n_tokens, valid) &
-                                                window_bits(p.past + u0 + q * 32, lo, p.past)
+                                                window_bits(past + u0 + q * 32, lo, past)
                                           : vis_bits(vrow, p.vis_words, u0 + q * 32, p.n_tokens, valid);
                     tmem_wait_ld();
                 }
@@ -1025,14 +1044,14 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
                 float sc[4];
 #pragma unroll
                 for (int r = 0; r < 4; ++r) sc[r] = j ? sc1[r] : sc0[r];
-                const int u = (kt0 + j) * BN + k - p.past;
+                const int u = (kt0 + j) * BN + k - past;
 #pragma unroll
                 for (int r = 0; r < 4; ++r) {
                     bool vis = false;
                     if (r < nt && ok) {
                         const int token = p.tail_token0 + r / p.group;
                         if (u < 0)
-                            vis = !kWindow || (int64_t)(u + p.past) >= __ldg(p.key_lo + token);
+                            vis = !kWindow || (int64_t)(u + past) >= __ldg(p.key_lo + token);
                         else if (u < p.n_tokens)
                             vis = (__ldg(p.vis + (int64_t)token * p.vis_words + (u >> 5)) >> (u & 31)) & 1u;
                     }
@@ -1153,9 +1172,16 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
 template <int CHUNK>
 __global__ void __launch_bounds__(128)
 combine_kernel(const __nv_bfloat16* __restrict__ part_o, const float* __restrict__ part_lse, int splits, int hkv,
-               int group, int n_tokens, __nv_bfloat16* out, int64_t o_stride_tok, int64_t o_stride_head) {
+               int group, int n_tokens, __nv_bfloat16* out, int64_t o_stride_tok, int64_t o_stride_head,
+               const int32_t* past_dev, int past_max, int tpc) {
     griddep_launch_dependents();
     griddep_wait();   // the partials come from the split kernel just before
+    if (past_dev) {   // only the splits that held run-time keys wrote partials
+        const int v = __ldg(past_dev);
+        const int past = v < 0 ? 0 : (v > past_max ? past_max : v);
+        const int n_kt = (past + n_tokens + BN - 1) / BN;
+        splits = min(splits, (n_kt + tpc - 1) / tpc);
+    }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int rows_head = group * n_tokens;
     const int64_t row = (int64_t)blockIdx.x * 4 + warp;
@@ -1279,15 +1305,19 @@ using namespace ddt;
 using namespace ddt::attn;
 
 // Launch of the split kernel (and, with several key splits, the merge).
-static int launch_split(const ddt_attention_args* a, const int64_t* key_lo, const SplitPlan& sp, void* workspace,
-                        size_t workspace_bytes, ddt_stream_t stream) {
+// past_dev (nullable): run-time prefix length; a->past_length is then its
+// upper bound, the grid is planned for it, and the K/V maps span all
+// kv_rows (rows past the run-time tree are masked by the tree bits and hold
+// the caller's finite cache contents, so P = 0 never meets a NaN).
+static int launch_split(const ddt_attention_args* a, const int64_t* key_lo, const int32_t* past_dev,
+                        const SplitPlan& sp, void* workspace, size_t workspace_bytes, ddt_stream_t stream) {
     if (!workspace || workspace_bytes < sp.ws_bytes || reinterpret_cast<uintptr_t>(workspace) % 256)
         return set_error(DDT_EWORKSPACE, "attention workspace needs %zu bytes (256-aligned), got %zu", sp.ws_bytes,
                          workspace_bytes);
     const int64_t group = a->hq / a->hkv;
-    const int64_t kv_len = a->past_length + a->n_tokens;
-    // K/V maps end at past + n_tokens: rows of a larger cache past the tree
-    // read as zeros, so whatever they hold never reaches P.V.
+    const int64_t kv_len = past_dev ? a->kv_rows : a->past_length + a->n_tokens;
+    // Without past_dev the K/V maps end at past + n_tokens: rows of a larger
+    // cache past the tree read as zeros, so whatever they hold never reaches P.V.
     CUtensorMap tq, tqt, tk, tv;
     int rc = make_map(&tq, a->q, HD, a->hq, a->n_tokens, a->q_stride_head * 2, a->q_stride_tok * 2, 64,
                       (uint32_t)group, (uint32_t)sp.tpt);
@@ -1332,6 +1362,7 @@ static int launch_split(const ddt_attention_args* a, const int64_t* key_lo, cons
     q.o_stride_tok = a->o_stride_tok;
     q.o_stride_head = a->o_stride_head;
     q.status = reinterpret_cast<int*>(ws);
+    q.past_dev = past_dev;
     q.part_o = nullptr;
     q.part_lse = nullptr;
     if (sp.splits > 1) {
@@ -1371,7 +1402,8 @@ static int launch_split(const ddt_attention_args* a, const int64_t* key_lo, cons
                   : sp.splits <= 17 ? split::combine_kernel<17>
                                     : split::combine_kernel<16>;
         le = cudaLaunchKernelEx(&cfg, ck, (const __nv_bfloat16*)q.part_o, (const float*)q.part_lse, sp.splits,
-                                (int)a->hkv, sp.group, (int)a->n_tokens, q.out, a->o_stride_tok, a->o_stride_head);
+                                (int)a->hkv, sp.group, (int)a->n_tokens, q.out, a->o_stride_tok, a->o_stride_head,
+                                past_dev, (int)a->past_length, sp.tpc);
         if (le != cudaSuccess) return set_error(DDT_ECUDA, "split_combine_kernel: %s", cudaGetErrorString(le));
         rc = check_launch("split_combine_kernel");
     }
@@ -1387,8 +1419,8 @@ extern "C" size_t ddt_tree_attention_workspace_size(int64_t n_tokens, int64_t hq
     return sp.usable && sp.ws_bytes > a ? sp.ws_bytes : a;
 }
 
-static int tree_attention_impl(const ddt_attention_args* a, const int64_t* key_lo, void* workspace,
-                               size_t workspace_bytes, ddt_stream_t stream) {
+static int tree_attention_impl(const ddt_attention_args* a, const int64_t* key_lo, const int32_t* past_dev,
+                               void* workspace, size_t workspace_bytes, ddt_stream_t stream) {
     if (!a) return set_error(DDT_EINVAL, "args is null");
     if (!a->q || !a->k || !a->v || !a->out || !a->visibility) return set_error(DDT_EINVAL, "null tensor pointer");
     if (a->head_dim != HD) return set_error(DDT_EUNSUPPORTED, "head_dim %lld (only 128)", (long long)a->head_dim);
@@ -1410,12 +1442,21 @@ static int tree_attention_impl(const ddt_attention_args* a, const int64_t* key_l
         return set_error(DDT_EINVAL, "strides must be multiples of 8 elements");
     int dev = 0;
     cudaGetDevice(&dev);
+    const SplitPlan sp = plan_split(a->n_tokens, a->hq, a->hkv, a->past_length, ddt_sm_count(dev));
+    if (past_dev) {
+        if (reinterpret_cast<uintptr_t>(past_dev) % alignof(int32_t))
+            return set_error(DDT_EINVAL, "past_dev must be 4-byte aligned");
+        if (!sp.usable)
+            return set_error(DDT_EUNSUPPORTED, "a run-time prefix needs the split kernel: %lld rows x %lld KV heads "
+                             "at prefix <= %lld do not fit it", (long long)(a->n_tokens * group),
+                             (long long)a->hkv, (long long)a->past_length);
+        return launch_split(a, key_lo, past_dev, sp, workspace, workspace_bytes, stream);
+    }
     const Plan pl = plan_for(a->n_tokens, a->hq, a->hkv, a->past_length, ddt_sm_count(dev));
     if (!workspace || workspace_bytes < pl.ws_bytes || reinterpret_cast<uintptr_t>(workspace) % 256)
         return set_error(DDT_EWORKSPACE, "attention workspace needs %zu bytes (256-aligned), got %zu", pl.ws_bytes,
                          workspace_bytes);
-    const SplitPlan sp = plan_split(a->n_tokens, a->hq, a->hkv, a->past_length, ddt_sm_count(dev));
-    if (sp.usable) return launch_split(a, key_lo, sp, workspace, workspace_bytes, stream);
+    if (sp.usable) return launch_split(a, key_lo, nullptr, sp, workspace, workspace_bytes, stream);
     CUtensorMap tq, tk, tv;
     int rc = make_map(&tq, a->q, HD, a->hq, a->n_tokens, a->q_stride_head * 2, a->q_stride_tok * 2, 64,
                       (uint32_t)group, (uint32_t)pl.tpt);
@@ -1475,12 +1516,20 @@ static int tree_attention_impl(const ddt_attention_args* a, const int64_t* key_l
 
 extern "C" int ddt_tree_attention(const ddt_attention_args* a, void* workspace, size_t workspace_bytes,
                                   ddt_stream_t stream) {
-    return tree_attention_impl(a, nullptr, workspace, workspace_bytes, stream);
+    return tree_attention_impl(a, nullptr, nullptr, workspace, workspace_bytes, stream);
 }
 
 extern "C" int ddt_tree_attention_window(const ddt_attention_args* a, const int64_t* key_lo, void* workspace,
                                          size_t workspace_bytes, ddt_stream_t stream) {
     if (!key_lo) return set_error(DDT_EINVAL, "key_lo is null");
     if (reinterpret_cast<uintptr_t>(key_lo) % alignof(int64_t)) return set_error(DDT_EINVAL, "key_lo must be 8-byte aligned");
-    return tree_attention_impl(a, key_lo, workspace, workspace_bytes, stream);
+    return tree_attention_impl(a, key_lo, nullptr, workspace, workspace_bytes, stream);
+}
+
+extern "C" int ddt_tree_attention_dev(const ddt_attention_args* a, const int64_t* key_lo, const int32_t* past_dev,
+                                      void* workspace, size_t workspace_bytes, ddt_stream_t stream) {
+    if (!past_dev) return set_error(DDT_EINVAL, "past_dev is null");
+    if (key_lo && reinterpret_cast<uintptr_t>(key_lo) % alignof(int64_t))
+        return set_error(DDT_EINVAL, "key_lo must be 8-byte aligned");
+    return tree_attention_impl(a, key_lo, past_dev, workspace, workspace_bytes, stream);
 }

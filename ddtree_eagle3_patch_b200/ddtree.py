@@ -378,167 +378,303 @@ def ddtree_generate(model, target, input_ids: torch.Tensor, mask_token_id: int, 
     accepted rows of the target's context features; one launch compacts
     every layer's K and V.  The accepted count stays on the device until the
     round's single host read, which also returns the new tokens for the stop
-    check.  Stage times come from CUDA events (``stage_times`` has the
-    reference's keys; the fused tree kernel's time is booked to
-    ``tree_build``, its three sub-stages read 0, and ``tree_compile`` is the
-    host time to describe the tree mask).
+    check.
+
+    From the third round on, the draft forward and the verify forward are
+    replayed from CUDA graphs captured once per call: both caches append at
+    a device-side row offset and the attention reads the prefix length from
+    the device, so one capture serves every round (set DDTREE_EAGER=1 to run
+    every round eagerly).  The graphs need this package's DFlashDraftModel
+    (other draft classes run eagerly), a target without sliding-window
+    layers, and a node budget of at least ``block_size - 1``.
+
+    Stage times come from CUDA events (``stage_times`` has the reference's
+    keys; the fused tree kernel's time is booked to ``tree_build``, its three
+    sub-stages read 0, and ``tree_compile`` is the host time to describe the
+    tree mask).
     """
     if block_size <= 1:
         return _target_only_generate(model, target, input_ids, mask_token_id, max_new_tokens, block_size,
                                      stop_token_ids, temperature)
-    from .cache import TreeAppendCache
-    from .model import apply_final_logit_softcapping, extract_context_feature
-    from .runtime import (EventClock, Readback, TreeMask, compact_on_device, device_sample_seed,
-                          tree_attention_for)
-
-    device = model.device
-    num_input_tokens = input_ids.shape[1]
-    max_length = num_input_tokens + max_new_tokens
-    draft_horizon = block_size - 1
-    tree_budget = draft_horizon if tree_budget is None else max(int(tree_budget), 0)
-    max_tree_nodes = 1 + tree_budget
-    vocab = target.lm_head.weight.shape[0] if hasattr(target, "lm_head") else target.config.vocab_size
-
-    output_ids = torch.full((1, max_length + max_tree_nodes), mask_token_id, dtype=torch.long, device=device)
-    position_ids = torch.arange(output_ids.shape[1], device=device).unsqueeze(0)
-    stop_ids = None if stop_token_ids is None else set(int(t) for t in stop_token_ids)
-    layer_types, sliding_window = detect_hybrid_attention(target)
-
-    target_cache = TreeAppendCache(max_length + max_tree_nodes + 1, config=target.config)
-    draft_cache = TreeAppendCache(max_length + max_tree_nodes + block_size + 1, config=model.config)
-    tree = kernels.DeviceTree.allocate(draft_horizon, vocab, tree_budget, device)
-    accepted = torch.zeros((max_tree_nodes,), dtype=torch.int64, device=device)
-    accept_info = torch.zeros((2,), dtype=torch.int64, device=device)
-    posterior = torch.empty((max_tree_nodes,), dtype=torch.int64, device=device)
-    tree_mask = TreeMask(target.dtype, device)
-    readback = Readback(4 + 6 * max_tree_nodes, device)
-    tables: dict = {}
-    seed = device_sample_seed() if temperature >= 1e-5 else 0
-
-    stage_times = empty_stage_times(DDTREE_STAGE_ORDER + DDTREE_TREE_BUILD_STAGE_ORDER)
-    clock = EventClock(device)
-    hidden_buf = None
-
+    from .runtime import tree_attention_for
     with tree_attention_for(target):
+        dec = _DDTreeDecoder(model, target, input_ids, mask_token_id, max_new_tokens, block_size, stop_token_ids,
+                             temperature, tree_budget, save_tree_traces)
+        return dec.run()
+
+
+class _DDTreeDecoder:
+    """State of one ddtree_generate call (buffers, caches, captured forwards)."""
+
+    def __init__(self, model, target, input_ids, mask_token_id, max_new_tokens, block_size, stop_token_ids,
+                 temperature, tree_budget, save_tree_traces):
+        import os
+        from .cache import TreeAppendCache
+        from .model import DFlashDraftModel
+        from .runtime import EventClock, Readback, TreeMask, device_sample_seed
+        self.model, self.target = model, target
+        self.device = device = model.device
+        self.P = input_ids.shape[1]
+        self.input_ids = input_ids
+        self.max_length = self.P + max_new_tokens
+        self.block = block_size
+        self.L = block_size - 1
+        self.budget = self.L if tree_budget is None else max(int(tree_budget), 0)
+        self.max_nodes = 1 + self.budget
+        self.mask_token_id = mask_token_id
+        self.temperature = temperature
+        self.traces = save_tree_traces
+        self.vocab = target.lm_head.weight.shape[0] if hasattr(target, "lm_head") else target.config.vocab_size
+        self.stop_ids = None if stop_token_ids is None else set(int(t) for t in stop_token_ids)
+        self.layer_types, self.window = detect_hybrid_attention(target)
+        self.output_ids = torch.full((1, self.max_length + self.max_nodes), mask_token_id, dtype=torch.long,
+                                     device=device)
+        self.position_ids = torch.arange(self.output_ids.shape[1], device=device).unsqueeze(0)
+        self.target_cache = TreeAppendCache(self.max_length + self.max_nodes + 1, config=target.config)
+        self.draft_cache = TreeAppendCache(self.max_length + self.max_nodes + block_size + 1, config=model.config)
+        self.tree = kernels.DeviceTree.allocate(self.L, self.vocab, self.budget, device)
+        self.accepted = torch.zeros((self.max_nodes,), dtype=torch.int64, device=device)
+        self.accept_info = torch.zeros((2,), dtype=torch.int64, device=device)
+        self.posterior = torch.empty((self.max_nodes,), dtype=torch.int64, device=device)
+        self.tree_mask = TreeMask(target.dtype, device)
+        self.readback = Readback(4 + 6 * self.max_nodes, device)
+        self.tables: dict = {}
+        self.seed = device_sample_seed() if temperature >= 1e-5 else 0
+        self.clock = EventClock(device)
+        self.hidden_buf = None
+        # static (device-length) mode: round state [start, ctx_offset, ctx_count, 0]
+        self.rs_host = torch.zeros((4,), dtype=torch.int32, pin_memory=True)
+        self.rs = torch.zeros((4,), dtype=torch.int32, device=device)
+        self.static = (isinstance(model, DFlashDraftModel) and self.window is None
+                       and self.budget >= self.L and os.environ.get("DDTREE_EAGER", "0") != "1")
+        self.graphs = None
+        self.graph_kernels = (0, 0)
+        self.replays = 0
+        self.n_nodes = tree_node_count(self.budget, self.L, self.vocab)
+        self.N = 1 + self.n_nodes
+
+    # ------------------------------------------------------------------ setup
+    def _setup_static(self, features: torch.Tensor) -> None:
+        """After the prefill: both caches switch to device-offset appends and
+        the attention workspace is sized for the longest prefix."""
+        t, d = self.target.config, self.model.config
+        hq_t, hkv_t = t.num_attention_heads, t.num_key_value_heads
+        hq_d, hkv_d = d.num_attention_heads, d.num_key_value_heads
+        self.past_max_t = self.target_cache.capacity - self.N
+        self.past_max_d = self.draft_cache.capacity - self.block
+        ws_t = kernels.attention_workspace(self.N, hq_t, hkv_t, self.past_max_t, self.device)
+        ws_d = kernels.attention_workspace(self.block, hq_d, hkv_d, self.past_max_d, self.device)
+        self.att_ws = ws_t if ws_t.numel() >= ws_d.numel() else ws_d
+        self.target_cache.set_static(self.rs[0:1])
+        self.draft_cache.set_static(self.rs[0:1])
+        self.ar_block = torch.arange(self.block, device=self.device)
+        self.block_buf = torch.empty((1, self.block), dtype=torch.long, device=self.device)
+        self.static_mask = self.tree_mask.static(self.tree.visibility[: self.N], self.rs[0:1], self.past_max_t,
+                                                 self.N, self.att_ws)
+
+    def _set_round_state(self, start: int, ctx_offset: int, ctx_count: int) -> None:
+        self.rs_host[0], self.rs_host[1], self.rs_host[2] = start, ctx_offset, ctx_count
+        self.rs.copy_(self.rs_host, non_blocking=True)
+
+    # ------------------------------------------------------------------ stages
+    def _draft_generic(self, start: int, target_hidden: torch.Tensor) -> torch.Tensor:
+        from .model import apply_final_logit_softcapping
+        block = self.output_ids[:, start: start + self.block]
+        noise = self.target.model.embed_tokens(block)
+        h = self.model(target_hidden=target_hidden, noise_embedding=noise,
+                       position_ids=self.position_ids[:, self.draft_cache.get_seq_length(): start + self.block],
+                       past_key_values=self.draft_cache, use_cache=True, is_causal=False)
+        logits = self.target.lm_head(h[:, -self.L:, :])
+        logits = apply_final_logit_softcapping(logits, self.model.final_logit_softcapping)
+        self.draft_cache.crop(start)
+        return logits
+
+    def _draft_static(self, ctx_hidden: torch.Tensor) -> torch.Tensor:
+        """Draft logits with every length read from ``self.rs`` (capturable)."""
+        from .model import apply_final_logit_softcapping
+        C = ctx_hidden.shape[1]
+        start = self.rs[0:1].long()
+        self.block_buf.copy_(self.output_ids[:, start + self.ar_block])
+        noise = self.target.model.embed_tokens(self.block_buf)
+        ar_c = self.ar_block if C == self.block else torch.arange(C, device=self.device)
+        pos = torch.cat([self.rs[1:2].long() + ar_c, start + self.ar_block]).unsqueeze(0)
+        h = self.model.forward_static(noise, ctx_hidden, pos, self.draft_cache, self.rs, self.past_max_d, self.att_ws)
+        logits = self.target.lm_head(h[:, -self.L:, :])
+        return apply_final_logit_softcapping(logits, self.model.final_logit_softcapping)
+
+    def _verify(self, start: int, mask):
+        from .model import extract_context_feature
+        out = self.target(self.tree.verify_ids[: self.N].unsqueeze(0),
+                          position_ids=self.tree.verify_pos[: self.N].unsqueeze(0), attention_mask=mask,
+                          past_key_values=self.target_cache, use_cache=True, output_hidden_states=True)
+        return out.logits, extract_context_feature(out.hidden_states, self.model.target_layer_ids)
+
+    def _capture(self, ctx_hidden: torch.Tensor) -> None:
+        """Capture the draft and verify forwards (after an eager round of the
+        same shapes has warmed every path)."""
+        from ._lib import load
+        lib = load()
+        pool = torch.cuda.graph_pool_handle()
+        gd, gv = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        n0 = lib.ddt_launch_count()
+        with torch.cuda.graph(gd, pool=pool):
+            draft_logits = self._draft_static(ctx_hidden)
+        n1 = lib.ddt_launch_count()
+        with torch.cuda.graph(gv, pool=pool):
+            logits, features = self._verify(0, self.static_mask)
+        n2 = lib.ddt_launch_count()
+        # this library's kernels inside each graph (counted once, at capture)
+        self.graph_kernels = (n1 - n0, n2 - n1)
+        self.graphs = (gd, gv, draft_logits, logits, features)
+
+    # ------------------------------------------------------------------ loop
+    def run(self) -> SimpleNamespace:
+        from ._lib import load
+        from .model import extract_context_feature
+        dev, clock = self.device, self.clock
+        launches0 = load().ddt_launch_count()
+        stage_times = empty_stage_times(DDTREE_STAGE_ORDER + DDTREE_TREE_BUILD_STAGE_ORDER)
+        P = self.P
         ev_prefill = clock.mark()
-        output = target(input_ids, position_ids=position_ids[:, :num_input_tokens], past_key_values=target_cache,
-                        use_cache=True, logits_to_keep=1, output_hidden_states=True)
-        output_ids[:, :num_input_tokens] = input_ids
-        output_ids[:, num_input_tokens: num_input_tokens + 1] = kernels.sample(output.logits, temperature)
-        target_hidden = extract_context_feature(output.hidden_states, model.target_layer_ids)
+        output = self.target(self.input_ids, position_ids=self.position_ids[:, :P], past_key_values=self.target_cache,
+                             use_cache=True, logits_to_keep=1, output_hidden_states=True)
+        self.output_ids[:, :P] = self.input_ids
+        self.output_ids[:, P: P + 1] = kernels.sample(output.logits, self.temperature)
+        target_hidden = extract_context_feature(output.hidden_states, self.model.target_layer_ids)
+        self.hidden_buf = torch.zeros((self.max_nodes, target_hidden.shape[-1]), dtype=target_hidden.dtype,
+                                      device=dev)
+        if self.static:
+            self._setup_static(target_hidden)
         ev_first = clock.mark()
 
         ev_decode = clock.mark()
         ev_round_clock = ev_decode
-        start = num_input_tokens
-        acceptance_lengths, round_ends = [], []
-        round_trees = [] if save_tree_traces else None
-        draft_prefill = True
-        rnd = 0
-        while start < max_length:
+        start, count, rnd = P, P, 0
+        acceptance, round_ends = [], []
+        round_trees = [] if self.traces else None
+        N, n_nodes = self.N, self.n_nodes
+        while start < self.max_length:
             ev0 = clock.mark()
-            block = output_ids[:, start: start + block_size]
-            noise_embedding = target.model.embed_tokens(block)
-            draft_hidden = model(target_hidden=target_hidden, noise_embedding=noise_embedding,
-                                 position_ids=position_ids[:, draft_cache.get_seq_length(): start + block_size],
-                                 past_key_values=draft_cache, use_cache=True, is_causal=False)
-            draft_logits = target.lm_head(draft_hidden[:, -draft_horizon:, :])
-            draft_logits = apply_final_logit_softcapping(draft_logits, model.final_logit_softcapping)
-            draft_cache.crop(start)
+            if self.static:
+                self._set_round_state(start, start - count, count)
+                if rnd == 0:
+                    draft_logits = self._draft_static(target_hidden)
+                elif self.graphs is None:
+                    draft_logits = self._draft_static(self.hidden_buf[None, : self.block])
+                else:
+                    self.graphs[0].replay()
+                    self.replays += 1
+                    draft_logits = self.graphs[2]
+            else:
+                draft_logits = self._draft_generic(start, target_hidden)
             ev1 = clock.mark()
-            if draft_prefill:
-                draft_prefill = False
+            if rnd == 0:
                 ev_decode = ev1
             else:
                 clock.span("draft", ev0, ev1)
 
-            rows = draft_logits.shape[1]
-            kernels.tree_build(draft_logits[0], tree_budget, root_token=output_ids[0, start: start + 1],
-                               start=start, out=tree)
-            n_nodes = tree_node_count(tree_budget, rows, draft_logits.shape[-1])
-            N = 1 + n_nodes
+            root = self.block_buf[0, 0:1] if self.static else self.output_ids[0, start: start + 1]
+            kernels.tree_build(draft_logits[0], self.budget, root_token=root, start=start, out=self.tree)
             ev2 = clock.mark()
             clock.span("tree_build", ev1, ev2)
 
-            bits = tree.visibility[:N]
-            mask = tree_mask(bits, start, N)
-            if sliding_window is not None:
-                key_lo = sliding_key_lo(tree.verify_pos[:N], sliding_window)
-                mask = {"full_attention": mask, "sliding_attention": tree_mask(bits, start, N, key_lo)}
+            bits = self.tree.visibility[:N]
+            if self.static:
+                mask = self.static_mask
+            else:
+                mask = self.tree_mask(bits, start, N)
+                if self.window is not None:
+                    key_lo = sliding_key_lo(self.tree.verify_pos[:N], self.window)
+                    mask = {"full_attention": mask, "sliding_attention": self.tree_mask(bits, start, N, key_lo)}
             ev3 = clock.mark()
             clock.span("tree_compile", ev2, ev3)
 
-            output = target(tree.verify_ids[:N].unsqueeze(0), position_ids=tree.verify_pos[:N].unsqueeze(0),
-                            attention_mask=mask, past_key_values=target_cache, use_cache=True,
-                            output_hidden_states=True)
+            if self.graphs is not None:
+                self.graphs[1].replay()
+                logits, features = self.graphs[3], self.graphs[4]
+            else:
+                logits, features = self._verify(start, mask)
             ev4 = clock.mark()
             clock.span("verify", ev3, ev4)
 
-            logits = output.logits[0]
-            if temperature < 1e-5:
-                kernels.tree_accept(logits, tree.parents, tree.node_token_ids, tree.info, max_accept=N,
-                                    accepted=accepted[:N], accept_info=accept_info, posterior=posterior[:N])
-            else:
-                post = kernels.sample_rows(logits, temperature, seed, rnd)
-                acc_t, info_t = kernels.tree_walk(post, tree.parents, tree.node_token_ids, tree.info, max_accept=N)
-                accepted[:N].copy_(acc_t)
-                accept_info.copy_(info_t)
-            features = extract_context_feature(output.hidden_states, model.target_layer_ids)
-            if hidden_buf is None or hidden_buf.shape[-1] != features.shape[-1]:
-                hidden_buf = torch.empty((max_tree_nodes, features.shape[-1]), dtype=features.dtype, device=device)
-            kernels.tree_commit(tree.verify_ids[:N], accepted[:N], accept_info, output_ids[0], start,
-                                hidden=features[0], hidden_out=hidden_buf[:N])
-            compact_on_device(target_cache, start, N, accepted, accept_info[:1], N, tables)
-            pieces = [(accept_info, 2), (output_ids[0, start:], N + 1)]
-            if save_tree_traces:
-                pieces += [(accepted, N), (tree.node_token_ids, n_nodes), (tree.node_depths, n_nodes),
-                           (tree.parents.to(torch.int64), N)]
-            got = readback.fetch(pieces)
+            count = self._accept_commit(logits[0], features[0], start, rnd)
+            got = self._fetch(start, count)
             count, new_tokens = int(got[0][0]), got[1][: int(got[0][0]) + 1]
-            target_cache.crop(start + count)
-            target_hidden = hidden_buf[None, :count]
-            acceptance_lengths.append(count)
-            start += count
+            if not self.static:
+                self.target_cache.crop(start + count)
+            target_hidden = self.hidden_buf[None, :count]
+            acceptance.append(count)
             ev5 = clock.mark()
             clock.span("commit", ev4, ev5)
             round_ends.append(ev5)
-            if save_tree_traces:
+            if self.traces:
                 parents = [int(p) for p in got[5]]
                 parents[0] = -1
                 round_trees.append({
                     "accepted_indices": [int(i) for i in got[2][:count]],
                     "tree": {"node_token_ids": [int(t) for t in got[3]], "node_depths": [int(d) for d in got[4]],
                              "parents": parents}})
+            start += count
             rnd += 1
-            if stop_ids is not None and any(t in stop_ids for t in new_tokens):
+            if self.static and rnd == 2 and self.graphs is None and start < self.max_length:
+                self._capture(self.hidden_buf[None, : self.block])
+            if self.stop_ids is not None and any(t in self.stop_ids for t in new_tokens):
                 break
-
         ev_end = clock.mark()
 
-    output_ids = output_ids[:, :max_length]
-    output_ids = output_ids[:, output_ids[0] != mask_token_id]
-    if stop_ids is not None:
-        gen = output_ids[0, num_input_tokens:].tolist()
-        for i, t in enumerate(gen):
-            if t in stop_ids:
-                output_ids = output_ids[:, : num_input_tokens + i + 1]
-                break
-    num_output_tokens = output_ids.shape[1] - num_input_tokens
-    clock.resolve(stage_times)
-    total_decode_time = EventClock.seconds(ev_decode, ev_end)
-    return SimpleNamespace(
-        output_ids=output_ids.cpu(),
-        num_input_tokens=num_input_tokens,
-        num_output_tokens=num_output_tokens,
-        time_to_first_token=EventClock.seconds(ev_prefill, ev_first),
-        time_per_output_token=total_decode_time / max(num_output_tokens, 1),
-        acceptance_lengths=acceptance_lengths,
-        decode_rounds=len(acceptance_lengths),
-        stage_times=stage_times,
-        round_timestamps=[EventClock.seconds(ev_round_clock, e) for e in round_ends],
-        round_trees=round_trees,
-    )
+        output_ids = self.output_ids[:, : self.max_length]
+        output_ids = output_ids[:, output_ids[0] != self.mask_token_id]
+        if self.stop_ids is not None:
+            for i, t in enumerate(output_ids[0, P:].tolist()):
+                if t in self.stop_ids:
+                    output_ids = output_ids[:, : P + i + 1]
+                    break
+        num_output_tokens = output_ids.shape[1] - P
+        clock.resolve(stage_times)
+        total_decode_time = clock.seconds(ev_decode, ev_end)
+        self.graphs = None
+        # kernels of this library run by the call: eager launches plus every
+        # replay of the captured ones
+        native = load().ddt_launch_count() - launches0 + self.replays * sum(self.graph_kernels) - \
+            sum(self.graph_kernels)
+        return SimpleNamespace(
+            output_ids=output_ids.cpu(),
+            num_input_tokens=P,
+            num_output_tokens=num_output_tokens,
+            time_to_first_token=clock.seconds(ev_prefill, ev_first),
+            time_per_output_token=total_decode_time / max(num_output_tokens, 1),
+            acceptance_lengths=acceptance,
+            decode_rounds=len(acceptance),
+            stage_times=stage_times,
+            round_timestamps=[clock.seconds(ev_round_clock, e) for e in round_ends],
+            round_trees=round_trees,
+            native_launches=int(native),
+            graph_rounds=self.replays,
+        )
 
+    def _accept_commit(self, logits: torch.Tensor, features: torch.Tensor, start: int, rnd: int) -> None:
+        from .runtime import compact_on_device
+        N = self.N
+        if self.temperature < 1e-5:
+            kernels.tree_accept(logits, self.tree.parents, self.tree.node_token_ids, self.tree.info, max_accept=N,
+                                accepted=self.accepted[:N], accept_info=self.accept_info, posterior=self.posterior[:N])
+        else:
+            post = kernels.sample_rows(logits, self.temperature, self.seed, rnd)
+            acc_t, info_t = kernels.tree_walk(post, self.tree.parents, self.tree.node_token_ids, self.tree.info,
+                                              max_accept=N)
+            self.accepted[:N].copy_(acc_t)
+            self.accept_info.copy_(info_t)
+        kernels.tree_commit(self.tree.verify_ids[:N], self.accepted[:N], self.accept_info, self.output_ids[0], start,
+                            hidden=features, hidden_out=self.hidden_buf[:N])
+        compact_on_device(self.target_cache, start, N, self.accepted, self.accept_info[:1], N, self.tables)
+
+    def _fetch(self, start: int, _count) -> list:
+        N, n = self.N, self.n_nodes
+        pieces = [(self.accept_info, 2), (self.output_ids[0, start:], N + 1)]
+        if self.traces:
+            pieces += [(self.accepted, N), (self.tree.node_token_ids, n), (self.tree.node_depths, n),
+                       (self.tree.parents.to(torch.int64), N)]
+        return self.readback.fetch(pieces)
 
 DFLASH_STAGE_ORDER = ("draft", "verify", "commit")
 

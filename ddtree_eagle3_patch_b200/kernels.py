@@ -139,7 +139,8 @@ _ATT_WS: dict = {}
 
 
 def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, past_length: int, visibility: torch.Tensor,
-                   scale: float, out: torch.Tensor | None = None, key_lo: torch.Tensor | None = None) -> torch.Tensor:
+                   scale: float, out: torch.Tensor | None = None, key_lo: torch.Tensor | None = None,
+                   past_dev: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
     """Kernel (2): one layer of tree-masked attention.
 
     q [n_tokens, hq, 128], k / v [hkv, kv_rows, 128] (bf16, last dim
@@ -149,6 +150,12 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, past_lengt
     ``key_lo`` (int64 [n_tokens] on the device) makes it a sliding-window
     layer: row t then sees prefix key j only if j >= key_lo[t]
     (``ddt_tree_attention_window``; see ``ddtree.sliding_key_lo``).
+
+    ``past_dev`` (int32 device scalar) makes the prefix length a run-time
+    value (``ddt_tree_attention_dev``): ``past_length`` is then its upper
+    bound, and one captured launch serves any prefix up to it.  ``workspace``
+    (uint8, 256-aligned) is the caller's own scratch, needed when the launch
+    is captured into a graph that must outlive the shared scratch.
 
     Called once per layer, so the host work is kept to one read of each
     tensor's shape and strides; the C entry point checks the rest."""
@@ -160,7 +167,7 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, past_lengt
         for t, n in ((q, "q"), (k, "k"), (v, "v"), (visibility, "visibility")):
             require_cuda(t, n)
     if q.dtype == torch.float32 and k.dtype == torch.float32 and v.dtype == torch.float32:
-        return tree_attention_f32(q, k, v, past_length, visibility, scale, out=out, key_lo=key_lo)
+        return tree_attention_f32(q, k, v, past_length, visibility, scale, out=out, key_lo=key_lo, past_dev=past_dev)
     if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
         raise TypeError("q, k, v must all be bf16 (tensor-core path) or all float32")
     qs, ks = q.stride(), k.stride()
@@ -177,18 +184,30 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, past_lengt
         visibility = visibility.contiguous()
     dev_index = q.get_device()
     past_length = int(past_length)
-    key = (n_tokens, hq, hkv, past_length, dev_index)
-    ws = _ATT_WS.get(key)
     lib = _lib.load()
-    if ws is None or ws[0] is not WORKSPACES.current("attention", dev_index):
-        ws_bytes = lib.ddt_tree_attention_workspace_size(n_tokens, hq, hkv, past_length, dev_index)
-        buf = WORKSPACES.get("attention", q.device, ws_bytes)
-        ws = (buf, buf.data_ptr(), buf.numel())
-        _ATT_WS[key] = ws
+    if workspace is not None:
+        ws = (workspace, workspace.data_ptr(), workspace.numel())
+    else:
+        key = (n_tokens, hq, hkv, past_length, dev_index)
+        ws = _ATT_WS.get(key)
+        if ws is None or ws[0] is not WORKSPACES.current("attention", dev_index):
+            ws_bytes = lib.ddt_tree_attention_workspace_size(n_tokens, hq, hkv, past_length, dev_index)
+            buf = WORKSPACES.get("attention", q.device, ws_bytes)
+            ws = (buf, buf.data_ptr(), buf.numel())
+            _ATT_WS[key] = ws
     os_ = out.stride()
     a = AttentionArgs(q.data_ptr(), qs[0], qs[1], k.data_ptr(), v.data_ptr(), ks[0], ks[1], kv_rows, out.data_ptr(),
                       os_[0], os_[1], n_tokens, hq, hkv, d, past_length, visibility.data_ptr(),
                       visibility.shape[1], float(scale))
+    if past_dev is not None:
+        if not past_dev.is_cuda or past_dev.dtype != torch.int32:
+            raise ValueError("past_dev must be an int32 CUDA tensor")
+        if key_lo is not None and (not key_lo.is_cuda or key_lo.dtype != torch.int64 or not key_lo.is_contiguous()
+                                   or key_lo.numel() < n_tokens):
+            raise ValueError("key_lo must be a contiguous int64 CUDA tensor with one entry per token")
+        check(lib.ddt_tree_attention_dev(ctypes.byref(a), ptr(key_lo), past_dev.data_ptr(), ws[1], ws[2],
+                                         _lib.raw_stream(dev_index)), "ddt_tree_attention_dev")
+        return out
     if key_lo is None:
         check(lib.ddt_tree_attention(ctypes.byref(a), ws[1], ws[2], _lib.raw_stream(dev_index)), "ddt_tree_attention")
         return out
@@ -237,10 +256,47 @@ def tree_attention_f32(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, past_l
     return out
 
 
-def attention_status(device: torch.device) -> int:
-    """Device-side status word of the attention kernel (0 = no bounded wait ran out)."""
-    ws = WORKSPACES.get("attention", device, 256)
+def attention_workspace(n_tokens: int, hq: int, hkv: int, max_past: int, device: torch.device) -> torch.Tensor:
+    """A caller-owned, zero-filled attention workspace for prefixes up to
+    ``max_past`` (status word first)."""
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    n = _lib.load().ddt_tree_attention_workspace_size(int(n_tokens), int(hq), int(hkv), int(max_past), index)
+    return torch.zeros(max(int(n), 256), dtype=torch.uint8, device=device)
+
+
+def attention_status(device: torch.device, workspace: torch.Tensor | None = None) -> int:
+    """Device-side status word of the attention kernel (0 = no bounded wait
+    ran out), of the shared scratch or of a caller's ``workspace``."""
+    ws = WORKSPACES.get("attention", device, 256) if workspace is None else workspace
     return int(ws[:4].view(torch.int32).item())
+
+
+def kv_append(k_src: torch.Tensor, v_src: torch.Tensor, k_dst: torch.Tensor, v_dst: torch.Tensor,
+              offset_dev: torch.Tensor, rows_dev: torch.Tensor | None = None) -> None:
+    """Copy rows [0, rows) of k_src / v_src ([..., heads, rows, dim]) into
+    rows offset .. offset + rows of k_dst / v_dst ([..., heads, capacity,
+    dim]) with the offset (and optionally a row count) read from device
+    int32 scalars (``ddt_kv_append``)."""
+    for t, n in ((k_src, "k_src"), (v_src, "v_src"), (k_dst, "k_dst"), (v_dst, "v_dst"), (offset_dev, "offset")):
+        require_cuda(t, n)
+    if offset_dev.dtype != torch.int32 or (rows_dev is not None and rows_dev.dtype != torch.int32):
+        raise ValueError("offset_dev / rows_dev must be int32")
+    ks = k_src.reshape(-1, k_src.shape[-2], k_src.shape[-1]) if k_src.dim() != 3 else k_src
+    vs = v_src.reshape(-1, v_src.shape[-2], v_src.shape[-1]) if v_src.dim() != 3 else v_src
+    kd = k_dst.reshape(-1, k_dst.shape[-2], k_dst.shape[-1]) if k_dst.dim() != 3 else k_dst
+    vd = v_dst.reshape(-1, v_dst.shape[-2], v_dst.shape[-1]) if v_dst.dim() != 3 else v_dst
+    if ks.stride() != vs.stride() or ks.shape != vs.shape or kd.stride() != vd.stride() or kd.shape != vd.shape:
+        raise ValueError("K and V must share shapes and strides")
+    if ks.shape[0] != kd.shape[0] or ks.shape[-1] != kd.shape[-1] or ks.dtype != kd.dtype:
+        raise ValueError("source and cache heads / head_dim / dtype differ")
+    if ks.stride(-1) != 1 or kd.stride(-1) != 1:
+        raise ValueError("head_dim must be contiguous")
+    e = ks.element_size()
+    rc = _lib.load().ddt_kv_append(ks.data_ptr(), vs.data_ptr(), ks.stride(0) * e, ks.stride(1) * e, kd.data_ptr(),
+                                   vd.data_ptr(), kd.stride(0) * e, kd.stride(1) * e, kd.shape[1], ks.shape[0],
+                                   ks.shape[1], ks.shape[2] * e, offset_dev.data_ptr(), ptr(rows_dev),
+                                   stream_of(ks.device))
+    check(rc, "ddt_kv_append")
 
 
 def tree_accept(logits: torch.Tensor, parents: torch.Tensor, node_token_ids: torch.Tensor,

@@ -144,6 +144,30 @@ class DFlashAttention(nn.Module):
         out = kernels.tree_attention(q[0], k[0], v[0], kv_len - q_len, bits, self.scaling)
         return self.o_proj(out.reshape(1, q_len, self.num_heads * hd))
 
+    def forward_static(self, hidden_states, target_hidden, position_embeddings, cache, rs, past_max: int,
+                       workspace) -> torch.Tensor:
+        """The same attention with every length on the device (a forward
+        that can be captured once and replayed each round).  ``rs`` is an
+        int32 device vector [start, ctx_offset, ctx_count]: the first
+        ctx_count of the context rows go to the draft cache at ctx_offset,
+        the block's rows at start, and the block's queries see the cache's
+        first start rows and every block row."""
+        q_len, ctx_len, hd = hidden_states.shape[1], target_hidden.shape[1], self.head_dim
+        q = self.q_norm(self.q_proj(hidden_states).view(1, q_len, self.num_heads, hd))
+        k = torch.cat([self.k_proj(target_hidden), self.k_proj(hidden_states)], dim=1)
+        v = torch.cat([self.v_proj(target_hidden), self.v_proj(hidden_states)], dim=1)
+        k = self.k_norm(k.view(1, ctx_len + q_len, self.num_kv_heads, hd)).transpose(1, 2)
+        v = v.view(1, ctx_len + q_len, self.num_kv_heads, hd).transpose(1, 2)
+        cos, sin = position_embeddings
+        q = q * cos[:, -q_len:].unsqueeze(2) + rotate_half(q) * sin[:, -q_len:].unsqueeze(2)
+        k = k * cos.unsqueeze(1) + rotate_half(k) * sin.unsqueeze(1)
+        cache.update_at(k[:, :, :ctx_len], v[:, :, :ctx_len], self.layer_idx, rs[1:2], rs[2:3])
+        kf, vf = cache.update_at(k[:, :, ctx_len:], v[:, :, ctx_len:], self.layer_idx, rs[0:1])
+        bits = _all_visible_bits(q_len, q.device)
+        out = kernels.tree_attention(q[0], kf[0], vf[0], past_max, bits, self.scaling, past_dev=rs[0:1],
+                                     workspace=workspace)
+        return self.o_proj(out.reshape(1, q_len, self.num_heads * hd))
+
 
 class DFlashDecoderLayer(nn.Module):
     """Pre-norm attention + MLP block (model/dflash.py:110-150)."""
@@ -158,6 +182,11 @@ class DFlashDecoderLayer(nn.Module):
     def forward(self, hidden_states, target_hidden, position_embeddings, past_key_values=None):
         h = hidden_states + self.self_attn(self.input_layernorm(hidden_states), target_hidden, position_embeddings,
                                            past_key_values)
+        return h + self.mlp(self.post_attention_layernorm(h))
+
+    def forward_static(self, hidden_states, target_hidden, position_embeddings, cache, rs, past_max, workspace):
+        h = hidden_states + self.self_attn.forward_static(self.input_layernorm(hidden_states), target_hidden,
+                                                          position_embeddings, cache, rs, past_max, workspace)
         return h + self.mlp(self.post_attention_layernorm(h))
 
 
@@ -200,4 +229,19 @@ class DFlashDraftModel(Qwen3PreTrainedModel):
         cache = past_key_values if use_cache else None
         for layer in self.layers:
             hidden_states = layer(hidden_states, ctx, position_embeddings, cache)
+        return self.norm(hidden_states)
+
+    def forward_static(self, noise_embedding: torch.Tensor, target_hidden: torch.Tensor, position_ids: torch.Tensor,
+                       cache, rs: torch.Tensor, past_max: int, workspace: torch.Tensor) -> torch.Tensor:
+        """``forward`` with the cache lengths on the device, for a forward
+        captured once and replayed every decode round.  ``cache`` is a
+        TreeAppendCache; ``rs`` the int32 device vector [start, ctx_offset,
+        ctx_count] (see DFlashAttention.forward_static); ``position_ids``
+        cover the context rows then the block rows.  ``past_max`` bounds
+        start."""
+        hidden_states = noise_embedding
+        ctx = self.hidden_norm(self.fc(target_hidden))
+        position_embeddings = self.rotary_emb(hidden_states, position_ids)
+        for layer in self.layers:
+            hidden_states = layer.forward_static(hidden_states, ctx, position_embeddings, cache, rs, past_max, workspace)
         return self.norm(hidden_states)

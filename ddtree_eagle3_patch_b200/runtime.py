@@ -111,6 +111,19 @@ class TreeMask:
             m.ddtree_key_lo = key_lo
         return m
 
+    def static(self, bits: torch.Tensor, past_dev: torch.Tensor, past_max: int, n: int,
+               workspace: torch.Tensor) -> torch.Tensor:
+        """The stand-in for a captured verify forward: the prefix length is
+        the int32 device scalar ``past_dev`` (at most ``past_max``), read by
+        the attention kernel at run time, and the attention uses the
+        caller's ``workspace`` (which the graph keeps alive)."""
+        m = self._zero.expand(1, 1, n, past_max + n)
+        m.ddtree_bits = bits
+        m.ddtree_past_dev = past_dev
+        m.ddtree_past_max = int(past_max)
+        m.ddtree_workspace = workspace
+        return m
+
 
 class Readback:
     """One pinned host buffer per decode call and one event: the round's

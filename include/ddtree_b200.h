@@ -170,6 +170,21 @@ DDT_API int ddt_tree_attention(const ddt_attention_args* args, void* workspace, 
 DDT_API int ddt_tree_attention_window(const ddt_attention_args* args, const int64_t* key_lo, void* workspace,
                               size_t workspace_bytes, ddt_stream_t stream);
 
+/* The same call with the prefix length read from device memory at run time,
+ * so that one captured launch serves every round of a decode loop (the
+ * verify attention of ddtree.py:523-531, and the draft's attention over its
+ * cache, model/dflash.py:89-106, whose prefix grows every round).
+ * args->past_length is the largest prefix the call may see: the launch is
+ * planned for it, kv_rows >= past_length + n_tokens, and *past_dev is clamped
+ * to [0, past_length].  K/V rows past the run-time tree are masked, and must
+ * hold finite values (a zero-filled or previously written cache).  key_lo is
+ * nullable (sliding window as in ddt_tree_attention_window).  Workspace as
+ * for ddt_tree_attention at past_length.  Shapes whose rows do not fit the
+ * split-key kernel (more than 147 128-row tiles x KV heads) return
+ * DDT_EUNSUPPORTED. */
+DDT_API int ddt_tree_attention_dev(const ddt_attention_args* args, const int64_t* key_lo, const int32_t* past_dev,
+                                   void* workspace, size_t workspace_bytes, ddt_stream_t stream);
+
 /* The same attention call for float32 targets (the reference's SDPA in the
  * target's dtype, ddtree.py:523-531): q, k, v and out are float32 with the
  * strides of ddt_attention_args counted in float elements (multiples of 4),
@@ -251,6 +266,20 @@ DDT_API int ddt_tree_commit(const int64_t* verify_ids, int64_t n_rows, const int
 DDT_API int ddt_kv_compact(void* const* tensors, int64_t n_tensors, int64_t heads, int64_t row_bytes,
                    int64_t head_stride_bytes, int64_t row_stride_bytes, int64_t past_length, int64_t cur_len,
                    const int64_t* keep, const int64_t* keep_count_dev, int64_t max_keep, ddt_stream_t stream);
+
+/* Append of new K/V rows into a preallocated cache at a device-side row
+ * offset.  Replaces DynamicCache.update's torch.cat of the whole cache
+ * (transformers cache_utils.py DynamicLayer.update, reached from the verify
+ * forward at ddtree.py:523-531 and the draft at ddtree.py:478-486): for every
+ * head h < heads and row r < rows (r < *rows_dev when rows_dev is given),
+ *   dst row (*offset_dev + r) of head h <- src row r of head h,
+ * for K and V; destination rows outside [0, dst_rows) are skipped.  Strides
+ * in bytes; pointers, strides and row_bytes multiples of 16. */
+DDT_API int ddt_kv_append(const void* k_src, const void* v_src, int64_t src_head_stride_bytes,
+                          int64_t src_row_stride_bytes, void* k_dst, void* v_dst, int64_t dst_head_stride_bytes,
+                          int64_t dst_row_stride_bytes, int64_t dst_rows, int64_t heads, int64_t rows,
+                          int64_t row_bytes, const int32_t* offset_dev, const int32_t* rows_dev /* nullable */,
+                          ddt_stream_t stream);
 
 /* ---------------------------------------------------------------------------
  * EAGLE3 path acceptance.  Replaces evaluate_eagle3_posterior

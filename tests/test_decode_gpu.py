@@ -54,9 +54,13 @@ def test_fixture_models_rebuild_on_cpu(decode_golden):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("eager", ["0", "1"], ids=["graphs", "eager"])
 @pytest.mark.parametrize("name", [c[0] for c in C.CASES])
-def test_ddtree_generate_matches_reference(name, decode_golden):
+def test_ddtree_generate_matches_reference(name, eager, decode_golden, monkeypatch):
+    """Both loop forms: captured draft/verify forwards replayed from the
+    third round (default), and every round eager (DDTREE_EAGER=1)."""
     from ddtree_eagle3_patch_b200.ddtree import ddtree_generate
+    monkeypatch.setenv("DDTREE_EAGER", eager)
     z = decode_golden
     p = name + "_"
     tgt, drf, vocab, block, budget, plen, max_new = _models(name, z)
@@ -81,6 +85,11 @@ def test_ddtree_generate_matches_reference(name, decode_golden):
                                     "tree_build_heap", "tree_build_visibility"}
     assert res.time_to_first_token > 0 and res.time_per_output_token > 0
     assert len(res.round_timestamps) == res.decode_rounds
+    if eager == "0":
+        assert res.graph_rounds == max(res.decode_rounds - 2, 0)
+    else:
+        assert res.graph_rounds == 0
+    assert res.native_launches > 0
     assert all(b >= a for a, b in zip(res.round_timestamps, res.round_timestamps[1:]))
 
 
@@ -110,13 +119,18 @@ def test_ddtree_generate_is_lossless_in_bf16():
     tgt, drf, vocab, block, budget, plen, max_new = _models("v300_b6_t12", z)
     tgt, drf = tgt.to(DEV, torch.bfloat16), drf.to(DEV, torch.bfloat16)
     ids = torch.from_numpy(z["v300_b6_t12_prompt"]).to(DEV)
-    spec = ddtree_generate(drf, tgt, ids, mask_token_id=vocab - 1, max_new_tokens=max_new, block_size=block,
-                           stop_token_ids=None, tree_budget=budget)
-    ar = ddtree_generate(drf, tgt, ids, mask_token_id=vocab - 1, max_new_tokens=max_new, block_size=1,
-                         stop_token_ids=None)
-    assert ar.acceptance_lengths == [1] * ar.decode_rounds
-    # no generated token was the mask token (it would be filtered out)
+    # the reference drops generated tokens equal to the mask token from its
+    # output (ddtree.py:566); pick a mask token neither run emits, so that
+    # positions line up for the comparison
+    for mask_id in range(vocab - 1, vocab - 9, -1):
+        spec = ddtree_generate(drf, tgt, ids, mask_token_id=mask_id, max_new_tokens=max_new, block_size=block,
+                               stop_token_ids=None, tree_budget=budget)
+        ar = ddtree_generate(drf, tgt, ids, mask_token_id=mask_id, max_new_tokens=max_new, block_size=1,
+                             stop_token_ids=None)
+        if spec.num_output_tokens == max_new and ar.num_output_tokens == max_new:
+            break
     assert spec.num_output_tokens == max_new and ar.num_output_tokens == max_new
+    assert ar.acceptance_lengths == [1] * ar.decode_rounds
     a, b = spec.output_ids[0], ar.output_ids[0]
     assert torch.equal(a[:plen], b[:plen])
     diff = (a != b).nonzero()
