@@ -121,9 +121,9 @@ def gather_counters(values, device=None):
         vec = vec.to(device)
     if not is_initialized():
         return vec.unsqueeze(0)
-    out = torch.empty((dist.get_world_size(), vec.numel()), dtype=torch.float64, device=vec.device)
+    out = torch.empty((dist.get_world_size() * vec.numel(),), dtype=torch.float64, device=vec.device)
     dist.all_gather_into_tensor(out, vec.contiguous())
-    return out
+    return out.view(dist.get_world_size(), vec.numel())
 
 
 def merge_counters(per_rank: Iterable[Dict[str, float]]) -> Dict[str, float]:

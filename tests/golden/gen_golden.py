@@ -2,7 +2,7 @@
 
 Run in the build container (where the reference is importable):
 
-    python tests/golden/gen_golden.py /root/reference
+    python tests/golden/gen_golden.py <reference checkout>
 
 It imports the reference's ``ddtree``, ``eagle3`` and ``model.utils`` modules
 in-process (with ``dflash.cuda_time`` pointed at ``time.perf_counter`` so the

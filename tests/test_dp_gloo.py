@@ -85,3 +85,79 @@ def test_single_process_fallbacks(monkeypatch):
     assert list(dist.shard_indices(5)) == [0, 1, 2, 3, 4]
     with pytest.raises(ValueError):
         dist.shard_indices(5, rank_=2, size_=2)
+
+
+def _counter_worker(rank: int, world: int, port: int, out):
+    os.environ.update({"RANK": str(rank), "WORLD_SIZE": str(world), "LOCAL_RANK": str(rank),
+                       "MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port)})
+    from datetime import timedelta
+    from ddtree_eagle3_patch_b200 import distributed as dist
+    dist.init(backend="gloo", timeout=timedelta(seconds=60))
+    try:
+        # tokens, rounds, seconds: one fixed-size vector per rank
+        m = dist.gather_counters([100.0 * (rank + 1), 10.0 + rank, 0.5 * (rank + 1)])
+        out.put((rank, m.tolist()))
+    finally:
+        torch.distributed.destroy_process_group()
+
+
+def test_gather_counters_one_collective():
+    """The end-of-run counter exchange: one all-gather of a fixed-size
+    float64 vector per rank, the same [world, n] matrix on every rank."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_counter_worker, args=(r, WORLD, port, q)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=120) for _ in range(WORLD))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    expect = [[100.0, 10.0, 0.5], [200.0, 11.0, 1.0]]
+    assert got[0] == expect and got[1] == expect
+
+
+def _failing_worker(rank: int, world: int, port: int, mode: str, out):
+    """Rank 1 fails between steps (exits, raises, or stalls); rank 0 goes on
+    to the next step's collective and must get an error within the process
+    group's timeout instead of waiting for ever."""
+    import time
+    os.environ.update({"RANK": str(rank), "WORLD_SIZE": str(world), "LOCAL_RANK": str(rank),
+                       "MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port)})
+    from datetime import timedelta
+    from ddtree_eagle3_patch_b200 import distributed as dist
+    dist.init(backend="gloo", timeout=timedelta(seconds=3))
+    dist.gather_counters([1.0, 2.0])            # step 1 completes on both ranks
+    if rank == 1:
+        if mode == "exit":
+            os._exit(0)
+        if mode == "raise":
+            raise RuntimeError("rank 1 failed between steps")
+        time.sleep(60)                           # stall: never joins step 2
+        os._exit(0)
+    t0 = time.perf_counter()
+    try:
+        dist.gather_counters([3.0, 4.0])        # step 2: the peer is gone
+        out.put(("no error", time.perf_counter() - t0))
+    except Exception as exc:                    # noqa: BLE001 - any error type is a detected failure
+        out.put((type(exc).__name__, time.perf_counter() - t0))
+    os._exit(0)
+
+
+@pytest.mark.parametrize("mode", ["exit", "raise", "stall"])
+def test_failed_rank_is_detected_by_the_next_collective(mode):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, WORLD, port, mode, q)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    kind, waited = q.get(timeout=90)
+    for p in procs:
+        p.join(timeout=5)
+        if p.is_alive():
+            p.kill()
+            p.join(timeout=5)
+    assert kind != "no error"
+    assert waited < 30.0, waited
