@@ -396,8 +396,12 @@ def ddtree_generate(model, target, input_ids: torch.Tensor, mask_token_id: int, 
     if block_size <= 1:
         return _target_only_generate(model, target, input_ids, mask_token_id, max_new_tokens, block_size,
                                      stop_token_ids, temperature)
+    import os
+    from contextlib import nullcontext
+    from .fused_layers import fused_decoder_layers
     from .runtime import tree_attention_for
-    with tree_attention_for(target):
+    fuse = os.environ.get("DDTREE_FUSED", "1") != "0"
+    with tree_attention_for(target), (fused_decoder_layers(target) if fuse else nullcontext()):
         dec = _DDTreeDecoder(model, target, input_ids, mask_token_id, max_new_tokens, block_size, stop_token_ids,
                              temperature, tree_budget, save_tree_traces)
         return dec.run()

@@ -1,0 +1,108 @@
+"""Fused forward of a Qwen3-style decoder layer for the captured verify
+forward of a decode round.
+
+The stock eager layer (transformers Qwen3DecoderLayer) issues ~50 kernels
+per layer at verify time, six of them GEMMs; the rest are small elementwise
+steps that dominate a round at batch 1.  ``fused_decoder_layers(target)``
+gives each supported layer of the target, for the duration of a decode
+call, a forward that keeps the six GEMMs (cuBLAS through torch, the two
+residual adds folded into the o_proj and down_proj GEMMs as addmm) and
+replaces everything else by four launches of this library:
+
+  rms_norm                 input_layernorm / post_attention_layernorm
+  qk_norm_rope_append      q_norm, k_norm, rotary embedding, and the K/V
+                           append into the static cache at the device-side
+                           prefix length
+  tree attention           the verify attention, prefix length on the device
+  silu_mul                 the MLP's act_fn(gate) * up
+
+The fused forward runs only where the stock one would run the verify
+attention through this library with a static cache (the stand-in mask of
+``TreeMask.static``); any other call (the prefill, a host-mode cache)
+takes the stock forward, so results outside the decode rounds are
+unchanged.  The fused steps follow the stock modules' rounding order; the
+addmm folds round the residual sum once instead of twice.
+"""
+from __future__ import annotations
+
+import types
+from contextlib import contextmanager
+
+import torch
+import torch.nn.functional as F
+
+from . import kernels
+
+
+def _is_silu(act) -> bool:
+    return isinstance(act, torch.nn.SiLU) or type(act).__name__ in ("SiLUActivation", "SiLU")
+
+
+def supported_layer(layer) -> bool:
+    """Qwen3-style layer: pre-norm attention with q_norm / k_norm, head_dim
+    128, SwiGLU MLP with SiLU, no biases."""
+    attn, mlp = getattr(layer, "self_attn", None), getattr(layer, "mlp", None)
+    if attn is None or mlp is None:
+        return False
+    names = ("q_proj", "k_proj", "v_proj", "o_proj", "q_norm", "k_norm")
+    if not all(hasattr(attn, n) for n in names) or not all(hasattr(mlp, n) for n in ("gate_proj", "up_proj",
+                                                                                       "down_proj", "act_fn")):
+        return False
+    if not hasattr(layer, "input_layernorm") or not hasattr(layer, "post_attention_layernorm"):
+        return False
+    lin = (attn.q_proj, attn.k_proj, attn.v_proj, attn.o_proj, mlp.gate_proj, mlp.up_proj, mlp.down_proj)
+    if any(getattr(m, "bias", None) is not None for m in lin):
+        return False
+    return getattr(attn, "head_dim", None) == 128 and _is_silu(mlp.act_fn) and getattr(attn, "sliding_window",
+                                                                                        None) is None
+
+
+def _fused_forward(self, hidden_states, attention_mask=None, position_ids=None, past_key_values=None,
+                   use_cache=False, position_embeddings=None, **kwargs):
+    past_dev = getattr(attention_mask, "ddtree_past_dev", None) if torch.is_tensor(attention_mask) else None
+    if past_dev is None or getattr(past_key_values, "offset_dev", None) is None or hidden_states.shape[0] != 1:
+        return type(self).forward(self, hidden_states, attention_mask=attention_mask, position_ids=position_ids,
+                                  past_key_values=past_key_values, use_cache=use_cache,
+                                  position_embeddings=position_embeddings, **kwargs)
+    attn, mlp = self.self_attn, self.mlp
+    x = hidden_states[0]
+    T = x.shape[0]
+    h = kernels.rms_norm(x, self.input_layernorm.weight, self.input_layernorm.variance_epsilon)
+    q = F.linear(h, attn.q_proj.weight)
+    k = F.linear(h, attn.k_proj.weight)
+    v = F.linear(h, attn.v_proj.weight)
+    cos, sin = position_embeddings
+    cache = past_key_values.layers[attn.layer_idx]
+    hq, hkv = q.shape[1] // 128, k.shape[1] // 128
+    qr = kernels.qk_norm_rope_append(q, k, v, attn.q_norm.weight, attn.k_norm.weight, attn.q_norm.variance_epsilon,
+                                     attn.k_norm.variance_epsilon, cos[0], sin[0], cache._k, cache._v,
+                                     past_key_values.offset_dev, hq, hkv)
+    o = kernels.tree_attention(qr, cache._k[0], cache._v[0], attention_mask.ddtree_past_max,
+                               attention_mask.ddtree_bits, attn.scaling, past_dev=past_dev,
+                               workspace=attention_mask.ddtree_workspace)
+    x2 = torch.addmm(x, o.view(T, -1), attn.o_proj.weight.t())
+    h2 = kernels.rms_norm(x2, self.post_attention_layernorm.weight, self.post_attention_layernorm.variance_epsilon)
+    a = kernels.silu_mul(F.linear(h2, mlp.gate_proj.weight), F.linear(h2, mlp.up_proj.weight))
+    return torch.addmm(x2, a, mlp.down_proj.weight.t()).unsqueeze(0)
+
+
+def _decoder_layers(model):
+    inner = getattr(model, "model", model)
+    layers = getattr(inner, "layers", None)
+    return list(layers) if layers is not None else []
+
+
+@contextmanager
+def fused_decoder_layers(target):
+    """Give every supported decoder layer of ``target`` the fused forward for
+    the duration of the block (an instance attribute, removed afterwards)."""
+    patched = []
+    try:
+        for layer in _decoder_layers(target):
+            if supported_layer(layer) and "forward" not in layer.__dict__:
+                layer.forward = types.MethodType(_fused_forward, layer)
+                patched.append(layer)
+        yield len(patched)
+    finally:
+        for layer in patched:
+            layer.__dict__.pop("forward", None)

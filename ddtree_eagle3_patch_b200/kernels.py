@@ -271,6 +271,65 @@ def attention_status(device: torch.device, workspace: torch.Tensor | None = None
     return int(ws[:4].view(torch.int32).item())
 
 
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Qwen3RMSNorm over the last dim of a [rows, cols] tensor (``ddt_rms_norm``)."""
+    require_cuda(x, "x")
+    if x.dim() != 2 or x.stride(1) != 1 or weight.dtype != x.dtype or not weight.is_contiguous():
+        raise ValueError("x must be [rows, cols] with contiguous rows; weight contiguous, same dtype")
+    if out is None:
+        out = torch.empty_like(x, memory_format=torch.contiguous_format)
+    check(_lib.load().ddt_rms_norm(x.data_ptr(), dtype_code(x.dtype), x.stride(0), weight.data_ptr(), out.data_ptr(),
+                                   out.stride(0), x.shape[0], x.shape[1], float(eps), stream_of(x.device)),
+          "ddt_rms_norm")
+    return out
+
+
+def qk_norm_rope_append(q_raw: torch.Tensor, new_k: torch.Tensor, new_v: torch.Tensor, q_norm_w: torch.Tensor,
+                        k_norm_w: torch.Tensor, eps_q: float, eps_k: float, cos: torch.Tensor, sin: torch.Tensor,
+                        cache_k: torch.Tensor, cache_v: torch.Tensor, rs: torch.Tensor, hq: int, hkv: int,
+                        ctx_k: torch.Tensor | None = None, ctx_v: torch.Tensor | None = None,
+                        q_out: torch.Tensor | None = None) -> torch.Tensor:
+    """``ddt_qk_norm_rope_append``: q_raw [T, hq*128], new_k / new_v [T,
+    hkv*128] (optional ctx_k / ctx_v [C, hkv*128] before them), cos / sin
+    [C + T, 128]; cache_k / cache_v [hkv, rows, 128] (any leading size-1
+    dims); rs int32 device [start, ctx_offset, ctx_count].  Returns the
+    rotated queries [T, hq, 128]."""
+    T = q_raw.shape[0]
+    C = 0 if ctx_k is None else ctx_k.shape[0]
+    for t in (q_raw, new_k, new_v, cos, sin) + (() if ctx_k is None else (ctx_k, ctx_v)):
+        if t.dim() != 2 or t.stride(1) != 1 or t.dtype != q_raw.dtype or not t.is_cuda:
+            raise ValueError("q / k / v / cos / sin must be 2-D CUDA tensors of one dtype with contiguous rows")
+    if new_k.stride() != new_v.stride() or (ctx_k is not None and ctx_k.stride() != ctx_v.stride()):
+        raise ValueError("K and V must share strides")
+    if cos.stride() != sin.stride() or cos.shape[0] < C + T:
+        raise ValueError("cos / sin need one row per K/V row")
+    ck = cache_k.reshape(-1, cache_k.shape[-2], cache_k.shape[-1])
+    cv = cache_v.reshape(-1, cache_v.shape[-2], cache_v.shape[-1])
+    if ck.data_ptr() != cache_k.data_ptr() or ck.stride() != cv.stride() or ck.shape[0] != hkv:
+        raise ValueError("cache K/V must be [hkv, rows, 128] views sharing strides")
+    if q_out is None:
+        q_out = torch.empty((T, hq, 128), dtype=q_raw.dtype, device=q_raw.device)
+    rc = _lib.load().ddt_qk_norm_rope_append(
+        dtype_code(q_raw.dtype), q_raw.data_ptr(), q_raw.stride(0), ptr(ctx_k), ptr(ctx_v),
+        0 if ctx_k is None else ctx_k.stride(0), C, new_k.data_ptr(), new_v.data_ptr(), new_k.stride(0), T,
+        q_norm_w.data_ptr(), k_norm_w.data_ptr(), float(eps_q), float(eps_k), cos.data_ptr(), sin.data_ptr(),
+        cos.stride(0), hq, hkv, 128, q_out.data_ptr(), q_out.stride(0), ck.data_ptr(), cv.data_ptr(), ck.stride(0),
+        ck.stride(1), ck.shape[1], rs.data_ptr(), stream_of(q_raw.device))
+    check(rc, "ddt_qk_norm_rope_append")
+    return q_out
+
+
+def silu_mul(gate: torch.Tensor, up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """to_dtype(silu(gate)) * up for contiguous tensors (``ddt_silu_mul``)."""
+    if not (gate.is_contiguous() and up.is_contiguous()) or gate.shape != up.shape or gate.dtype != up.dtype:
+        raise ValueError("gate and up must be contiguous and alike")
+    if out is None:
+        out = torch.empty_like(gate)
+    check(_lib.load().ddt_silu_mul(gate.data_ptr(), up.data_ptr(), out.data_ptr(), dtype_code(gate.dtype),
+                                   gate.numel(), stream_of(gate.device)), "ddt_silu_mul")
+    return out
+
+
 def kv_append(k_src: torch.Tensor, v_src: torch.Tensor, k_dst: torch.Tensor, v_dst: torch.Tensor,
               offset_dev: torch.Tensor, rows_dev: torch.Tensor | None = None) -> None:
     """Copy rows [0, rows) of k_src / v_src ([..., heads, rows, dim]) into

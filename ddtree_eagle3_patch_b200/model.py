@@ -19,10 +19,12 @@ over the draft cache's rows in place.
 """
 from __future__ import annotations
 
+import os
 from typing import Optional
 
 import numpy as np
 import torch
+import torch.nn.functional as F
 from torch import nn
 from transformers.models.qwen3.modeling_qwen3 import (
     Qwen3Config,
@@ -185,9 +187,39 @@ class DFlashDecoderLayer(nn.Module):
         return h + self.mlp(self.post_attention_layernorm(h))
 
     def forward_static(self, hidden_states, target_hidden, position_embeddings, cache, rs, past_max, workspace):
-        h = hidden_states + self.self_attn.forward_static(self.input_layernorm(hidden_states), target_hidden,
-                                                          position_embeddings, cache, rs, past_max, workspace)
-        return h + self.mlp(self.post_attention_layernorm(h))
+        """The layer with device-side cache lengths.  For the Qwen3-style
+        layer (head_dim 128, no biases, SiLU) the elementwise steps run as
+        fused kernels: RMSNorm, q/k norm + rotary embedding + both cache
+        appends in one launch, SiLU * up; the residual adds fold into the
+        o_proj / down_proj GEMMs."""
+        from .fused_layers import supported_layer
+        if not supported_layer(self) or os.environ.get("DDTREE_FUSED", "1") == "0":
+            h = hidden_states + self.self_attn.forward_static(self.input_layernorm(hidden_states), target_hidden,
+                                                              position_embeddings, cache, rs, past_max, workspace)
+            return h + self.mlp(self.post_attention_layernorm(h))
+        attn, mlp = self.self_attn, self.mlp
+        x, c = hidden_states[0], target_hidden[0]
+        T = x.shape[0]
+        h = kernels.rms_norm(x, self.input_layernorm.weight, self.input_layernorm.variance_epsilon)
+        q = F.linear(h, attn.q_proj.weight)
+        k_c, v_c = F.linear(c, attn.k_proj.weight), F.linear(c, attn.v_proj.weight)
+        k_n, v_n = F.linear(h, attn.k_proj.weight), F.linear(h, attn.v_proj.weight)
+        layer_cache = cache.layers[attn.layer_idx]
+        if not layer_cache.is_initialized:
+            empty = torch.empty((1, attn.num_kv_heads, 0, attn.head_dim), dtype=x.dtype, device=x.device)
+            layer_cache.lazy_initialization(empty, empty)
+        cos, sin = position_embeddings
+        qr = kernels.qk_norm_rope_append(q, k_n, v_n, attn.q_norm.weight, attn.k_norm.weight,
+                                         attn.q_norm.variance_epsilon, attn.k_norm.variance_epsilon, cos[0], sin[0],
+                                         layer_cache._k, layer_cache._v, rs, attn.num_heads, attn.num_kv_heads,
+                                         ctx_k=k_c, ctx_v=v_c)
+        bits = _all_visible_bits(T, x.device)
+        o = kernels.tree_attention(qr, layer_cache._k[0], layer_cache._v[0], past_max, bits, attn.scaling,
+                                   past_dev=rs[0:1], workspace=workspace)
+        x2 = torch.addmm(x, o.view(T, -1), attn.o_proj.weight.t())
+        h2 = kernels.rms_norm(x2, self.post_attention_layernorm.weight, self.post_attention_layernorm.variance_epsilon)
+        a = kernels.silu_mul(F.linear(h2, mlp.gate_proj.weight), F.linear(h2, mlp.up_proj.weight))
+        return torch.addmm(x2, a, mlp.down_proj.weight.t()).unsqueeze(0)
 
 
 class DFlashDraftModel(Qwen3PreTrainedModel):

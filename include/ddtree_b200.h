@@ -282,6 +282,42 @@ DDT_API int ddt_kv_append(const void* k_src, const void* v_src, int64_t src_head
                           ddt_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * Fused elementwise steps of a Qwen3-style decoder layer for the verify and
+ * draft forwards of a round (the target layers run by ddtree.py:523-531 and
+ * the DFlash layers of model/dflash.py:36-150).  Each follows the stock
+ * module's arithmetic order, rounding to the dtype where it does.
+ * ------------------------------------------------------------------------- */
+
+/* Qwen3RMSNorm of `rows` rows: y = w * to_dtype(x * rsqrt(mean(x^2) + eps)),
+ * mean and rsqrt in fp32.  Strides in elements. */
+DDT_API int ddt_rms_norm(const void* x, int dtype, int64_t x_row_stride, const void* weight, void* y,
+                         int64_t y_row_stride, int64_t rows, int64_t cols, float eps, ddt_stream_t stream);
+
+/* q_norm / k_norm (RMSNorm over head_dim = 128), the rotary embedding
+ * (x * cos) + (rotate_half(x) * sin), and the append of the new K/V rows:
+ *   - K/V rows: ctx_rows context rows (ctx_k / ctx_v) then new_rows rows
+ *     (new_k / new_v), each [rows, hkv * 128]; cos / sin have one row per
+ *     K/V row, in that order;
+ *   - queries: q_raw [new_rows, hq * 128], one per new row; rotated queries
+ *     go to q_out [new_rows, hq * 128];
+ *   - cache rows (device int32 rs = {start, ctx_offset, ctx_count}): new
+ *     row r goes to start + r, context row r < ctx_count to ctx_offset + r
+ *     (rows >= ctx_count are not written), rows outside [0, cache_rows) are
+ *     skipped.  V is written unchanged.  Strides in elements. */
+DDT_API int ddt_qk_norm_rope_append(int dtype, const void* q_raw, int64_t q_row_stride, const void* ctx_k,
+                                    const void* ctx_v, int64_t ctx_row_stride, int64_t ctx_rows, const void* new_k,
+                                    const void* new_v, int64_t new_row_stride, int64_t new_rows,
+                                    const void* q_norm_weight, const void* k_norm_weight, float eps_q, float eps_k,
+                                    const void* cos, const void* sin, int64_t cs_row_stride, int64_t hq, int64_t hkv,
+                                    int64_t head_dim, void* q_out, int64_t q_out_row_stride, void* cache_k,
+                                    void* cache_v, int64_t cache_head_stride, int64_t cache_row_stride,
+                                    int64_t cache_rows, const int32_t* rs, ddt_stream_t stream);
+
+/* out = to_dtype(silu(gate)) * up, elementwise over n contiguous values
+ * (Qwen3MLP's act_fn(gate_proj(x)) * up_proj(x)). */
+DDT_API int ddt_silu_mul(const void* gate, const void* up, void* out, int dtype, int64_t n, ddt_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * EAGLE3 path acceptance.  Replaces evaluate_eagle3_posterior
  * (eagle3.py:46-79) for temperature 0: argmax of every verify row, the
  * longest accepted prefix over the rows of retrieve_indices (-1 padded),
