@@ -735,6 +735,8 @@ def run_decode(args, rank, world, local):
                     "api": "ddtree_eagle3_patch_b200.ddtree.ddtree_generate (host prompt in, host ids out)"},
             "gpu_launches": int(launches), "clocks": clock, "attention_status": status,
             "model_build_s": round(t_build, 1),
+            "graph_capture_ms_per_call": round(1e3 * sum(r.graph_capture_s for r in results) / len(results), 2),
+            "graph_rounds": sum(r.graph_rounds for r in results),
         }
         if world == 1 and not args.no_cpu_baseline:
             out["cpu_baseline"] = cpu_decode_baseline(rounds=2)

@@ -39,7 +39,56 @@ template <typename T>
 __device__ __forceinline__ float rnd(float v) { return to_f32<T>(from_f32<T>(v)); }
 
 // ---------------------------------------------------------------------------
-// RMSNorm of rows: one CTA per row.
+// RMSNorm of rows whose 16-byte vectors fit VPT per thread: the row is read
+// once into registers, reduced, and written from registers.
+template <typename T, int THREADS, int VPT>
+__global__ void __launch_bounds__(THREADS)
+rms_norm_vec_kernel(const T* __restrict__ x, int64_t x_stride, const T* __restrict__ w, T* __restrict__ y,
+                    int64_t y_stride, int cols, float eps) {
+    constexpr int E = 16 / sizeof(T);
+    const int nv = cols / E;
+    const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)blockIdx.x * x_stride);
+    const uint4* wr = reinterpret_cast<const uint4*>(w);
+    uint4* yr = reinterpret_cast<uint4*>(y + (int64_t)blockIdx.x * y_stride);
+    uint4 v[VPT];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+        const int c = threadIdx.x + i * THREADS;
+        v[i] = c < nv ? xr[c] : make_uint4(0u, 0u, 0u, 0u);
+        const T* e = reinterpret_cast<const T*>(&v[i]);
+#pragma unroll
+        for (int j = 0; j < E; ++j) {
+            const float f = to_f32<T>(e[j]);
+            ss = fmaf(f, f, ss);
+        }
+    }
+    __shared__ float red[THREADS / 32];
+#pragma unroll
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(DDT_FULL_MASK, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < THREADS / 32; ++i) s += red[i];
+    const float r = rsqrtf(s / (float)cols + eps);
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+        const int c = threadIdx.x + i * THREADS;
+        if (c >= nv) break;
+        const uint4 wv = wr[c];
+        const T* e = reinterpret_cast<const T*>(&v[i]);
+        const T* we = reinterpret_cast<const T*>(&wv);
+        uint4 o;
+        T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+        for (int j = 0; j < E; ++j) oe[j] = from_f32<T>(to_f32<T>(we[j]) * rnd<T>(to_f32<T>(e[j]) * r));
+        yr[c] = o;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// RMSNorm of rows: one CTA per row (any width or alignment).
 template <typename T, int THREADS>
 __global__ void __launch_bounds__(THREADS)
 rms_norm_kernel(const T* __restrict__ x, int64_t x_stride, const T* __restrict__ w, T* __restrict__ y,
@@ -147,7 +196,7 @@ qk_norm_rope_append_kernel(RopeParams p) {
     }
     const bool store_kv = dest >= 0 && dest < p.cache_rows;
     const int n_tasks = 2 * p.hkv + (is_b ? p.hq : 0);
-    for (int task = warp; task < n_tasks; task += 8) {
+    for (int task = blockIdx.y * 8 + warp; task < n_tasks; task += 8 * gridDim.y) {
         if (task < p.hkv) {                         // K head: norm + rope -> cache
             const int h = task;
             float o[4];
@@ -181,12 +230,39 @@ qk_norm_rope_append_kernel(RopeParams p) {
 // SiLU(gate) * up, elementwise (silu rounded to the dtype first, as torch's
 // act_fn(gate) * up does).
 template <typename T>
+__device__ __forceinline__ T silu_times(T g, T u) {
+    const float gv = to_f32<T>(g);
+    const float s = rnd<T>(gv / (1.f + expf(-gv)));
+    return from_f32<T>(s * to_f32<T>(u));
+}
+
+// grid (column blocks, rows): each thread one 16-byte vector of a row when
+// the row strides allow it, else one element
+template <typename T, bool VEC>
 __global__ void __launch_bounds__(256)
-silu_mul_kernel(const T* __restrict__ g, const T* __restrict__ u, T* __restrict__ out, int64_t n) {
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-        const float gv = to_f32<T>(g[i]);
-        const float s = rnd<T>(gv / (1.f + expf(-gv)));
-        out[i] = from_f32<T>(s * to_f32<T>(u[i]));
+silu_mul_kernel(const T* __restrict__ g, const T* __restrict__ u, int64_t in_stride, T* __restrict__ out,
+                int64_t out_stride, int64_t rows, int64_t cols) {
+    const int64_t r = blockIdx.y;
+    const T* gr = g + r * in_stride;
+    const T* ur = u + r * in_stride;
+    T* orow = out + r * out_stride;
+    if (VEC) {
+        constexpr int E = 16 / sizeof(T);
+        for (int64_t c = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * E; c < cols;
+             c += (int64_t)gridDim.x * blockDim.x * E) {
+            const uint4 gv = *reinterpret_cast<const uint4*>(gr + c);
+            const uint4 uv = *reinterpret_cast<const uint4*>(ur + c);
+            uint4 ov;
+            const T* ge = reinterpret_cast<const T*>(&gv);
+            const T* ue = reinterpret_cast<const T*>(&uv);
+            T* oe = reinterpret_cast<T*>(&ov);
+#pragma unroll
+            for (int j = 0; j < E; ++j) oe[j] = silu_times<T>(ge[j], ue[j]);
+            *reinterpret_cast<uint4*>(orow + c) = ov;
+        }
+    } else {
+        for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < cols; c += (int64_t)gridDim.x * blockDim.x)
+            orow[c] = silu_times<T>(gr[c], ur[c]);
     }
 }
 
@@ -202,6 +278,27 @@ extern "C" int ddt_rms_norm(const void* x, int dtype, int64_t x_row_stride, cons
     if (rows == 0) return DDT_OK;
     if (rows > 0x7fffffff || cols > (1 << 24)) return set_error(DDT_EUNSUPPORTED, "sizes too large");
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int esz = dtype == DDT_F32 ? 4 : 2;
+    const int per_vec = 16 / esz;
+    const bool vec = reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(y) % 16 == 0 &&
+                     reinterpret_cast<uintptr_t>(weight) % 16 == 0 && cols % per_vec == 0 &&
+                     x_row_stride % per_vec == 0 && y_row_stride % per_vec == 0;
+    const int64_t nvec = cols / per_vec;
+#define DDT_RMS_VEC(T, VPT)                                                                                         \
+    fused::rms_norm_vec_kernel<T, 256, VPT><<<(unsigned)rows, 256, 0, st>>>(                                         \
+        static_cast<const T*>(x), x_row_stride, static_cast<const T*>(weight), static_cast<T*>(y), y_row_stride,     \
+        (int)cols, eps)
+    if (vec && nvec <= 256 * 4 && (dtype == DDT_BF16 || dtype == DDT_F32 || dtype == DDT_F16)) {
+        if (dtype == DDT_BF16) {
+            if (nvec <= 512) DDT_RMS_VEC(__nv_bfloat16, 2); else DDT_RMS_VEC(__nv_bfloat16, 4);
+        } else if (dtype == DDT_F16) {
+            if (nvec <= 512) DDT_RMS_VEC(__half, 2); else DDT_RMS_VEC(__half, 4);
+        } else {
+            if (nvec <= 512) DDT_RMS_VEC(float, 2); else DDT_RMS_VEC(float, 4);
+        }
+#undef DDT_RMS_VEC
+        return check_launch("rms_norm_vec_kernel");
+    }
     if (dtype == DDT_BF16)
         fused::rms_norm_kernel<__nv_bfloat16, 256><<<(unsigned)rows, 256, 0, st>>>(
             static_cast<const __nv_bfloat16*>(x), x_row_stride, static_cast<const __nv_bfloat16*>(weight),
@@ -268,7 +365,8 @@ extern "C" int ddt_qk_norm_rope_append(int dtype, const void* q_raw, int64_t q_r
     p.cache_rows = cache_rows;
     p.rs = rs;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    const unsigned grid = (unsigned)(ctx_rows + new_rows);
+    // one warp per head task: (K heads, V heads, Q heads) of a row over grid.y CTAs of 8 warps
+    const dim3 grid((unsigned)(ctx_rows + new_rows), (unsigned)ceil_div(2 * hkv + hq, 8));
     if (dtype == DDT_BF16)
         fused::qk_norm_rope_append_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(p);
     else if (dtype == DDT_F32)
@@ -280,29 +378,45 @@ extern "C" int ddt_qk_norm_rope_append(int dtype, const void* q_raw, int64_t q_r
     return check_launch("qk_norm_rope_append_kernel");
 }
 
-extern "C" int ddt_silu_mul(const void* gate, const void* up, void* out, int dtype, int64_t n, ddt_stream_t stream) {
+extern "C" int ddt_silu_mul_rows(const void* gate, const void* up, int64_t in_row_stride, void* out,
+                                 int64_t out_row_stride, int64_t rows, int64_t cols, int dtype, ddt_stream_t stream) {
     if (!gate || !up || !out) return set_error(DDT_EINVAL, "null argument");
-    if (n < 0) return set_error(DDT_EINVAL, "bad size");
-    if (n == 0) return DDT_OK;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    const int sms = ddt_sm_count(dev);
-    const int64_t want = ceil_div(n, 256);
-    const unsigned blocks = (unsigned)(want < 8LL * (sms > 0 ? sms : 148) ? want : 8LL * (sms > 0 ? sms : 148));
+    if (rows < 0 || cols < 0 || (rows > 1 && (in_row_stride < cols || out_row_stride < cols)))
+        return set_error(DDT_EINVAL, "bad sizes");
+    if (rows == 0 || cols == 0) return DDT_OK;
+    if (rows > 65535) return set_error(DDT_EUNSUPPORTED, "rows %lld > 65535", (long long)rows);
+    const int esz = dtype == DDT_F32 ? 4 : 2;
+    const int per_vec = 16 / esz;
+    const bool vec = reinterpret_cast<uintptr_t>(gate) % 16 == 0 && reinterpret_cast<uintptr_t>(up) % 16 == 0 &&
+                     reinterpret_cast<uintptr_t>(out) % 16 == 0 && cols % per_vec == 0 &&
+                     (rows == 1 || (in_row_stride % per_vec == 0 && out_row_stride % per_vec == 0));
+    const int64_t per_row = vec ? cols / per_vec : cols;
+    const int64_t cap = 65535;
+    const int64_t bx = ceil_div(per_row, 256);
+    const dim3 grid((unsigned)(bx < cap ? bx : cap), (unsigned)rows);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+#define DDT_SILU(T)                                                                                                \
+    do {                                                                                                           \
+        if (vec)                                                                                                   \
+            fused::silu_mul_kernel<T, true><<<grid, 256, 0, st>>>(static_cast<const T*>(gate),                     \
+                static_cast<const T*>(up), in_row_stride, static_cast<T*>(out), out_row_stride, rows, cols);        \
+        else                                                                                                       \
+            fused::silu_mul_kernel<T, false><<<grid, 256, 0, st>>>(static_cast<const T*>(gate),                    \
+                static_cast<const T*>(up), in_row_stride, static_cast<T*>(out), out_row_stride, rows, cols);        \
+    } while (0)
     if (dtype == DDT_BF16)
-        fused::silu_mul_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(gate),
-                                                                       static_cast<const __nv_bfloat16*>(up),
-                                                                       static_cast<__nv_bfloat16*>(out), n);
+        DDT_SILU(__nv_bfloat16);
     else if (dtype == DDT_F32)
-        fused::silu_mul_kernel<float><<<blocks, 256, 0, st>>>(static_cast<const float*>(gate),
-                                                               static_cast<const float*>(up),
-                                                               static_cast<float*>(out), n);
+        DDT_SILU(float);
     else if (dtype == DDT_F16)
-        fused::silu_mul_kernel<__half><<<blocks, 256, 0, st>>>(static_cast<const __half*>(gate),
-                                                                static_cast<const __half*>(up),
-                                                                static_cast<__half*>(out), n);
+        DDT_SILU(__half);
     else
         return set_error(DDT_EINVAL, "dtype %d", dtype);
+#undef DDT_SILU
     return check_launch("silu_mul_kernel");
+}
+
+extern "C" int ddt_silu_mul(const void* gate, const void* up, void* out, int dtype, int64_t n, ddt_stream_t stream) {
+    if (n < 0) return set_error(DDT_EINVAL, "bad size");
+    return ddt_silu_mul_rows(gate, up, n, out, n, 1, n, dtype, stream);
 }

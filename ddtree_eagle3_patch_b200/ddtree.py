@@ -454,6 +454,7 @@ class _DDTreeDecoder:
         self.graphs = None
         self.graph_kernels = (0, 0)
         self.replays = 0
+        self.capture_s = 0.0
         self.n_nodes = tree_node_count(self.budget, self.L, self.vocab)
         self.N = 1 + self.n_nodes
 
@@ -518,6 +519,7 @@ class _DDTreeDecoder:
         same shapes has warmed every path)."""
         from ._lib import load
         lib = load()
+        t0 = time.perf_counter()
         pool = torch.cuda.graph_pool_handle()
         gd, gv = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
         n0 = lib.ddt_launch_count()
@@ -530,6 +532,7 @@ class _DDTreeDecoder:
         # this library's kernels inside each graph (counted once, at capture)
         self.graph_kernels = (n1 - n0, n2 - n1)
         self.graphs = (gd, gv, draft_logits, logits, features)
+        self.capture_s = time.perf_counter() - t0
 
     # ------------------------------------------------------------------ loop
     def run(self) -> SimpleNamespace:
@@ -654,6 +657,7 @@ class _DDTreeDecoder:
             round_trees=round_trees,
             native_launches=int(native),
             graph_rounds=self.replays,
+            graph_capture_s=self.capture_s,
         )
 
     def _accept_commit(self, logits: torch.Tensor, features: torch.Tensor, start: int, rnd: int) -> None:

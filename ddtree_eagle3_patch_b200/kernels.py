@@ -320,13 +320,25 @@ def qk_norm_rope_append(q_raw: torch.Tensor, new_k: torch.Tensor, new_v: torch.T
 
 
 def silu_mul(gate: torch.Tensor, up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
-    """to_dtype(silu(gate)) * up for contiguous tensors (``ddt_silu_mul``)."""
-    if not (gate.is_contiguous() and up.is_contiguous()) or gate.shape != up.shape or gate.dtype != up.dtype:
-        raise ValueError("gate and up must be contiguous and alike")
+    """to_dtype(silu(gate)) * up: contiguous tensors (``ddt_silu_mul``) or
+    2-D [rows, cols] views sharing a row stride, such as the two halves of
+    one gate/up projection (``ddt_silu_mul_rows``)."""
+    if gate.shape != up.shape or gate.dtype != up.dtype:
+        raise ValueError("gate and up must be alike")
+    if gate.is_contiguous() and up.is_contiguous():
+        if out is None:
+            out = torch.empty_like(gate)
+        check(_lib.load().ddt_silu_mul(gate.data_ptr(), up.data_ptr(), out.data_ptr(), dtype_code(gate.dtype),
+                                       gate.numel(), stream_of(gate.device)), "ddt_silu_mul")
+        return out
+    if gate.dim() != 2 or gate.stride(1) != 1 or gate.stride() != up.stride():
+        raise ValueError("strided gate / up must be [rows, cols] views with one row stride")
+    rows, cols = gate.shape
     if out is None:
-        out = torch.empty_like(gate)
-    check(_lib.load().ddt_silu_mul(gate.data_ptr(), up.data_ptr(), out.data_ptr(), dtype_code(gate.dtype),
-                                   gate.numel(), stream_of(gate.device)), "ddt_silu_mul")
+        out = torch.empty((rows, cols), dtype=gate.dtype, device=gate.device)
+    check(_lib.load().ddt_silu_mul_rows(gate.data_ptr(), up.data_ptr(), gate.stride(0), out.data_ptr(),
+                                        out.stride(0), rows, cols, dtype_code(gate.dtype), stream_of(gate.device)),
+          "ddt_silu_mul_rows")
     return out
 
 

@@ -197,13 +197,22 @@ class DFlashDecoderLayer(nn.Module):
             h = hidden_states + self.self_attn.forward_static(self.input_layernorm(hidden_states), target_hidden,
                                                               position_embeddings, cache, rs, past_max, workspace)
             return h + self.mlp(self.post_attention_layernorm(h))
+        from .fused_layers import packed_weights
         attn, mlp = self.self_attn, self.mlp
         x, c = hidden_states[0], target_hidden[0]
         T = x.shape[0]
+        nq, nk = attn.num_heads * attn.head_dim, attn.num_kv_heads * attn.head_dim
         h = kernels.rms_norm(x, self.input_layernorm.weight, self.input_layernorm.variance_epsilon)
-        q = F.linear(h, attn.q_proj.weight)
-        k_c, v_c = F.linear(c, attn.k_proj.weight), F.linear(c, attn.v_proj.weight)
-        k_n, v_n = F.linear(h, attn.k_proj.weight), F.linear(h, attn.v_proj.weight)
+        packed = packed_weights(self)
+        if packed is not None:
+            qkv = F.linear(h, packed[0])
+            q, k_n, v_n = qkv[:, :nq], qkv[:, nq: nq + nk], qkv[:, nq + nk:]
+            kv = F.linear(c, packed[0][nq:])
+            k_c, v_c = kv[:, :nk], kv[:, nk:]
+        else:
+            q = F.linear(h, attn.q_proj.weight)
+            k_c, v_c = F.linear(c, attn.k_proj.weight), F.linear(c, attn.v_proj.weight)
+            k_n, v_n = F.linear(h, attn.k_proj.weight), F.linear(h, attn.v_proj.weight)
         layer_cache = cache.layers[attn.layer_idx]
         if not layer_cache.is_initialized:
             empty = torch.empty((1, attn.num_kv_heads, 0, attn.head_dim), dtype=x.dtype, device=x.device)
@@ -218,8 +227,13 @@ class DFlashDecoderLayer(nn.Module):
                                    past_dev=rs[0:1], workspace=workspace)
         x2 = torch.addmm(x, o.view(T, -1), attn.o_proj.weight.t())
         h2 = kernels.rms_norm(x2, self.post_attention_layernorm.weight, self.post_attention_layernorm.variance_epsilon)
-        a = kernels.silu_mul(F.linear(h2, mlp.gate_proj.weight), F.linear(h2, mlp.up_proj.weight))
-        return torch.addmm(x2, a, mlp.down_proj.weight.t()).unsqueeze(0)
+        if packed is not None:
+            gu = F.linear(h2, packed[1])
+            inter = gu.shape[1] // 2
+            a = kernels.silu_mul(gu[:, :inter], gu[:, inter:])
+        else:
+            a = kernels.silu_mul(F.linear(h2, mlp.gate_proj.weight), F.linear(h2, mlp.up_proj.weight))
+        return x2.addmm_(a, mlp.down_proj.weight.t()).unsqueeze(0)
 
 
 class DFlashDraftModel(Qwen3PreTrainedModel):

@@ -317,6 +317,12 @@ DDT_API int ddt_qk_norm_rope_append(int dtype, const void* q_raw, int64_t q_row_
  * (Qwen3MLP's act_fn(gate_proj(x)) * up_proj(x)). */
 DDT_API int ddt_silu_mul(const void* gate, const void* up, void* out, int dtype, int64_t n, ddt_stream_t stream);
 
+/* The same over `rows` rows of `cols` values: gate and up share the row
+ * stride in_row_stride (e.g. the two halves of one [rows, 2 * cols] gate/up
+ * projection), out has out_row_stride.  Strides in elements. */
+DDT_API int ddt_silu_mul_rows(const void* gate, const void* up, int64_t in_row_stride, void* out,
+                              int64_t out_row_stride, int64_t rows, int64_t cols, int dtype, ddt_stream_t stream);
+
 /* ---------------------------------------------------------------------------
  * EAGLE3 path acceptance.  Replaces evaluate_eagle3_posterior
  * (eagle3.py:46-79) for temperature 0: argmax of every verify row, the

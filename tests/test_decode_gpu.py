@@ -53,14 +53,26 @@ def test_fixture_models_rebuild_on_cpu(decode_golden):
                               decode_golden[p + "prompt"])
 
 
+MODES = {  # DDTREE_EAGER, DDTREE_FUSED, DDTREE_PACK
+    "graphs": ("0", "1", "1"),            # the default: captured forwards, fused layers, packed weights
+    "eager": ("1", "1", "1"),             # every round eager
+    "graphs_unfused": ("0", "0", "1"),    # captured forwards over the stock layers
+    "graphs_unpacked": ("0", "1", "0"),   # fused layers with one GEMM per projection
+}
+
+
 @pytest.mark.gpu
-@pytest.mark.parametrize("eager", ["0", "1"], ids=["graphs", "eager"])
+@pytest.mark.parametrize("mode", list(MODES))
 @pytest.mark.parametrize("name", [c[0] for c in C.CASES])
-def test_ddtree_generate_matches_reference(name, eager, decode_golden, monkeypatch):
-    """Both loop forms: captured draft/verify forwards replayed from the
-    third round (default), and every round eager (DDTREE_EAGER=1)."""
+def test_ddtree_generate_matches_reference(name, mode, decode_golden, monkeypatch):
+    """Every loop form: captured draft/verify forwards replayed from the
+    third round (default), every round eager, the stock layers inside the
+    graphs, and the fused layers without packed weights."""
     from ddtree_eagle3_patch_b200.ddtree import ddtree_generate
+    eager, fused, pack = MODES[mode]
     monkeypatch.setenv("DDTREE_EAGER", eager)
+    monkeypatch.setenv("DDTREE_FUSED", fused)
+    monkeypatch.setenv("DDTREE_PACK", pack)
     z = decode_golden
     p = name + "_"
     tgt, drf, vocab, block, budget, plen, max_new = _models(name, z)
