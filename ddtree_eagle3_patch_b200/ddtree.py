@@ -402,40 +402,72 @@ def ddtree_generate(model, target, input_ids: torch.Tensor, mask_token_id: int, 
     from .runtime import tree_attention_for
     fuse = os.environ.get("DDTREE_FUSED", "1") != "0"
     with tree_attention_for(target), (fused_decoder_layers(target) if fuse else nullcontext()):
-        dec = _DDTreeDecoder(model, target, input_ids, mask_token_id, max_new_tokens, block_size, stop_token_ids,
-                             temperature, tree_budget, save_tree_traces)
+        budget = block_size - 1 if tree_budget is None else max(int(tree_budget), 0)
+        needed = input_ids.shape[1] + max_new_tokens + (1 + budget) + 1
+        dec = _decoder_session(model, target, block_size, tree_budget, needed)
+        dec.start_call(input_ids, mask_token_id, max_new_tokens, stop_token_ids, temperature, save_tree_traces)
         return dec.run()
 
 
-class _DDTreeDecoder:
-    """State of one ddtree_generate call (buffers, caches, captured forwards)."""
+def _weights_fingerprint(*modules) -> tuple:
+    """Addresses and versions of every parameter: a captured forward reads
+    the weights by address, so a session is reused only while they hold."""
+    return tuple((p.data_ptr(), p._version) for m in modules for p in m.parameters())
 
-    def __init__(self, model, target, input_ids, mask_token_id, max_new_tokens, block_size, stop_token_ids,
-                 temperature, tree_budget, save_tree_traces):
-        import os
+
+def _decoder_session(model, target, block_size, tree_budget, needed_rows: int):
+    """The decode session of (draft, target, block size, budget): buffers of
+    at least ``needed_rows`` cache rows and, once captured, the draft and
+    verify graphs.  Kept on the target (outside its state dict) and reused
+    by later calls while the weights and settings match, so a call pays no
+    capture; ``release_decode_sessions(target)`` frees it."""
+    import os
+    eager = os.environ.get("DDTREE_EAGER", "0") == "1"
+    fused = (os.environ.get("DDTREE_FUSED", "1"), os.environ.get("DDTREE_PACK", "1"))
+    key = (id(model), block_size, tree_budget, eager, fused)
+    fp = _weights_fingerprint(model, target)
+    held = target.__dict__.get("_ddtree_session")
+    if held is not None:
+        k, sess = held
+        if k == key and sess.capacity >= needed_rows and sess.fingerprint == fp and sess.model is model:
+            sess.target = target   # held for the call only (the session lives on the target)
+            return sess
+        target.__dict__.pop("_ddtree_session", None)
+        del sess, held
+    capacity = -(-needed_rows // 1024) * 1024
+    sess = _DDTreeDecoder(model, target, block_size, tree_budget, capacity, eager)
+    sess.fingerprint = fp
+    target.__dict__["_ddtree_session"] = (key, sess)
+    return sess
+
+
+def release_decode_sessions(target) -> None:
+    """Free the buffers and graphs that ddtree_generate keeps on ``target``."""
+    target.__dict__.pop("_ddtree_session", None)
+
+
+class _DDTreeDecoder:
+    """A decode session: buffers, caches and captured forwards, reused by
+    the ddtree_generate calls of one (draft, target) pair; ``start_call``
+    sets the per-call state."""
+
+    def __init__(self, model, target, block_size, tree_budget, capacity: int, eager: bool):
         from .cache import TreeAppendCache
         from .model import DFlashDraftModel
-        from .runtime import EventClock, Readback, TreeMask, device_sample_seed
+        from .runtime import Readback, TreeMask
         self.model, self.target = model, target
         self.device = device = model.device
-        self.P = input_ids.shape[1]
-        self.input_ids = input_ids
-        self.max_length = self.P + max_new_tokens
+        self.capacity = capacity
         self.block = block_size
         self.L = block_size - 1
         self.budget = self.L if tree_budget is None else max(int(tree_budget), 0)
         self.max_nodes = 1 + self.budget
-        self.mask_token_id = mask_token_id
-        self.temperature = temperature
-        self.traces = save_tree_traces
         self.vocab = target.lm_head.weight.shape[0] if hasattr(target, "lm_head") else target.config.vocab_size
-        self.stop_ids = None if stop_token_ids is None else set(int(t) for t in stop_token_ids)
         self.layer_types, self.window = detect_hybrid_attention(target)
-        self.output_ids = torch.full((1, self.max_length + self.max_nodes), mask_token_id, dtype=torch.long,
-                                     device=device)
-        self.position_ids = torch.arange(self.output_ids.shape[1], device=device).unsqueeze(0)
-        self.target_cache = TreeAppendCache(self.max_length + self.max_nodes + 1, config=target.config)
-        self.draft_cache = TreeAppendCache(self.max_length + self.max_nodes + block_size + 1, config=model.config)
+        self.output_ids = torch.zeros((1, capacity), dtype=torch.long, device=device)
+        self.position_ids = torch.arange(capacity, device=device).unsqueeze(0)
+        self.target_cache = TreeAppendCache(capacity, config=target.config)
+        self.draft_cache = TreeAppendCache(capacity + block_size, config=model.config)
         self.tree = kernels.DeviceTree.allocate(self.L, self.vocab, self.budget, device)
         self.accepted = torch.zeros((self.max_nodes,), dtype=torch.int64, device=device)
         self.accept_info = torch.zeros((2,), dtype=torch.int64, device=device)
@@ -443,25 +475,49 @@ class _DDTreeDecoder:
         self.tree_mask = TreeMask(target.dtype, device)
         self.readback = Readback(4 + 6 * self.max_nodes, device)
         self.tables: dict = {}
-        self.seed = device_sample_seed() if temperature >= 1e-5 else 0
-        self.clock = EventClock(device)
         self.hidden_buf = None
+        self.att_ws = None
         # static (device-length) mode: round state [start, ctx_offset, ctx_count, 0]
         self.rs_host = torch.zeros((4,), dtype=torch.int32, pin_memory=True)
         self.rs = torch.zeros((4,), dtype=torch.int32, device=device)
         self.static = (isinstance(model, DFlashDraftModel) and self.window is None
-                       and self.budget >= self.L and os.environ.get("DDTREE_EAGER", "0") != "1")
+                       and self.budget >= self.L and not eager)
         self.graphs = None
         self.graph_kernels = (0, 0)
-        self.replays = 0
-        self.capture_s = 0.0
         self.n_nodes = tree_node_count(self.budget, self.L, self.vocab)
         self.N = 1 + self.n_nodes
 
+    def start_call(self, input_ids, mask_token_id, max_new_tokens, stop_token_ids, temperature,
+                   save_tree_traces) -> None:
+        from .runtime import EventClock, device_sample_seed
+        self.P = input_ids.shape[1]
+        self.input_ids = input_ids
+        self.max_length = self.P + max_new_tokens
+        # the reference's buffer length, which bounds a draft block near the end
+        self.out_len = self.max_length + self.max_nodes
+        self.mask_token_id = mask_token_id
+        self.temperature = temperature
+        self.traces = save_tree_traces
+        self.stop_ids = None if stop_token_ids is None else set(int(t) for t in stop_token_ids)
+        self.seed = device_sample_seed() if temperature >= 1e-5 else 0
+        self.clock = EventClock(self.device)
+        self.replays = 0
+        self.capture_s = 0.0
+        self.output_ids.fill_(mask_token_id)
+        for cache in (self.target_cache, self.draft_cache):
+            cache.set_static(None)
+            for layer in cache.layers:
+                layer.reset()
+
     # ------------------------------------------------------------------ setup
     def _setup_static(self, features: torch.Tensor) -> None:
-        """After the prefill: both caches switch to device-offset appends and
-        the attention workspace is sized for the longest prefix."""
+        """After the prefill: both caches switch to device-offset appends; on
+        the session's first call the attention workspace (sized for the
+        longest prefix) and the static buffers are allocated."""
+        self.target_cache.set_static(self.rs[0:1])
+        self.draft_cache.set_static(self.rs[0:1])
+        if self.att_ws is not None:
+            return
         t, d = self.target.config, self.model.config
         hq_t, hkv_t = t.num_attention_heads, t.num_key_value_heads
         hq_d, hkv_d = d.num_attention_heads, d.num_key_value_heads
@@ -470,8 +526,6 @@ class _DDTreeDecoder:
         ws_t = kernels.attention_workspace(self.N, hq_t, hkv_t, self.past_max_t, self.device)
         ws_d = kernels.attention_workspace(self.block, hq_d, hkv_d, self.past_max_d, self.device)
         self.att_ws = ws_t if ws_t.numel() >= ws_d.numel() else ws_d
-        self.target_cache.set_static(self.rs[0:1])
-        self.draft_cache.set_static(self.rs[0:1])
         self.ar_block = torch.arange(self.block, device=self.device)
         self.block_buf = torch.empty((1, self.block), dtype=torch.long, device=self.device)
         self.static_mask = self.tree_mask.static(self.tree.visibility[: self.N], self.rs[0:1], self.past_max_t,
@@ -484,10 +538,11 @@ class _DDTreeDecoder:
     # ------------------------------------------------------------------ stages
     def _draft_generic(self, start: int, target_hidden: torch.Tensor) -> torch.Tensor:
         from .model import apply_final_logit_softcapping
-        block = self.output_ids[:, start: start + self.block]
+        block = self.output_ids[:, start: min(start + self.block, self.out_len)]
         noise = self.target.model.embed_tokens(block)
         h = self.model(target_hidden=target_hidden, noise_embedding=noise,
-                       position_ids=self.position_ids[:, self.draft_cache.get_seq_length(): start + self.block],
+                       position_ids=self.position_ids[:, self.draft_cache.get_seq_length():
+                                                      min(start + self.block, self.out_len)],
                        past_key_values=self.draft_cache, use_cache=True, is_causal=False)
         logits = self.target.lm_head(h[:, -self.L:, :])
         logits = apply_final_logit_softcapping(logits, self.model.final_logit_softcapping)
@@ -548,8 +603,10 @@ class _DDTreeDecoder:
         self.output_ids[:, :P] = self.input_ids
         self.output_ids[:, P: P + 1] = kernels.sample(output.logits, self.temperature)
         target_hidden = extract_context_feature(output.hidden_states, self.model.target_layer_ids)
-        self.hidden_buf = torch.zeros((self.max_nodes, target_hidden.shape[-1]), dtype=target_hidden.dtype,
-                                      device=dev)
+        F = target_hidden.shape[-1]
+        if self.hidden_buf is None or self.hidden_buf.shape[-1] != F or self.hidden_buf.dtype != target_hidden.dtype:
+            self.hidden_buf = torch.zeros((self.max_nodes, F), dtype=target_hidden.dtype, device=dev)
+            self.graphs = None   # a captured draft reads this buffer
         if self.static:
             self._setup_static(target_hidden)
         ev_first = clock.mark()
@@ -639,26 +696,29 @@ class _DDTreeDecoder:
         num_output_tokens = output_ids.shape[1] - P
         clock.resolve(stage_times)
         total_decode_time = clock.seconds(ev_decode, ev_end)
-        self.graphs = None
         # kernels of this library run by the call: eager launches plus every
-        # replay of the captured ones
+        # replay of the captured ones (launches counted at a capture never ran)
         native = load().ddt_launch_count() - launches0 + self.replays * sum(self.graph_kernels) - \
-            sum(self.graph_kernels)
-        return SimpleNamespace(
-            output_ids=output_ids.cpu(),
-            num_input_tokens=P,
-            num_output_tokens=num_output_tokens,
-            time_to_first_token=clock.seconds(ev_prefill, ev_first),
-            time_per_output_token=total_decode_time / max(num_output_tokens, 1),
-            acceptance_lengths=acceptance,
-            decode_rounds=len(acceptance),
-            stage_times=stage_times,
-            round_timestamps=[clock.seconds(ev_round_clock, e) for e in round_ends],
-            round_trees=round_trees,
-            native_launches=int(native),
-            graph_rounds=self.replays,
-            graph_capture_s=self.capture_s,
-        )
+            (sum(self.graph_kernels) if self.capture_s > 0 else 0)
+        try:
+            return SimpleNamespace(
+                output_ids=output_ids.cpu(),
+                num_input_tokens=P,
+                num_output_tokens=num_output_tokens,
+                time_to_first_token=clock.seconds(ev_prefill, ev_first),
+                time_per_output_token=total_decode_time / max(num_output_tokens, 1),
+                acceptance_lengths=acceptance,
+                decode_rounds=len(acceptance),
+                stage_times=stage_times,
+                round_timestamps=[clock.seconds(ev_round_clock, e) for e in round_ends],
+                round_trees=round_trees,
+                native_launches=int(native),
+                graph_rounds=self.replays,
+                graph_capture_s=self.capture_s,
+            )
+        finally:
+            # the session lives on the target: drop the reference back to it
+            self.target = None
 
     def _accept_commit(self, logits: torch.Tensor, features: torch.Tensor, start: int, rnd: int) -> None:
         from .runtime import compact_on_device

@@ -106,6 +106,32 @@ def test_ddtree_generate_matches_reference(name, mode, decode_golden, monkeypatc
 
 
 @pytest.mark.gpu
+def test_session_reused_across_calls(decode_golden):
+    """A second call on the same models reuses the captured graphs (no new
+    capture) and gives the same result; a longer call gets a new session."""
+    from ddtree_eagle3_patch_b200.ddtree import ddtree_generate, release_decode_sessions
+    z = decode_golden
+    name = "v16_b8_t32"
+    p = name + "_"
+    tgt, drf, vocab, block, budget, plen, max_new = _models(name, z)
+    tgt, drf = tgt.to(DEV), drf.to(DEV)
+    ids = torch.from_numpy(z[p + "prompt"]).to(DEV)
+    kw = dict(mask_token_id=vocab - 1, max_new_tokens=max_new, block_size=block, stop_token_ids=None,
+              tree_budget=budget)
+    r1 = ddtree_generate(drf, tgt, ids, **kw)
+    assert r1.graph_capture_s > 0
+    r2 = ddtree_generate(drf, tgt, ids, **kw)
+    assert r2.graph_capture_s == 0 and r2.graph_rounds == r2.decode_rounds - 1
+    assert r2.output_ids.tolist() == z[p + "output_ids"].tolist() == r1.output_ids.tolist()
+    assert r2.acceptance_lengths == r1.acceptance_lengths
+    # a different prompt on the same session
+    r3 = ddtree_generate(drf, tgt, ids[:, 3:], **kw)
+    assert r3.graph_capture_s == 0 and r3.num_input_tokens == plen - 3
+    release_decode_sessions(tgt)
+    assert "_ddtree_session" not in tgt.__dict__
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("name", [c[0] for c in C.CASES])
 def test_ddtree_generate_stop_token_matches_reference(name, decode_golden):
     from ddtree_eagle3_patch_b200.ddtree import ddtree_generate
