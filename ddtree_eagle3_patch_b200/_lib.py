@@ -97,6 +97,9 @@ _SIGNATURES = {
                                                _c_i64, _c_i64, _c_p, _c_p]),
     "ddt_silu_mul": (ctypes.c_int, [_c_p, _c_p, _c_p, ctypes.c_int, _c_i64, _c_p]),
     "ddt_silu_mul_rows": (ctypes.c_int, [_c_p, _c_p, _c_i64, _c_p, _c_i64, _c_i64, _c_i64, ctypes.c_int, _c_p]),
+    "ddt_wgemm_workspace_size": (ctypes.c_size_t, [_c_i64, _c_i64, _c_i64]),
+    "ddt_wgemm": (ctypes.c_int, [_c_p, _c_i64, _c_i64, _c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_p, _c_i64, _c_i64,
+                                 _c_p, ctypes.c_size_t, _c_p]),
     "ddt_tree_accept_workspace_size": (ctypes.c_size_t, [_c_i64, _c_i64]),
     "ddt_tree_accept": (ctypes.c_int, [_c_p, ctypes.c_int, _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_p,
                                        _c_i64, _c_p, _c_p, ctypes.c_size_t, _c_p]),

@@ -18,7 +18,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libddtree_b200.so"
 SOURCES = ["capi.cu", "tree_build.cu", "accept.cu", "attention.cu", "attention_f32.cu", "cache.cu", "fused.cu",
-           "mask.cu", "sample.cu"]
+           "mask.cu", "sample.cu", "wgemm.cu"]
 HEADERS = ["common.cuh", "sm100.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -23,6 +23,7 @@ import torch
 
 from . import kernels
 from ._lib import DDT_INFO_NONFINITE, DDTreeError
+from .fused_layers import head_logits
 
 DDTREE_STAGE_ORDER = ("draft", "tree_build", "tree_compile", "verify", "commit")
 DDTREE_TREE_BUILD_STAGE_ORDER = ("tree_build_copy", "tree_build_heap", "tree_build_visibility")
@@ -559,7 +560,7 @@ class _DDTreeDecoder:
         ar_c = self.ar_block if C == self.block else torch.arange(C, device=self.device)
         pos = torch.cat([self.rs[1:2].long() + ar_c, start + self.ar_block]).unsqueeze(0)
         h = self.model.forward_static(noise, ctx_hidden, pos, self.draft_cache, self.rs, self.past_max_d, self.att_ws)
-        logits = self.target.lm_head(h[:, -self.L:, :])
+        logits = head_logits(self.target.lm_head, h[:, -self.L:, :])
         return apply_final_logit_softcapping(logits, self.model.final_logit_softcapping)
 
     def _verify(self, start: int, mask):

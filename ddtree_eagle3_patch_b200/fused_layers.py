@@ -81,6 +81,34 @@ def packed_weights(layer):
     return cached[1], cached[2]
 
 
+def residual_linear(a: torch.Tensor, w: torch.Tensor, residual: torch.Tensor) -> torch.Tensor:
+    """residual + a @ w.T, rounded once (``torch.addmm``).  bf16 decode
+    shapes run on the weight-streaming tcgen05 GEMM with the residual added
+    in its epilogue (the o_proj and down_proj of a layer: at 33 rows it
+    streams 21 / 50 MB of weights in 9.4 / 14.1 us against cuBLAS's 10.2 /
+    16.7 us on B200); anything else on cuBLAS.  ``DDTREE_WGEMM=0`` keeps
+    cuBLAS."""
+    if os.environ.get("DDTREE_WGEMM", "1") != "0" and kernels.wgemm_supported(a, w) \
+            and residual.dtype == torch.bfloat16 and residual.stride(1) == 1:
+        return kernels.wgemm(a, w, residual=residual)
+    return torch.addmm(residual, a, w.t())
+
+
+def head_logits(lm_head, h: torch.Tensor) -> torch.Tensor:
+    """``lm_head(h)`` for the draft rows of a round ([1, L, hidden]).  A
+    bias-free bf16 head runs on the weight-streaming GEMM (Qwen3-4B's
+    151936 x 2560 head at 15 rows: 116 us against cuBLAS's 129 us on
+    B200); anything else calls the module.  ``DDTREE_WGEMM=0`` keeps the
+    module."""
+    w = getattr(lm_head, "weight", None)
+    if (os.environ.get("DDTREE_WGEMM", "1") != "0" and isinstance(lm_head, torch.nn.Linear)
+            and lm_head.bias is None and h.dim() == 3 and h.shape[0] == 1):
+        x = h[0]
+        if kernels.wgemm_supported(x, w):
+            return kernels.wgemm(x, w).unsqueeze(0)
+    return lm_head(h)
+
+
 def _fused_forward(self, hidden_states, attention_mask=None, position_ids=None, past_key_values=None,
                    use_cache=False, position_embeddings=None, **kwargs):
     past_dev = getattr(attention_mask, "ddtree_past_dev", None) if torch.is_tensor(attention_mask) else None
@@ -107,7 +135,7 @@ def _fused_forward(self, hidden_states, attention_mask=None, position_ids=None, 
     o = kernels.tree_attention(qr, cache._k[0], cache._v[0], attention_mask.ddtree_past_max,
                                attention_mask.ddtree_bits, attn.scaling, past_dev=past_dev,
                                workspace=attention_mask.ddtree_workspace)
-    x2 = torch.addmm(x, o.view(T, -1), attn.o_proj.weight.t())
+    x2 = residual_linear(o.view(T, -1), attn.o_proj.weight, x)
     h2 = kernels.rms_norm(x2, self.post_attention_layernorm.weight, self.post_attention_layernorm.variance_epsilon)
     if packed is not None:
         gu = F.linear(h2, packed[1])
@@ -115,7 +143,7 @@ def _fused_forward(self, hidden_states, attention_mask=None, position_ids=None, 
         a = kernels.silu_mul(gu[:, :inter], gu[:, inter:])
     else:
         a = kernels.silu_mul(F.linear(h2, mlp.gate_proj.weight), F.linear(h2, mlp.up_proj.weight))
-    return x2.addmm_(a, mlp.down_proj.weight.t()).unsqueeze(0)
+    return residual_linear(a, mlp.down_proj.weight, x2).unsqueeze(0)
 
 
 def _decoder_layers(model):

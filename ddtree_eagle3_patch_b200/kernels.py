@@ -342,6 +342,65 @@ def silu_mul(gate: torch.Tensor, up: torch.Tensor, out: torch.Tensor | None = No
     return out
 
 
+_WGEMM_WS_BYTES = 4096
+_WGEMM_WS: dict = {}
+
+
+def _wgemm_workspace(device: torch.device) -> torch.Tensor:
+    """One fixed, zero-filled scratch per device holding the status word of
+    ``wgemm`` (split-K partials are reduced across the cluster in shared
+    memory, so nothing else is needed); allocated once and never replaced,
+    so launches captured into a graph keep a valid address."""
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    ws = _WGEMM_WS.get(index)
+    if ws is None:
+        ws = torch.zeros(_WGEMM_WS_BYTES, dtype=torch.uint8, device=device)
+        _WGEMM_WS[index] = ws
+    return ws
+
+
+def wgemm_supported(x: torch.Tensor, w: torch.Tensor) -> bool:
+    """Shapes the weight-streaming GEMM takes: bf16, 1-64 rows of x, weight
+    rows a multiple of 128, K a multiple of 64, 16-byte aligned rows."""
+    return (x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and x.dim() == 2 and w.dim() == 2
+            and 1 <= x.shape[0] <= 64 and w.shape[0] % 128 == 0 and w.shape[1] % 64 == 0 and x.shape[1] == w.shape[1]
+            and x.stride(1) == 1 and w.stride(1) == 1 and x.stride(0) % 8 == 0 and w.stride(0) % 8 == 0
+            and x.data_ptr() % 16 == 0 and w.data_ptr() % 16 == 0 and x.is_cuda and w.is_cuda)
+
+
+def wgemm(x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor | None = None,
+          out: torch.Tensor | None = None, splits: int = 0) -> torch.Tensor:
+    """y = x @ w.T (+ residual) on the weight-streaming tcgen05 GEMM
+    (``ddt_wgemm``): x [T <= 64, K], w [N, K] bf16; the residual is added in
+    fp32 before the one rounding, as ``torch.addmm`` does."""
+    if not wgemm_supported(x, w):
+        raise ValueError("wgemm: unsupported shapes / layout (see wgemm_supported)")
+    T, K = x.shape
+    N = w.shape[0]
+    if out is None:
+        out = torch.empty((T, N), dtype=torch.bfloat16, device=x.device)
+    if residual is not None and (residual.dtype != torch.bfloat16 or residual.stride(1) != 1
+                                 or tuple(residual.shape) != (T, N)):
+        raise ValueError("residual must be [T, N] bf16 with contiguous rows")
+    if out.dtype != torch.bfloat16 or out.stride(1) != 1 or tuple(out.shape) != (T, N):
+        raise ValueError("out must be [T, N] bf16 with contiguous rows")
+    lib = _lib.load()
+    need = lib.ddt_wgemm_workspace_size(T, N, K)
+    ws = _wgemm_workspace(x.device)
+    if need > ws.numel():
+        raise ValueError(f"wgemm workspace of {ws.numel()} bytes is smaller than the {need} needed")
+    rc = lib.ddt_wgemm(x.data_ptr(), x.stride(0), T, w.data_ptr(), w.stride(0), N, K, ptr(residual),
+                       0 if residual is None else residual.stride(0), out.data_ptr(), out.stride(0), int(splits),
+                       ws.data_ptr(), ws.numel(), _lib.raw_stream(x.device.index))
+    check(rc, "ddt_wgemm")
+    return out
+
+
+def wgemm_status(device: torch.device) -> int:
+    """Status word of the wgemm scratch (0 = no bounded wait ran out)."""
+    return int(_wgemm_workspace(device)[:4].view(torch.int32).item())
+
+
 def kv_append(k_src: torch.Tensor, v_src: torch.Tensor, k_dst: torch.Tensor, v_dst: torch.Tensor,
               offset_dev: torch.Tensor, rows_dev: torch.Tensor | None = None) -> None:
     """Copy rows [0, rows) of k_src / v_src ([..., heads, rows, dim]) into

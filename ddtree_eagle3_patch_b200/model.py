@@ -197,7 +197,7 @@ class DFlashDecoderLayer(nn.Module):
             h = hidden_states + self.self_attn.forward_static(self.input_layernorm(hidden_states), target_hidden,
                                                               position_embeddings, cache, rs, past_max, workspace)
             return h + self.mlp(self.post_attention_layernorm(h))
-        from .fused_layers import packed_weights
+        from .fused_layers import packed_weights, residual_linear
         attn, mlp = self.self_attn, self.mlp
         x, c = hidden_states[0], target_hidden[0]
         T = x.shape[0]
@@ -225,7 +225,7 @@ class DFlashDecoderLayer(nn.Module):
         bits = _all_visible_bits(T, x.device)
         o = kernels.tree_attention(qr, layer_cache._k[0], layer_cache._v[0], past_max, bits, attn.scaling,
                                    past_dev=rs[0:1], workspace=workspace)
-        x2 = torch.addmm(x, o.view(T, -1), attn.o_proj.weight.t())
+        x2 = residual_linear(o.view(T, -1), attn.o_proj.weight, x)
         h2 = kernels.rms_norm(x2, self.post_attention_layernorm.weight, self.post_attention_layernorm.variance_epsilon)
         if packed is not None:
             gu = F.linear(h2, packed[1])
@@ -233,7 +233,7 @@ class DFlashDecoderLayer(nn.Module):
             a = kernels.silu_mul(gu[:, :inter], gu[:, inter:])
         else:
             a = kernels.silu_mul(F.linear(h2, mlp.gate_proj.weight), F.linear(h2, mlp.up_proj.weight))
-        return x2.addmm_(a, mlp.down_proj.weight.t()).unsqueeze(0)
+        return residual_linear(a, mlp.down_proj.weight, x2).unsqueeze(0)
 
 
 class DFlashDraftModel(Qwen3PreTrainedModel):

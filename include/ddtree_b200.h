@@ -323,6 +323,24 @@ DDT_API int ddt_silu_mul(const void* gate, const void* up, void* out, int dtype,
 DDT_API int ddt_silu_mul_rows(const void* gate, const void* up, int64_t in_row_stride, void* out,
                               int64_t out_row_stride, int64_t rows, int64_t cols, int dtype, ddt_stream_t stream);
 
+/* Weight-streaming GEMM for the projections of the verify and draft
+ * forwards (the target's and the draft's linear layers and lm_head run by
+ * ddtree.py:476-486 and :523-531), at decode sizes:
+ *   y[t, n] = sum_k x[t, k] * w[n, k] (+ residual[t, n]),   0 < T <= 64,
+ * bf16 in and out, fp32 accumulation on the tensor cores, the residual added
+ * in fp32 before the single rounding (torch.addmm).  N a multiple of 128, K
+ * of 64; x and w 16-byte aligned with row strides of multiples of 8
+ * elements (strides in elements).  The K range is split across up to 8
+ * CTAs of a thread-block cluster (splits 0 = chosen from the shape and the
+ * SM count, else the caller's count, capped at 8 and at K / 64), whose
+ * partials are summed in cluster-rank order, so results do not depend on
+ * timing.  Workspace: the status word, zero-filled once,
+ * ddt_wgemm_workspace_size bytes, 256-byte aligned. */
+DDT_API size_t ddt_wgemm_workspace_size(int64_t T, int64_t N, int64_t K);
+DDT_API int ddt_wgemm(const void* x, int64_t x_stride, int64_t T, const void* w, int64_t w_stride, int64_t N,
+                      int64_t K, const void* residual /* nullable */, int64_t r_stride, void* y, int64_t y_stride,
+                      int64_t splits, void* workspace, size_t workspace_bytes, ddt_stream_t stream);
+
 /* ---------------------------------------------------------------------------
  * EAGLE3 path acceptance.  Replaces evaluate_eagle3_posterior
  * (eagle3.py:46-79) for temperature 0: argmax of every verify row, the

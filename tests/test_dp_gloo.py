@@ -128,20 +128,23 @@ def _failing_worker(rank: int, world: int, port: int, mode: str, out):
     from datetime import timedelta
     from ddtree_eagle3_patch_b200 import distributed as dist
     dist.init(backend="gloo", timeout=timedelta(seconds=3))
-    dist.gather_counters([1.0, 2.0])            # step 1 completes on both ranks
-    if rank == 1:
-        if mode == "exit":
-            os._exit(0)
-        if mode == "raise":
-            raise RuntimeError("rank 1 failed between steps")
-        time.sleep(60)                           # stall: never joins step 2
-        os._exit(0)
     t0 = time.perf_counter()
     try:
+        dist.gather_counters([1.0, 2.0])        # step 1 on both ranks
+        if rank == 1:
+            time.sleep(0.5)                      # let rank 0 finish receiving step 1
+            if mode == "exit":
+                os._exit(0)
+            if mode == "raise":
+                raise RuntimeError("rank 1 failed between steps")
+            time.sleep(60)                       # stall: never joins step 2
+            os._exit(0)
+        t0 = time.perf_counter()
         dist.gather_counters([3.0, 4.0])        # step 2: the peer is gone
         out.put(("no error", time.perf_counter() - t0))
     except Exception as exc:                    # noqa: BLE001 - any error type is a detected failure
-        out.put((type(exc).__name__, time.perf_counter() - t0))
+        if rank == 0:
+            out.put((type(exc).__name__, time.perf_counter() - t0))
     os._exit(0)
 
 
