@@ -518,6 +518,7 @@ def run_kernel_only(args, local):
     w = Workload(device, seed=1000)
     tree = kernels.tree_build(w.draft[0], BUDGET)
     lp, ids = tree.top_lp.clone(), tree.top_ids.clone()
+    exp_tree = kernels.DeviceTree.allocate(ROWS, lp.shape[1], BUDGET, device)   # outputs reused every launch
     acc, info, post = kernels.tree_accept(w.verify[0], tree.parents, tree.node_token_ids, tree.info,
                                           max_accept=ROWS + 1)
     tensors = [t for pair in zip(w.ks, w.vs) for t in pair]
@@ -534,7 +535,7 @@ def run_kernel_only(args, local):
             # temperature 1 draw of every verify row (the accept path at temperature > 0)
             kernels.sample_rows(w.verify[i % 2], 1.0, seed=1234, offset=i, out=acc_bufs_sample)
         elif args.kernel == "expand":
-            kernels.tree_from_log_probs(lp, ids, BUDGET)
+            kernels.tree_from_log_probs(lp, ids, BUDGET, out=exp_tree)
         elif args.kernel == "accept":
             # the step's own preallocated outputs: no allocation or fill per launch
             kernels.tree_accept(w.verify[i % 2], tree.parents, tree.node_token_ids, tree.info, max_accept=ROWS + 1,

@@ -85,8 +85,8 @@ _SIGNATURES = {
                                        _c_p]),
     "ddt_tree_attention_window": (ctypes.c_int, [ctypes.POINTER(AttentionArgs), _c_p, _c_p, ctypes.c_size_t, _c_p]),
     "ddt_tree_attention_f32": (ctypes.c_int, [ctypes.POINTER(AttentionArgs), _c_p, _c_p, _c_p]),
-    "ddt_tree_attention_dev": (ctypes.c_int, [ctypes.POINTER(AttentionArgs), _c_p, _c_p, _c_p, ctypes.c_size_t,
-                                              _c_p]),
+    "ddt_tree_attention_dev": (ctypes.c_int, [ctypes.POINTER(AttentionArgs), _c_p, _c_p, _c_p, _c_p,
+                                              ctypes.c_size_t, _c_p]),
     "ddt_kv_append": (ctypes.c_int, [_c_p, _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
                                      _c_i64, _c_p, _c_p, _c_p]),
     "ddt_rms_norm": (ctypes.c_int, [_c_p, ctypes.c_int, _c_i64, _c_p, _c_p, _c_i64, _c_i64, _c_i64, ctypes.c_float,
@@ -100,6 +100,9 @@ _SIGNATURES = {
     "ddt_wgemm_workspace_size": (ctypes.c_size_t, [_c_i64, _c_i64, _c_i64]),
     "ddt_wgemm": (ctypes.c_int, [_c_p, _c_i64, _c_i64, _c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_p, _c_i64, _c_i64,
                                  _c_p, ctypes.c_size_t, _c_p]),
+    "ddt_wgemm_gate_up": (ctypes.c_int, [_c_p, _c_i64, _c_i64, _c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_i64, _c_p,
+                                         ctypes.c_size_t, _c_p]),
+    "ddt_set_pdl": (ctypes.c_int, [ctypes.c_int]),
     "ddt_tree_accept_workspace_size": (ctypes.c_size_t, [_c_i64, _c_i64]),
     "ddt_tree_accept": (ctypes.c_int, [_c_p, ctypes.c_int, _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_p,
                                        _c_i64, _c_p, _c_p, ctypes.c_size_t, _c_p]),

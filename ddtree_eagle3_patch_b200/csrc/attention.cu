@@ -460,6 +460,11 @@ struct Params {
     // it) and the kernel reads the actual prefix here, clamped to [0, past]:
     // CTAs whose key tiles lie past the actual keys exit at once.
     const int32_t* past_dev;
+    // Keys [0, stable) are written by no kernel still running on the stream:
+    // K tiles wholly below it load before griddepcontrol.wait.  Read from
+    // stable_dev at run time when set (clamped to [0, past]), else `stable`.
+    const int32_t* stable_dev;
+    int stable;
 };
 
 // Prefix length and key-tile count of this launch (see Params::past_dev).
@@ -700,9 +705,9 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
             // each TMA copy, MMA and commit.
             const bool leader = elect_one_sync();
             // ------------------------------------------------------------ loads
-            // K tiles that hold only prefix keys were written before this step,
-            // so they load before the preceding kernel in the stream has
-            // finished; Q and a K tile holding the tree's own keys load after.
+            // K tiles that hold only stable keys (Params::stable) load before
+            // the preceding kernel in the stream has finished; Q and every
+            // other K tile load after it.
             // V is not needed before the first softmax ends: its tiles load
             // once Q and K_0 have landed and the first S products are queued,
             // so the S products' operands are not queued behind V in the
@@ -722,7 +727,10 @@ tree_attn_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
                 tma_load_3d_hint(vb, &tv, 0, key0, g, &bars[bV0 + j], kv_policy);
                 tma_load_3d_hint(vb + kHalf, &tv, 64, key0, g, &bars[bV0 + j], kv_policy);
             };
-            auto prefix_only = [&](int j) { return (kt0 + j + 1) * BN <= past; };
+            int stable = p.stable;
+            if (p.stable_dev) stable = __ldg(p.stable_dev);
+            stable = stable < 0 ? 0 : (stable > past ? past : stable);
+            auto prefix_only = [&](int j) { return (kt0 + j + 1) * BN <= stable; };
             if (leader) {
                 prefetch_tmap(&tk);
                 prefetch_tmap(&tv);
@@ -1310,7 +1318,8 @@ using namespace ddt::attn;
 // kv_rows (rows past the run-time tree are masked by the tree bits and hold
 // the caller's finite cache contents, so P = 0 never meets a NaN).
 static int launch_split(const ddt_attention_args* a, const int64_t* key_lo, const int32_t* past_dev,
-                        const SplitPlan& sp, void* workspace, size_t workspace_bytes, ddt_stream_t stream) {
+                        const int32_t* stable_dev, const SplitPlan& sp, void* workspace, size_t workspace_bytes,
+                        ddt_stream_t stream) {
     if (!workspace || workspace_bytes < sp.ws_bytes || reinterpret_cast<uintptr_t>(workspace) % 256)
         return set_error(DDT_EWORKSPACE, "attention workspace needs %zu bytes (256-aligned), got %zu", sp.ws_bytes,
                          workspace_bytes);
@@ -1363,6 +1372,11 @@ static int launch_split(const ddt_attention_args* a, const int64_t* key_lo, cons
     q.o_stride_head = a->o_stride_head;
     q.status = reinterpret_cast<int*>(ws);
     q.past_dev = past_dev;
+    // Host-length calls: the whole prefix is stable unless this library's
+    // own kernels may be running ahead of this one (ddt_set_pdl), when no
+    // key loads early.  Device-length calls: what the caller states.
+    q.stable_dev = stable_dev;
+    q.stable = (past_dev || pdl_enabled()) ? 0 : (int)a->past_length;
     q.part_o = nullptr;
     q.part_lse = nullptr;
     if (sp.splits > 1) {
@@ -1420,7 +1434,8 @@ extern "C" size_t ddt_tree_attention_workspace_size(int64_t n_tokens, int64_t hq
 }
 
 static int tree_attention_impl(const ddt_attention_args* a, const int64_t* key_lo, const int32_t* past_dev,
-                               void* workspace, size_t workspace_bytes, ddt_stream_t stream) {
+                               const int32_t* stable_dev, void* workspace, size_t workspace_bytes,
+                               ddt_stream_t stream) {
     if (!a) return set_error(DDT_EINVAL, "args is null");
     if (!a->q || !a->k || !a->v || !a->out || !a->visibility) return set_error(DDT_EINVAL, "null tensor pointer");
     if (a->head_dim != HD) return set_error(DDT_EUNSUPPORTED, "head_dim %lld (only 128)", (long long)a->head_dim);
@@ -1450,13 +1465,13 @@ static int tree_attention_impl(const ddt_attention_args* a, const int64_t* key_l
             return set_error(DDT_EUNSUPPORTED, "a run-time prefix needs the split kernel: %lld rows x %lld KV heads "
                              "at prefix <= %lld do not fit it", (long long)(a->n_tokens * group),
                              (long long)a->hkv, (long long)a->past_length);
-        return launch_split(a, key_lo, past_dev, sp, workspace, workspace_bytes, stream);
+        return launch_split(a, key_lo, past_dev, stable_dev, sp, workspace, workspace_bytes, stream);
     }
     const Plan pl = plan_for(a->n_tokens, a->hq, a->hkv, a->past_length, ddt_sm_count(dev));
     if (!workspace || workspace_bytes < pl.ws_bytes || reinterpret_cast<uintptr_t>(workspace) % 256)
         return set_error(DDT_EWORKSPACE, "attention workspace needs %zu bytes (256-aligned), got %zu", pl.ws_bytes,
                          workspace_bytes);
-    if (sp.usable) return launch_split(a, key_lo, nullptr, sp, workspace, workspace_bytes, stream);
+    if (sp.usable) return launch_split(a, key_lo, nullptr, nullptr, sp, workspace, workspace_bytes, stream);
     CUtensorMap tq, tk, tv;
     int rc = make_map(&tq, a->q, HD, a->hq, a->n_tokens, a->q_stride_head * 2, a->q_stride_tok * 2, 64,
                       (uint32_t)group, (uint32_t)pl.tpt);
@@ -1516,20 +1531,23 @@ static int tree_attention_impl(const ddt_attention_args* a, const int64_t* key_l
 
 extern "C" int ddt_tree_attention(const ddt_attention_args* a, void* workspace, size_t workspace_bytes,
                                   ddt_stream_t stream) {
-    return tree_attention_impl(a, nullptr, nullptr, workspace, workspace_bytes, stream);
+    return tree_attention_impl(a, nullptr, nullptr, nullptr, workspace, workspace_bytes, stream);
 }
 
 extern "C" int ddt_tree_attention_window(const ddt_attention_args* a, const int64_t* key_lo, void* workspace,
                                          size_t workspace_bytes, ddt_stream_t stream) {
     if (!key_lo) return set_error(DDT_EINVAL, "key_lo is null");
     if (reinterpret_cast<uintptr_t>(key_lo) % alignof(int64_t)) return set_error(DDT_EINVAL, "key_lo must be 8-byte aligned");
-    return tree_attention_impl(a, key_lo, nullptr, workspace, workspace_bytes, stream);
+    return tree_attention_impl(a, key_lo, nullptr, nullptr, workspace, workspace_bytes, stream);
 }
 
 extern "C" int ddt_tree_attention_dev(const ddt_attention_args* a, const int64_t* key_lo, const int32_t* past_dev,
-                                      void* workspace, size_t workspace_bytes, ddt_stream_t stream) {
+                                      const int32_t* stable_dev, void* workspace, size_t workspace_bytes,
+                                      ddt_stream_t stream) {
     if (!past_dev) return set_error(DDT_EINVAL, "past_dev is null");
     if (key_lo && reinterpret_cast<uintptr_t>(key_lo) % alignof(int64_t))
         return set_error(DDT_EINVAL, "key_lo must be 8-byte aligned");
-    return tree_attention_impl(a, key_lo, past_dev, workspace, workspace_bytes, stream);
+    if (stable_dev && reinterpret_cast<uintptr_t>(stable_dev) % alignof(int32_t))
+        return set_error(DDT_EINVAL, "stable_dev must be 4-byte aligned");
+    return tree_attention_impl(a, key_lo, past_dev, stable_dev, workspace, workspace_bytes, stream);
 }

@@ -23,6 +23,8 @@ kv_append_kernel(const unsigned char* __restrict__ k_src, const unsigned char* _
                  int64_t s_head, int64_t s_row, unsigned char* k_dst, unsigned char* v_dst, int64_t d_head,
                  int64_t d_row, int64_t dst_rows, int rows, int row_bytes, const int32_t* offset_dev,
                  const int32_t* rows_dev) {
+    griddep_launch_dependents();
+    griddep_wait();
     const int h = blockIdx.x >> 1;
     const bool is_v = blockIdx.x & 1;
     const int off = __ldg(offset_dev);
@@ -65,9 +67,10 @@ extern "C" int ddt_kv_append(const void* k_src, const void* v_src, int64_t src_h
         return set_error(DDT_EINVAL, "row strides smaller than a row");
     if (reinterpret_cast<uintptr_t>(offset_dev) % 4 || (rows_dev && reinterpret_cast<uintptr_t>(rows_dev) % 4))
         return set_error(DDT_EINVAL, "offset_dev / rows_dev must be 4-byte aligned");
-    cache::kv_append_kernel<<<(unsigned)(2 * heads), cache::kThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-        static_cast<const unsigned char*>(k_src), static_cast<const unsigned char*>(v_src), src_head_stride_bytes,
-        src_row_stride_bytes, static_cast<unsigned char*>(k_dst), static_cast<unsigned char*>(v_dst),
-        dst_head_stride_bytes, dst_row_stride_bytes, dst_rows, (int)rows, (int)row_bytes, offset_dev, rows_dev);
+    launch_k(cache::kv_append_kernel, dim3((unsigned)(2 * heads)), dim3(cache::kThreads), 0,
+             reinterpret_cast<cudaStream_t>(stream), static_cast<const unsigned char*>(k_src),
+             static_cast<const unsigned char*>(v_src), src_head_stride_bytes, src_row_stride_bytes,
+             static_cast<unsigned char*>(k_dst), static_cast<unsigned char*>(v_dst), dst_head_stride_bytes,
+             dst_row_stride_bytes, dst_rows, (int)rows, (int)row_bytes, offset_dev, rows_dev);
     return check_launch("kv_append_kernel");
 }

@@ -29,7 +29,21 @@ int check_launch(const char* what) {
     return DDT_OK;
 }
 
+// Programmatic dependent launch of the decode-layer kernels (ddt_set_pdl).
+static std::atomic<int> g_pdl{0};
+
+bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed) != 0; }
+
+unsigned pdl_attr(cudaLaunchAttribute* a) {
+    if (!g_pdl.load(std::memory_order_relaxed)) return 0;
+    a->id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    a->val.programmaticStreamSerializationAllowed = 1;
+    return 1;
+}
+
 }  // namespace ddt
+
+extern "C" int ddt_set_pdl(int enabled) { return ddt::g_pdl.exchange(enabled ? 1 : 0); }
 
 extern "C" const char* ddt_last_error(void) { return ddt::g_last_error; }
 

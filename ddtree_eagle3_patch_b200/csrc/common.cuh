@@ -15,6 +15,36 @@ namespace ddt {
 // Record an error message for ddt_last_error() and return the status.
 int set_error(int status, const char* fmt, ...);
 int check_launch(const char* what);
+// Fill *a with the programmatic-stream-serialization launch attribute and
+// return 1 while ddt_set_pdl(1) is in force; else return 0.
+unsigned pdl_attr(cudaLaunchAttribute* a);
+bool pdl_enabled();
+
+// Launch `kernel` on `st`, as a programmatic dependent launch while
+// ddt_set_pdl(1) is in force.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                     Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    cfg.numAttrs = pdl_attr(attr);
+    cfg.attrs = attr;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+}
+
+// Programmatic dependent launch: wait until the preceding grid in the
+// stream has completed and its memory is visible (returns at once when the
+// kernel was not launched as a dependent) ...
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// ... and let the next grid in the stream be scheduled once every CTA of this
+// grid has executed this (or exited).
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 
 // Order-preserving map of an fp32 bit pattern onto uint32 (larger float ->
 // larger integer; NaN with the sign bit clear maps above +inf).
@@ -44,6 +74,28 @@ template <>
 __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
 template <>
 __device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
+
+template <typename T>
+__device__ __forceinline__ T from_f32(float v);
+template <>
+__device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+template <>
+__device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
+
+// value rounded to T and back (identity for float)
+template <typename T>
+__device__ __forceinline__ float rnd(float v) { return to_f32<T>(from_f32<T>(v)); }
+
+// SiLU(g) * u for g, u already in T: silu rounded to T first, then the
+// product rounded, as torch's act_fn(gate) * up does in T.
+template <typename T>
+__device__ __forceinline__ T silu_times(T g, T u) {
+    const float gv = to_f32<T>(g);
+    const float s = rnd<T>(gv / (1.f + expf(-gv)));
+    return from_f32<T>(s * to_f32<T>(u));
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));

@@ -25,19 +25,6 @@
 namespace ddt {
 namespace fused {
 
-template <typename T>
-__device__ __forceinline__ T from_f32(float v);
-template <>
-__device__ __forceinline__ float from_f32<float>(float v) { return v; }
-template <>
-__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
-template <>
-__device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
-
-// value rounded to T and back (identity for float)
-template <typename T>
-__device__ __forceinline__ float rnd(float v) { return to_f32<T>(from_f32<T>(v)); }
-
 // ---------------------------------------------------------------------------
 // RMSNorm of rows whose 16-byte vectors fit VPT per thread: the row is read
 // once into registers, reduced, and written from registers.
@@ -45,6 +32,8 @@ template <typename T, int THREADS, int VPT>
 __global__ void __launch_bounds__(THREADS)
 rms_norm_vec_kernel(const T* __restrict__ x, int64_t x_stride, const T* __restrict__ w, T* __restrict__ y,
                     int64_t y_stride, int cols, float eps) {
+    griddep_launch_dependents();
+    griddep_wait();
     constexpr int E = 16 / sizeof(T);
     const int nv = cols / E;
     const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)blockIdx.x * x_stride);
@@ -93,6 +82,8 @@ template <typename T, int THREADS>
 __global__ void __launch_bounds__(THREADS)
 rms_norm_kernel(const T* __restrict__ x, int64_t x_stride, const T* __restrict__ w, T* __restrict__ y,
                 int64_t y_stride, int cols, float eps) {
+    griddep_launch_dependents();
+    griddep_wait();
     const T* xr = x + (int64_t)blockIdx.x * x_stride;
     T* yr = y + (int64_t)blockIdx.x * y_stride;
     float ss = 0.f;
@@ -177,6 +168,8 @@ __device__ __forceinline__ void norm_rope_head(const T* src, const T* w, float e
 template <typename T>
 __global__ void __launch_bounds__(256)
 qk_norm_rope_append_kernel(RopeParams p) {
+    griddep_launch_dependents();
+    griddep_wait();
     const int t = blockIdx.x;                       // K/V row: [0, a_rows) ctx, then b rows
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const bool is_b = t >= p.a_rows;
@@ -227,14 +220,7 @@ qk_norm_rope_append_kernel(RopeParams p) {
 }
 
 // ---------------------------------------------------------------------------
-// SiLU(gate) * up, elementwise (silu rounded to the dtype first, as torch's
-// act_fn(gate) * up does).
-template <typename T>
-__device__ __forceinline__ T silu_times(T g, T u) {
-    const float gv = to_f32<T>(g);
-    const float s = rnd<T>(gv / (1.f + expf(-gv)));
-    return from_f32<T>(s * to_f32<T>(u));
-}
+// SiLU(gate) * up, elementwise (silu_times in common.cuh).
 
 // grid (column blocks, rows): each thread one 16-byte vector of a row when
 // the row strides allow it, else one element
@@ -242,6 +228,8 @@ template <typename T, bool VEC>
 __global__ void __launch_bounds__(256)
 silu_mul_kernel(const T* __restrict__ g, const T* __restrict__ u, int64_t in_stride, T* __restrict__ out,
                 int64_t out_stride, int64_t rows, int64_t cols) {
+    griddep_launch_dependents();
+    griddep_wait();
     const int64_t r = blockIdx.y;
     const T* gr = g + r * in_stride;
     const T* ur = u + r * in_stride;
@@ -285,9 +273,9 @@ extern "C" int ddt_rms_norm(const void* x, int dtype, int64_t x_row_stride, cons
                      x_row_stride % per_vec == 0 && y_row_stride % per_vec == 0;
     const int64_t nvec = cols / per_vec;
 #define DDT_RMS_VEC(T, VPT)                                                                                         \
-    fused::rms_norm_vec_kernel<T, 256, VPT><<<(unsigned)rows, 256, 0, st>>>(                                         \
-        static_cast<const T*>(x), x_row_stride, static_cast<const T*>(weight), static_cast<T*>(y), y_row_stride,     \
-        (int)cols, eps)
+    launch_k(fused::rms_norm_vec_kernel<T, 256, VPT>, dim3((unsigned)rows), dim3(256), 0, st,                        \
+             static_cast<const T*>(x), x_row_stride, static_cast<const T*>(weight), static_cast<T*>(y),              \
+             y_row_stride, (int)cols, eps)
     if (vec && nvec <= 256 * 4 && (dtype == DDT_BF16 || dtype == DDT_F32 || dtype == DDT_F16)) {
         if (dtype == DDT_BF16) {
             if (nvec <= 512) DDT_RMS_VEC(__nv_bfloat16, 2); else DDT_RMS_VEC(__nv_bfloat16, 4);
@@ -299,18 +287,19 @@ extern "C" int ddt_rms_norm(const void* x, int dtype, int64_t x_row_stride, cons
 #undef DDT_RMS_VEC
         return check_launch("rms_norm_vec_kernel");
     }
+    const dim3 grid((unsigned)rows);
     if (dtype == DDT_BF16)
-        fused::rms_norm_kernel<__nv_bfloat16, 256><<<(unsigned)rows, 256, 0, st>>>(
-            static_cast<const __nv_bfloat16*>(x), x_row_stride, static_cast<const __nv_bfloat16*>(weight),
-            static_cast<__nv_bfloat16*>(y), y_row_stride, (int)cols, eps);
+        launch_k(fused::rms_norm_kernel<__nv_bfloat16, 256>, grid, dim3(256), 0, st,
+                 static_cast<const __nv_bfloat16*>(x), x_row_stride, static_cast<const __nv_bfloat16*>(weight),
+                 static_cast<__nv_bfloat16*>(y), y_row_stride, (int)cols, eps);
     else if (dtype == DDT_F32)
-        fused::rms_norm_kernel<float, 256><<<(unsigned)rows, 256, 0, st>>>(
-            static_cast<const float*>(x), x_row_stride, static_cast<const float*>(weight), static_cast<float*>(y),
-            y_row_stride, (int)cols, eps);
+        launch_k(fused::rms_norm_kernel<float, 256>, grid, dim3(256), 0, st, static_cast<const float*>(x),
+                 x_row_stride, static_cast<const float*>(weight), static_cast<float*>(y), y_row_stride, (int)cols,
+                 eps);
     else if (dtype == DDT_F16)
-        fused::rms_norm_kernel<__half, 256><<<(unsigned)rows, 256, 0, st>>>(
-            static_cast<const __half*>(x), x_row_stride, static_cast<const __half*>(weight),
-            static_cast<__half*>(y), y_row_stride, (int)cols, eps);
+        launch_k(fused::rms_norm_kernel<__half, 256>, grid, dim3(256), 0, st, static_cast<const __half*>(x),
+                 x_row_stride, static_cast<const __half*>(weight), static_cast<__half*>(y), y_row_stride, (int)cols,
+                 eps);
     else
         return set_error(DDT_EINVAL, "dtype %d", dtype);
     return check_launch("rms_norm_kernel");
@@ -368,11 +357,11 @@ extern "C" int ddt_qk_norm_rope_append(int dtype, const void* q_raw, int64_t q_r
     // one warp per head task: (K heads, V heads, Q heads) of a row over grid.y CTAs of 8 warps
     const dim3 grid((unsigned)(ctx_rows + new_rows), (unsigned)ceil_div(2 * hkv + hq, 8));
     if (dtype == DDT_BF16)
-        fused::qk_norm_rope_append_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(p);
+        launch_k(fused::qk_norm_rope_append_kernel<__nv_bfloat16>, grid, dim3(256), 0, st, p);
     else if (dtype == DDT_F32)
-        fused::qk_norm_rope_append_kernel<float><<<grid, 256, 0, st>>>(p);
+        launch_k(fused::qk_norm_rope_append_kernel<float>, grid, dim3(256), 0, st, p);
     else if (dtype == DDT_F16)
-        fused::qk_norm_rope_append_kernel<__half><<<grid, 256, 0, st>>>(p);
+        launch_k(fused::qk_norm_rope_append_kernel<__half>, grid, dim3(256), 0, st, p);
     else
         return set_error(DDT_EINVAL, "dtype %d", dtype);
     return check_launch("qk_norm_rope_append_kernel");
@@ -398,11 +387,11 @@ extern "C" int ddt_silu_mul_rows(const void* gate, const void* up, int64_t in_ro
 #define DDT_SILU(T)                                                                                                \
     do {                                                                                                           \
         if (vec)                                                                                                   \
-            fused::silu_mul_kernel<T, true><<<grid, 256, 0, st>>>(static_cast<const T*>(gate),                     \
-                static_cast<const T*>(up), in_row_stride, static_cast<T*>(out), out_row_stride, rows, cols);        \
+            launch_k(fused::silu_mul_kernel<T, true>, grid, dim3(256), 0, st, static_cast<const T*>(gate),         \
+                     static_cast<const T*>(up), in_row_stride, static_cast<T*>(out), out_row_stride, rows, cols);   \
         else                                                                                                       \
-            fused::silu_mul_kernel<T, false><<<grid, 256, 0, st>>>(static_cast<const T*>(gate),                    \
-                static_cast<const T*>(up), in_row_stride, static_cast<T*>(out), out_row_stride, rows, cols);        \
+            launch_k(fused::silu_mul_kernel<T, false>, grid, dim3(256), 0, st, static_cast<const T*>(gate),        \
+                     static_cast<const T*>(up), in_row_stride, static_cast<T*>(out), out_row_stride, rows, cols);   \
     } while (0)
     if (dtype == DDT_BF16)
         DDT_SILU(__nv_bfloat16);

@@ -199,13 +199,6 @@ __device__ __forceinline__ float ex2_approx(float x) {
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
 }
-// Programmatic dependent launch: wait until the preceding grid in the
-// stream has completed and its memory is visible (returns at once when the
-// kernel was not launched as a dependent) ...
-__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-// ... and let the next grid in the stream be scheduled once every CTA of this
-// grid has executed this (or exited).
-__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 // True in exactly one lane of a converged warp (the lowest active lane).
 __device__ __forceinline__ bool elect_one_sync() {
     uint32_t pred = 0;

@@ -235,7 +235,13 @@ struct ExpandSmem {
     int32_t* n_parent;   // node i: parent        (i in [0, budget])
     int32_t* n_dr;       //         depth << 16 | rank
     int32_t* scalars;    // [4]
+    unsigned char* par;  // table of the parallel expansion, or null
 };
+
+// the parallel expansion's limits (its table is sized for them)
+__host__ __device__ inline bool par_expand_fits(int64_t rows, int64_t budget) {
+    return budget <= 64 && rows <= 16;
+}
 
 __host__ __device__ inline size_t expand_smem_bytes(int64_t rows, int64_t topk, int64_t budget) {
     size_t o = 0;
@@ -243,6 +249,7 @@ __host__ __device__ inline size_t expand_smem_bytes(int64_t rows, int64_t topk, 
     o += align256(sizeof(double) * (budget + 1));
     o += align256(sizeof(int32_t) * (budget + 1)) * 4;
     o += 256;
+    if (par_expand_fits(rows, budget)) o += 96 * 1024;   // >= par_smem_bytes(), checked below
     return o;
 }
 
@@ -262,6 +269,8 @@ __device__ inline ExpandSmem carve_expand(unsigned char* base, int64_t rows, int
     e.n_dr = reinterpret_cast<int32_t*>(base + o);
     o += align256(sizeof(int32_t) * (budget + 1));
     e.scalars = reinterpret_cast<int32_t*>(base + o);
+    o += 256;
+    e.par = par_expand_fits(rows, budget) ? base + o : nullptr;
     return e;
 }
 
@@ -573,6 +582,285 @@ __device__ int expand_regs(const ExpandSmem& e, int rows, int topk, int budget, 
     return count;
 }
 
+// ---------------------------------------------------------------------------
+// Parallel form of the same expansion (budget <= 64, rows <= 16).
+//
+// Every frontier entry is created from the entry just popped: its sibling
+// fl(fl(S - a_r) + a_{r+1}) or its first child fl(S + a_0), where a is a
+// row of log-probs sorted descending and S <= a_r <= 0 is the popped path
+// score.  Both are never above S: a child adds a_0 <= 0; for a sibling,
+// S - a_r lies in [S, 0] on S's grid (a_r's float32 grid is no finer while
+// |S| < 2^29 |a_r|), so the first sum is exact and the second rounds
+// S - a_r + a_{r+1} <= S, a value below the representable S, to at most S.
+// With keys that never improve along the generating edges, the heap pops
+// the nodes in the global order of (score desc, ranks tuple asc), so the
+// popped set is the best `budget` nodes of the whole rank tree.
+//
+// Those are found depth by depth: the pool holds the best `budget` nodes
+// seen so far, sorted; each depth-(d-1) pool node (the root at d = 1)
+// generates its children's scores with the reference's sibling recurrence,
+// one thread per parent, while the child beats the pool's current last
+// entry (later siblings only get worse) and has fewer than `budget` nodes
+// on its generating path; the new nodes are merged into the pool by rank
+// counting.  A node dropped from the pool has `budget` better nodes, and so
+// has every node under it.  The ranks tuple is kept as a left-aligned
+// string of 7-bit fields (rank + 1 per depth), compared as two integers, so
+// ties of the score are decided exactly as Python's tuple order does.
+//
+// Each computed step is checked (no increase, finite); on a failed check,
+// or more nodes than the table holds, the serial loop below runs instead.
+// ---------------------------------------------------------------------------
+constexpr int kParMaxBudget = 64;
+constexpr int kParNodes = 1024;
+constexpr int kScratchStride = kParMaxBudget + 1;   // odd stride: the slots' rows fall in different banks
+
+struct ParSmem {
+    double* score;                 // [kParNodes] path score
+    unsigned long long* key;       //             ord_f64(-score): smaller = pops first
+    unsigned long long* phi;       //             ranks tuple, depths 1..9
+    unsigned long long* plo;       //             ranks tuple, depths 10..16
+    int32_t* parent;               //             node id of the parent, -1 = root
+    int32_t* dr;                   //             depth << 16 | rank
+    int32_t* acnt;                 //             nodes on the generating path before it
+    int32_t* pos;                  //             position in the final pool
+    int32_t* pool;                 // [kParMaxBudget] node ids, in pop order
+    int32_t* pool2;                // [kParMaxBudget] the next pool
+    double* scratch;               // [kParMaxBudget][kScratchStride] one depth's chain scores per pool slot
+    int32_t* ctl;                  // [4] flags, then [kParMaxBudget + 1] chain offsets
+};
+
+__host__ __device__ constexpr size_t par_smem_bytes() {
+    return ((sizeof(double) + 3 * sizeof(unsigned long long) + 4 * sizeof(int32_t)) * kParNodes + 255) / 256 * 256 +
+           (2 * sizeof(int32_t) * kParMaxBudget + 255) / 256 * 256 +
+           (sizeof(double) * kParMaxBudget * kScratchStride + 255) / 256 * 256 +
+           (sizeof(int32_t) * (4 + kParMaxBudget + 1) + 255) / 256 * 256;
+}
+static_assert(par_smem_bytes() <= 96 * 1024, "parallel expansion table exceeds its shared-memory share");
+
+__device__ inline ParSmem carve_par(unsigned char* base) {
+    ParSmem P;
+    size_t o = 0;
+    P.score = reinterpret_cast<double*>(base + o);
+    o += sizeof(double) * kParNodes;
+    P.key = reinterpret_cast<unsigned long long*>(base + o);
+    o += sizeof(unsigned long long) * kParNodes;
+    P.phi = reinterpret_cast<unsigned long long*>(base + o);
+    o += sizeof(unsigned long long) * kParNodes;
+    P.plo = reinterpret_cast<unsigned long long*>(base + o);
+    o += sizeof(unsigned long long) * kParNodes;
+    P.parent = reinterpret_cast<int32_t*>(base + o);
+    o += sizeof(int32_t) * kParNodes;
+    P.dr = reinterpret_cast<int32_t*>(base + o);
+    o += sizeof(int32_t) * kParNodes;
+    P.acnt = reinterpret_cast<int32_t*>(base + o);
+    o += sizeof(int32_t) * kParNodes;
+    P.pos = reinterpret_cast<int32_t*>(base + o);
+    o += sizeof(int32_t) * kParNodes;
+    o = align256(o);
+    P.pool = reinterpret_cast<int32_t*>(base + o);
+    P.pool2 = P.pool + kParMaxBudget;
+    o = align256(o + 2 * sizeof(int32_t) * kParMaxBudget);
+    P.scratch = reinterpret_cast<double*>(base + o);
+    o = align256(o + sizeof(double) * kParMaxBudget * kScratchStride);
+    P.ctl = reinterpret_cast<int32_t*>(base + o);
+    return P;
+}
+
+// (key, ranks tuple) order of two (key, hi, lo) triples
+__device__ __forceinline__ bool par_before(unsigned long long ka, unsigned long long ha, unsigned long long la,
+                                           unsigned long long kb, unsigned long long hb, unsigned long long lb) {
+    if (ka != kb) return ka < kb;
+    if (ha != hb) return ha < hb;
+    return la < lb;
+}
+__device__ __forceinline__ bool par_node_before(const ParSmem& P, int a, int b) {
+    return par_before(P.key[a], P.phi[a], P.plo[a], P.key[b], P.phi[b], P.plo[b]);
+}
+
+// Ranks tuple of a node at depth d with rank r under a parent's tuple.
+__device__ __forceinline__ void par_path(unsigned long long& h, unsigned long long& l, int d, int r) {
+    const unsigned long long f = (unsigned long long)(r + 1);
+    if (d <= 9)
+        h |= f << (56 - 7 * (d - 1));
+    else
+        l |= f << (56 - 7 * (d - 10));
+}
+
+__device__ __forceinline__ void par_store(const ParSmem& P, int id, double c, unsigned long long h,
+                                          unsigned long long l, int parent, int d, int r, int acnt) {
+    P.score[id] = c;
+    P.key[id] = ord_f64(-c);
+    P.phi[id] = h;
+    P.plo[id] = l;
+    P.parent[id] = parent;
+    P.dr[id] = (d << 16) | r;
+    P.acnt[id] = acnt;
+}
+
+// Scores of the children of pool node `parent` at depth d, best first, into
+// out[0..n) while they can still enter the pool (the reference's child and
+// sibling recurrences, ddtree.py:171, 176); returns n, or -1 on a step that
+// increases the score.  Only the score chain is serial: the entries are
+// written afterwards by all threads.
+__device__ int par_chain(const ExpandSmem& e, const ParSmem& P, int parent, int d, int topk, int budget, int tau,
+                         double* out) {
+    const float* row = e.lp + (d - 1) * topk;
+    const double S = P.score[parent];
+    const int a_p = P.acnt[parent];
+    double c = __dadd_rn(S, (double)row[0]);
+    if (!(c <= S)) return -1;
+    const bool full = tau >= 0;
+    unsigned long long th = 0ull, tl = 0ull, tk = 0ull;
+    unsigned long long h0 = P.phi[parent], l0 = P.plo[parent];
+    if (full) {
+        tk = P.key[tau];
+        th = P.phi[tau];
+        tl = P.plo[tau];
+    }
+    int n = 0;
+    for (int r = 0; r < topk && a_p + 1 + r < budget; ++r) {
+        if (full) {
+            unsigned long long h = h0, l = l0;
+            par_path(h, l, d, r);
+            if (!par_before(ord_f64(-c), h, l, tk, th, tl)) break;   // and so every later sibling
+        }
+        out[r] = c;
+        n = r + 1;
+        if (r + 1 < topk) {
+            const double c2 = __dadd_rn(__dadd_rn(c, -(double)row[r]), (double)row[r + 1]);
+            if (!(c2 <= c)) return -1;
+            c = c2;
+        }
+    }
+    return n;
+}
+
+// Runs on all threads of the CTA; returns the node count, or -1 when the
+// serial loop has to run instead.  Fills e.n_parent / e.n_dr like it.
+__device__ int expand_par(const ExpandSmem& e, const ParSmem& P, int rows, int topk, int budget) {
+    const int tid = threadIdx.x;
+    // finite log-probs, and row 0 sorted (the depth-1 scores below rely on it)
+    bool bad = false;
+    for (int i = tid; i < rows * topk; i += kThreads) {
+        const float v = e.lp[i];
+        bad |= !(fabsf(v) <= 3.402823466e38f);
+        if (i + 1 < topk) bad |= !(e.lp[i + 1] <= v);
+    }
+    if (__syncthreads_or(bad)) return -1;
+    if (tid == 0) P.ctl[2] = 0;
+    // Depth 1: the reference's first entry is lp[0,0] and each sibling step
+    // fl(fl(S - a_r) + a_{r+1}) with S = a_r gives a_{r+1} exactly, so node r
+    // scores lp[0, r]; that order (scores non-increasing, tuples increasing)
+    // is already the pop order.
+    int np = topk < budget ? topk : budget;
+    for (int r = tid; r < np; r += kThreads) {
+        unsigned long long h = 0ull, l = 0ull;
+        par_path(h, l, 1, r);
+        par_store(P, r, (double)e.lp[r], h, l, -1, 1, r, r);
+        P.pool[r] = r;
+    }
+    int nb = np;
+    double* scratch = P.scratch;
+    int* soff = P.ctl + 4;
+    __syncthreads();
+    for (int d = 2; d <= rows; ++d) {
+        const int tau = np == budget ? P.pool[budget - 1] : -1;
+        // (a) each depth-(d-1) pool node's chain, one thread per pool slot
+        if (tid < kParMaxBudget) {
+            int n = 0;
+            if (tid < np) {
+                const int id = P.pool[tid];
+                if ((P.dr[id] >> 16) == d - 1) n = par_chain(e, P, id, d, topk, budget, tau,
+                                                             scratch + tid * kScratchStride);
+            }
+            if (n < 0) atomicOr(&P.ctl[2], 1);
+            soff[tid + 1] = n < 0 ? 0 : n;
+        }
+        __syncthreads();
+        // (b) offsets of the chains (one warp)
+        if (tid < 32) {
+            const int a = soff[2 * tid + 1], b = soff[2 * tid + 2];
+            int s = a + b;
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(DDT_FULL_MASK, s, o);
+                if (tid >= o) s += v;
+            }
+            soff[2 * tid + 1] = s - b;
+            soff[2 * tid + 2] = s;
+            if (tid == 0) soff[0] = 0;
+        }
+        __syncthreads();
+        if (P.ctl[2]) return -1;
+        const int m = soff[kParMaxBudget];
+        if (m == 0) break;   // no node at depth d: none deeper either
+        if (nb + m > kParNodes) return -1;
+        const int ne = nb + m;
+        // (c) the new entries, all threads
+        for (int x = tid; x < m; x += kThreads) {
+            int lo_s = 0, hi_s = kParMaxBudget - 1;   // the slot s with soff[s] <= x < soff[s + 1]
+            while (lo_s < hi_s) {
+                const int mid = (lo_s + hi_s + 1) >> 1;
+                if (soff[mid] <= x)
+                    lo_s = mid;
+                else
+                    hi_s = mid - 1;
+            }
+            const int r = x - soff[lo_s];
+            const int parent = P.pool[lo_s];
+            unsigned long long h = P.phi[parent], l = P.plo[parent];
+            par_path(h, l, d, r);
+            par_store(P, nb + x, scratch[lo_s * kScratchStride + r], h, l, parent, d, r, P.acnt[parent] + 1 + r);
+        }
+        __syncthreads();
+        const int total = np + m;
+        for (int x = tid; x < total; x += kThreads) {
+            int id, rank;
+            if (x < np) {
+                id = P.pool[x];
+                rank = x;
+                for (int j = nb; j < ne; ++j) rank += par_node_before(P, j, id) ? 1 : 0;
+            } else {
+                id = nb + (x - np);
+                int lo_i = 0, hi_i = np;   // pool entries before it (the pool is sorted)
+                while (lo_i < hi_i) {
+                    const int mid = (lo_i + hi_i) >> 1;
+                    if (par_node_before(P, P.pool[mid], id))
+                        lo_i = mid + 1;
+                    else
+                        hi_i = mid;
+                }
+                rank = lo_i;
+                for (int j = nb; j < ne; ++j) rank += (j != id && par_node_before(P, j, id)) ? 1 : 0;
+            }
+            if (rank < budget) P.pool2[rank] = id;
+        }
+        __syncthreads();
+        np = total < budget ? total : budget;
+        for (int x = tid; x < np; x += kThreads) P.pool[x] = P.pool2[x];
+        nb = ne;
+        __syncthreads();
+    }
+    // pop order = pool order; a parent's position comes first
+    for (int x = tid; x < nb; x += kThreads) P.pos[x] = -1;
+    __syncthreads();
+    for (int x = tid; x < np; x += kThreads) P.pos[P.pool[x]] = x;
+    __syncthreads();
+    for (int x = tid; x < np; x += kThreads) {
+        const int id = P.pool[x];
+        const int par = P.parent[id];
+        const int pidx = par < 0 ? 0 : P.pos[par] + 1;
+        if (par >= 0 && (P.pos[par] < 0 || P.pos[par] >= x)) atomicOr(&P.ctl[2], 4);
+        e.n_parent[x + 1] = pidx;
+        e.n_dr[x + 1] = P.dr[id];
+    }
+    if (tid == 0) {
+        e.n_parent[0] = -1;
+        e.n_dr[0] = 0;
+    }
+    __syncthreads();
+    return P.ctl[2] ? -1 : np;
+}
+
 // Runs on all threads of one CTA.  lp / ids: [rows, topk] in global memory.
 __device__ void expand_tree(const float* lp_g, const int64_t* ids_g, int rows, int topk, int budget,
                             const int64_t* root_token, int64_t start, const ddt_tree_outputs out, ExpandSmem e) {
@@ -580,7 +868,10 @@ __device__ void expand_tree(const float* lp_g, const int64_t* ids_g, int rows, i
     for (int i = tid; i < rows * topk; i += kThreads) e.lp[i] = __ldcg(lp_g + i);
     __syncthreads();
 
-    if (warp == 0) {
+    const int par_count = e.par ? expand_par(e, carve_par(e.par), rows, topk, budget) : -1;
+    if (par_count >= 0) {
+        if (tid == 0) e.scalars[1] = par_count;
+    } else if (warp == 0) {
         int count;
         // before pop t the frontier holds at most t + 1 <= budget entries, so
         // 32 * S >= budget slots suffice; the last pop's appended entry may

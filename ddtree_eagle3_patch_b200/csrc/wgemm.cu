@@ -28,6 +28,18 @@
 // does not depend on timing and no partial touches global memory.  CTAs are
 // ~92 KB of shared memory (a 4-stage ring), two per SM.  Every wait is
 // bounded; a wait that runs out sets the status word.
+//
+// Gate/up mode (ddt_wgemm_gate_up): the weight holds the MLP's gate and up
+// projections interleaved in blocks of 64 rows (gate rows 64b .. 64b+63,
+// then the same up rows), so a CTA's 128 rows pair each gate row with its
+// up row and the epilogue writes act(gate) * up: the [T, 2I] intermediate is
+// never stored and no separate elementwise kernel runs.
+//
+// Launched as a programmatic dependent (ddt_set_pdl), the kernel signals its
+// own dependents at once and its producer puts the first ring stages' weight
+// loads in flight before griddepcontrol.wait: the weights do not depend on
+// the preceding kernels, so their latency overlaps those kernels' tails.
+// Token rows, the residual and the output are touched only after the wait.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <mutex>
@@ -59,6 +71,7 @@ struct Cfg {
 
 struct Params {
     int T, N, nk_total, splits;
+    int gate_up;   // interleaved gate/up weight: write act(gate) * up, N / 2 columns
     const __nv_bfloat16* residual;
     int64_t r_stride;
     __nv_bfloat16* y;
@@ -102,6 +115,10 @@ wgemm_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUt
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    // TMEM is held before dependents are released: a later kernel's CTA on
+    // this SM can then only wait for this one's columns, never hold them
+    griddep_launch_dependents();
+    if (warp != 0) griddep_wait();   // the producer waits after its weight prefetch
     const uint32_t tmem = *tmem_slot;
     const uint32_t s_addr = smem_u32(smem);
 
@@ -110,15 +127,28 @@ wgemm_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUt
         const bool leader = elect_one_sync();
         const uint64_t pol_w = policy_evict_first();   // weights are read once
         const uint64_t pol_x = policy_evict_last();    // token rows are read by every CTA
-        int issued = 0;
-        for (int i = 0; i < nk; ++i) {
+        // the first stages' weight tiles go out before the wait on the
+        // preceding grid; their token tiles follow it
+        const int pre = nk < kStages ? nk : kStages;
+        if (leader) {
+            for (int i = 0; i < pre; ++i) {
+                mbar_arrive_expect_tx(&full[i], C::kStage);
+                tma_load_2d_hint(smem + i * C::kStage, &tw, (kb + i) * BK, n0, &full[i], pol_w);
+            }
+        }
+        griddep_wait();
+        if (leader) {
+            for (int i = 0; i < pre; ++i)
+                tma_load_2d_hint(smem + i * C::kStage + kWTile, &tx, (kb + i) * BK, 0, &full[i], pol_x);
+        }
+        __syncwarp();
+        int issued = pre;
+        for (int i = pre; i < nk; ++i) {
             const int s = i % kStages;
-            if (i >= kStages) {
-                const bool ok = mbar_wait(&empty[s], (uint32_t)((i / kStages - 1) & 1));
-                if (!__all_sync(DDT_FULL_MASK, ok)) {
-                    if (leader) flag_error(p.status, 1);
-                    break;
-                }
+            const bool ok = mbar_wait(&empty[s], (uint32_t)((i / kStages - 1) & 1));
+            if (!__all_sync(DDT_FULL_MASK, ok)) {
+                if (leader) flag_error(p.status, 1);
+                break;
             }
             if (leader) {
                 unsigned char* st = smem + s * C::kStage;
@@ -189,7 +219,25 @@ wgemm_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUt
             for (int c = 0; c < 32; ++c) acc[32 + c] = __uint_as_float(r[c]);
         }
     }
-    if (p.splits == 1) {
+    if (p.splits == 1 && p.gate_up) {
+        // the up rows (lanes 64..127) hand their accumulators to the gate
+        // rows through the idle ring
+        float* up = reinterpret_cast<float*>(smem);   // [TP][64]
+        if (row >= 64) {
+#pragma unroll
+            for (int t = 0; t < TP; ++t) up[t * 64 + row - 64] = acc[t];
+        }
+        __syncthreads();
+        if (row < 64) {
+            const int col = nb * 64 + row;
+#pragma unroll
+            for (int t = 0; t < TP; ++t) {
+                if (t < p.T)
+                    p.y[(int64_t)t * p.y_stride + col] =
+                        silu_times(__float2bfloat16_rn(acc[t]), __float2bfloat16_rn(up[t * 64 + row]));
+            }
+        }
+    } else if (p.splits == 1) {
 #pragma unroll
         for (int t = 0; t < TP; ++t) {
             if (t < p.T) {
@@ -211,6 +259,7 @@ wgemm_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUt
         for (int t = 0; t < TP; ++t) stage[t * BN + row] = acc[t];
         cluster_sync();
         const int r = (int)cluster_ctarank();
+        float* pair = stage + TP * BN;   // gate/up mode: the reduced [TP][128] sums
         for (int t = r; t < p.T; t += p.splits) {
             float part[kMaxSplits];
 #pragma unroll
@@ -219,8 +268,21 @@ wgemm_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUt
             float v = 0.f;
 #pragma unroll
             for (int q = 0; q < kMaxSplits; ++q) v += part[q];
+            if (p.gate_up) {
+                pair[t * BN + row] = v;
+                continue;
+            }
             if (p.residual) v += __bfloat162float(p.residual[(int64_t)t * p.r_stride + n]);
             p.y[(int64_t)t * p.y_stride + n] = __float2bfloat16_rn(v);
+        }
+        if (p.gate_up) {
+            __syncthreads();
+            if (row < 64) {
+                const int col = nb * 64 + row;
+                for (int t = r; t < p.T; t += p.splits)
+                    p.y[(int64_t)t * p.y_stride + col] = silu_times(__float2bfloat16_rn(pair[t * BN + row]),
+                                                                    __float2bfloat16_rn(pair[t * BN + 64 + row]));
+            }
         }
         cluster_sync();
     }
@@ -287,13 +349,18 @@ static int launch(const CUtensorMap& tw, const CUtensorMap& tx, const Params& p,
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = C::kSmem;
     cfg.stream = st;
-    cudaLaunchAttribute attr_c[1];
-    attr_c[0].id = cudaLaunchAttributeClusterDimension;   // the splits of a row block share a cluster
-    attr_c[0].val.clusterDim.x = 1;
-    attr_c[0].val.clusterDim.y = (unsigned)p.splits;
-    attr_c[0].val.clusterDim.z = 1;
+    cudaLaunchAttribute attr_c[2];
+    unsigned na = 0;
+    if (p.splits > 1) {
+        attr_c[na].id = cudaLaunchAttributeClusterDimension;   // the splits of a row block share a cluster
+        attr_c[na].val.clusterDim.x = 1;
+        attr_c[na].val.clusterDim.y = (unsigned)p.splits;
+        attr_c[na].val.clusterDim.z = 1;
+        ++na;
+    }
+    na += pdl_attr(&attr_c[na]);
     cfg.attrs = attr_c;
-    cfg.numAttrs = p.splits > 1 ? 1 : 0;
+    cfg.numAttrs = na;
     const cudaError_t e = cudaLaunchKernelEx(&cfg, wgemm_kernel<TP>, tw, tx, p);
     if (e != cudaSuccess) return set_error(DDT_ECUDA, "wgemm_kernel: %s", cudaGetErrorString(e));
     return check_launch("wgemm_kernel");
@@ -305,17 +372,15 @@ static int launch(const CUtensorMap& tw, const CUtensorMap& tx, const Params& p,
 using namespace ddt;
 
 extern "C" size_t ddt_wgemm_workspace_size(int64_t T, int64_t N, int64_t K) {
-    if (T <= 0 || N < wgemm::BN || K < wgemm::BK) return 256;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    const int splits = wgemm::choose_splits(N, K, ddt_sm_count(dev));
-    (void)splits;
-    return 256;                                                           // the status word
+    (void)T;
+    (void)N;
+    (void)K;
+    return 256;   // the status word
 }
 
-extern "C" int ddt_wgemm(const void* x, int64_t x_stride, int64_t T, const void* w, int64_t w_stride, int64_t N,
-                         int64_t K, const void* residual, int64_t r_stride, void* y, int64_t y_stride,
-                         int64_t splits_hint, void* workspace, size_t workspace_bytes, ddt_stream_t stream) {
+static int wgemm_run(const void* x, int64_t x_stride, int64_t T, const void* w, int64_t w_stride, int64_t N,
+                     int64_t K, const void* residual, int64_t r_stride, void* y, int64_t y_stride, int gate_up,
+                     int64_t splits_hint, void* workspace, size_t workspace_bytes, ddt_stream_t stream) {
     using namespace ddt::wgemm;
     if (!x || !w || !y) return set_error(DDT_EINVAL, "null argument");
     if (T <= 0 || T > 64) return set_error(DDT_EUNSUPPORTED, "T=%lld outside [1, 64]", (long long)T);
@@ -323,7 +388,8 @@ extern "C" int ddt_wgemm(const void* x, int64_t x_stride, int64_t T, const void*
         return set_error(DDT_EUNSUPPORTED, "N=%lld must be a multiple of 128 and K=%lld of 64", (long long)N,
                          (long long)K);
     if (N / BN > 65535) return set_error(DDT_EUNSUPPORTED, "N too large");
-    if (x_stride < K || w_stride < K || y_stride < N || (residual && r_stride < N))
+    const int64_t out_cols = gate_up ? N / 2 : N;
+    if (x_stride < K || w_stride < K || y_stride < out_cols || (residual && r_stride < N))
         return set_error(DDT_EINVAL, "strides smaller than the rows");
     auto mis = [](const void* ptr, int b) { return reinterpret_cast<uintptr_t>(ptr) % b != 0; };
     if (mis(x, 16) || mis(w, 16) || (x_stride * 2) % 16 || (w_stride * 2) % 16)
@@ -349,6 +415,7 @@ extern "C" int ddt_wgemm(const void* x, int64_t x_stride, int64_t T, const void*
     p.N = (int)N;
     p.nk_total = (int)(K / BK);
     p.splits = splits;
+    p.gate_up = gate_up;
     p.residual = static_cast<const __nv_bfloat16*>(residual);
     p.r_stride = r_stride;
     p.y = static_cast<__nv_bfloat16*>(y);
@@ -362,4 +429,18 @@ extern "C" int ddt_wgemm(const void* x, int64_t x_stride, int64_t T, const void*
         case 48: return launch<48>(tw, tx, p, nblocks, st);
         default: return launch<64>(tw, tx, p, nblocks, st);
     }
+}
+
+extern "C" int ddt_wgemm(const void* x, int64_t x_stride, int64_t T, const void* w, int64_t w_stride, int64_t N,
+                         int64_t K, const void* residual, int64_t r_stride, void* y, int64_t y_stride,
+                         int64_t splits_hint, void* workspace, size_t workspace_bytes, ddt_stream_t stream) {
+    return wgemm_run(x, x_stride, T, w, w_stride, N, K, residual, r_stride, y, y_stride, 0, splits_hint, workspace,
+                     workspace_bytes, stream);
+}
+
+extern "C" int ddt_wgemm_gate_up(const void* x, int64_t x_stride, int64_t T, const void* w_gate_up,
+                                 int64_t w_stride, int64_t N2, int64_t K, void* y, int64_t y_stride,
+                                 int64_t splits_hint, void* workspace, size_t workspace_bytes, ddt_stream_t stream) {
+    return wgemm_run(x, x_stride, T, w_gate_up, w_stride, N2, K, nullptr, 0, y, y_stride, 1, splits_hint, workspace,
+                     workspace_bytes, stream);
 }

@@ -402,7 +402,8 @@ def ddtree_generate(model, target, input_ids: torch.Tensor, mask_token_id: int, 
     from .fused_layers import fused_decoder_layers
     from .runtime import tree_attention_for
     fuse = os.environ.get("DDTREE_FUSED", "1") != "0"
-    with tree_attention_for(target), (fused_decoder_layers(target) if fuse else nullcontext()):
+    with tree_attention_for(target), (fused_decoder_layers(target) if fuse else nullcontext()), \
+            kernels.pdl(fuse and os.environ.get("DDTREE_PDL", "1") != "0"):
         budget = block_size - 1 if tree_budget is None else max(int(tree_budget), 0)
         needed = input_ids.shape[1] + max_new_tokens + (1 + budget) + 1
         dec = _decoder_session(model, target, block_size, tree_budget, needed)
@@ -424,8 +425,9 @@ def _decoder_session(model, target, block_size, tree_budget, needed_rows: int):
     capture; ``release_decode_sessions(target)`` frees it."""
     import os
     eager = os.environ.get("DDTREE_EAGER", "0") == "1"
-    fused = (os.environ.get("DDTREE_FUSED", "1"), os.environ.get("DDTREE_PACK", "1"))
-    key = (id(model), block_size, tree_budget, eager, fused)
+    # every DDTREE_* switch (fused layers, packing, GEMM choice, PDL) shapes the captured graphs
+    switches = tuple(sorted((k, v) for k, v in os.environ.items() if k.startswith("DDTREE_")))
+    key = (id(model), block_size, tree_budget, eager, switches)
     fp = _weights_fingerprint(model, target)
     held = target.__dict__.get("_ddtree_session")
     if held is not None:

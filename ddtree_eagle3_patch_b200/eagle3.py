@@ -134,7 +134,8 @@ def eagle3_generate(model, target, input_ids: torch.Tensor, max_new_tokens: int,
     graph = None
     graph_kernels = replays = 0
 
-    with tree_attention_for(target), (fused_decoder_layers(target) if fuse else nullcontext()):
+    with tree_attention_for(target), (fused_decoder_layers(target) if fuse else nullcontext()), \
+            kernels.pdl(fuse and os.environ.get("DDTREE_PDL", "1") != "0"):
         ev_prefill = clock.mark()
         output = target(input_ids, position_ids=position_ids[:, :P], past_key_values=cache, use_cache=True,
                         logits_to_keep=1, output_hidden_states=True)

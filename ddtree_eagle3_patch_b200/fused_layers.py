@@ -59,10 +59,12 @@ def supported_layer(layer) -> bool:
 
 
 def packed_weights(layer):
-    """``([Wq; Wk; Wv], [Wgate; Wup])`` of a layer: one GEMM for the three
-    projections and one for the two MLP inputs instead of five, each
+    """``([Wq; Wk; Wv], Wgate/Wup interleaved)`` of a layer: one GEMM for the
+    three projections and one for the two MLP inputs instead of five, each
     streaming the same bytes (at a few dozen rows every GEMM is bound by its
     weight bytes plus a fixed latency, so fewer, larger ones are faster).
+    The MLP pair is interleaved in blocks of 64 rows
+    (``kernels.interleave_gate_up``) so one GEMM also applies act(gate) * up.
     Built once and kept on the layer (outside its state dict) while the
     source weights are unchanged; it costs a second copy of those weights
     (4.7 GB for Qwen3-4B).  ``None`` when DDTREE_PACK=0."""
@@ -70,26 +72,62 @@ def packed_weights(layer):
         return None
     attn, mlp = layer.self_attn, layer.mlp
     src = (attn.q_proj.weight, attn.k_proj.weight, attn.v_proj.weight, mlp.gate_proj.weight, mlp.up_proj.weight)
+    if src[3].shape[0] % 64:
+        return None
     key = tuple((w.data_ptr(), w._version, tuple(w.shape)) for w in src)
     cached = layer.__dict__.get("_ddtree_packed")
     if cached is None or cached[0] != key:
         with torch.no_grad():
             wqkv = torch.cat([w.detach() for w in src[:3]], 0)
-            wgu = torch.cat([w.detach() for w in src[3:]], 0)
+            wgu = kernels.interleave_gate_up(src[3].detach(), src[4].detach())
         cached = (key, wqkv, wgu)
         layer.__dict__["_ddtree_packed"] = cached
     return cached[1], cached[2]
 
 
-def residual_linear(a: torch.Tensor, w: torch.Tensor, residual: torch.Tensor) -> torch.Tensor:
+# Projections the weight-streaming GEMM serves by default.  The target's
+# packed q/k/v (6144 x 2560 at Qwen3-4B) stays on cuBLAS: in the captured
+# decode round it measured 286 tok/s there against 268 on this kernel.
+_WGEMM_DEFAULT = {"qkv": "0"}
+
+
+def _wgemm_on(kind: str) -> bool:
+    """The weight-streaming GEMM serves projection ``kind`` (``qkv``,
+    ``draft_qkv``, ``o``, ``gate_up``, ``down``, ``head``): DDTREE_WGEMM=0
+    turns it off everywhere, DDTREE_WGEMM_<KIND>=0/1 per projection."""
+    if os.environ.get("DDTREE_WGEMM", "1") == "0":
+        return False
+    return os.environ.get(f"DDTREE_WGEMM_{kind.upper()}", _WGEMM_DEFAULT.get(kind, "1")) != "0"
+
+
+def linear_rows(x: torch.Tensor, w: torch.Tensor, kind: str) -> torch.Tensor:
+    """x @ w.T for the few rows of a decode forward: the weight-streaming
+    tcgen05 GEMM where it takes the shapes, else cuBLAS."""
+    if _wgemm_on(kind) and kernels.wgemm_supported(x, w):
+        return kernels.wgemm(x, w)
+    return F.linear(x, w)
+
+
+def gate_up_act(h: torch.Tensor, w_packed: torch.Tensor) -> torch.Tensor:
+    """act(h Wg^T) * (h Wu^T) from the interleaved pair: one launch of the
+    weight-streaming GEMM with the SiLU product in its epilogue, else cuBLAS
+    and the elementwise kernel."""
+    if _wgemm_on("gate_up") and kernels.wgemm_supported(h, w_packed):
+        return kernels.wgemm_gate_up(h, w_packed)
+    T = h.shape[0]
+    gu = F.linear(h, w_packed).view(T, -1, 2, 64)
+    inter = w_packed.shape[0] // 2
+    return kernels.silu_mul(gu[:, :, 0].reshape(T, inter), gu[:, :, 1].reshape(T, inter))
+
+
+def residual_linear(a: torch.Tensor, w: torch.Tensor, residual: torch.Tensor, kind: str) -> torch.Tensor:
     """residual + a @ w.T, rounded once (``torch.addmm``).  bf16 decode
     shapes run on the weight-streaming tcgen05 GEMM with the residual added
     in its epilogue (the o_proj and down_proj of a layer: at 33 rows it
     streams 21 / 50 MB of weights in 9.4 / 14.1 us against cuBLAS's 10.2 /
-    16.7 us on B200); anything else on cuBLAS.  ``DDTREE_WGEMM=0`` keeps
-    cuBLAS."""
-    if os.environ.get("DDTREE_WGEMM", "1") != "0" and kernels.wgemm_supported(a, w) \
-            and residual.dtype == torch.bfloat16 and residual.stride(1) == 1:
+    16.7 us on B200); anything else on cuBLAS."""
+    if _wgemm_on(kind) and kernels.wgemm_supported(a, w) and residual.dtype == torch.bfloat16 \
+            and residual.stride(1) == 1:
         return kernels.wgemm(a, w, residual=residual)
     return torch.addmm(residual, a, w.t())
 
@@ -101,7 +139,7 @@ def head_logits(lm_head, h: torch.Tensor) -> torch.Tensor:
     B200); anything else calls the module.  ``DDTREE_WGEMM=0`` keeps the
     module."""
     w = getattr(lm_head, "weight", None)
-    if (os.environ.get("DDTREE_WGEMM", "1") != "0" and isinstance(lm_head, torch.nn.Linear)
+    if (_wgemm_on("head") and isinstance(lm_head, torch.nn.Linear)
             and lm_head.bias is None and h.dim() == 3 and h.shape[0] == 1):
         x = h[0]
         if kernels.wgemm_supported(x, w):
@@ -123,7 +161,7 @@ def _fused_forward(self, hidden_states, attention_mask=None, position_ids=None, 
     h = kernels.rms_norm(x, self.input_layernorm.weight, self.input_layernorm.variance_epsilon)
     packed = packed_weights(self)
     if packed is not None:
-        qkv = F.linear(h, packed[0])
+        qkv = linear_rows(h, packed[0], "qkv")
         q, k, v = qkv[:, : hq * 128], qkv[:, hq * 128: (hq + hkv) * 128], qkv[:, (hq + hkv) * 128:]
     else:
         q, k, v = F.linear(h, attn.q_proj.weight), F.linear(h, attn.k_proj.weight), F.linear(h, attn.v_proj.weight)
@@ -132,18 +170,17 @@ def _fused_forward(self, hidden_states, attention_mask=None, position_ids=None, 
     qr = kernels.qk_norm_rope_append(q, k, v, attn.q_norm.weight, attn.k_norm.weight, attn.q_norm.variance_epsilon,
                                      attn.k_norm.variance_epsilon, cos[0], sin[0], cache._k, cache._v,
                                      past_key_values.offset_dev, hq, hkv)
+    # the tree rows just appended start at the prefix: every key before them is stable
     o = kernels.tree_attention(qr, cache._k[0], cache._v[0], attention_mask.ddtree_past_max,
                                attention_mask.ddtree_bits, attn.scaling, past_dev=past_dev,
-                               workspace=attention_mask.ddtree_workspace)
-    x2 = residual_linear(o.view(T, -1), attn.o_proj.weight, x)
+                               workspace=attention_mask.ddtree_workspace, stable_dev=past_dev)
+    x2 = residual_linear(o.view(T, -1), attn.o_proj.weight, x, "o")
     h2 = kernels.rms_norm(x2, self.post_attention_layernorm.weight, self.post_attention_layernorm.variance_epsilon)
     if packed is not None:
-        gu = F.linear(h2, packed[1])
-        inter = gu.shape[1] // 2
-        a = kernels.silu_mul(gu[:, :inter], gu[:, inter:])
+        a = gate_up_act(h2, packed[1])
     else:
         a = kernels.silu_mul(F.linear(h2, mlp.gate_proj.weight), F.linear(h2, mlp.up_proj.weight))
-    return residual_linear(a, mlp.down_proj.weight, x2).unsqueeze(0)
+    return residual_linear(a, mlp.down_proj.weight, x2, "down").unsqueeze(0)
 
 
 def _decoder_layers(model):

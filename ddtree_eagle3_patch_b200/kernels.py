@@ -4,6 +4,7 @@ from __future__ import annotations
 
 import ctypes
 import math
+from contextlib import contextmanager
 from dataclasses import dataclass
 
 import torch
@@ -92,14 +93,18 @@ def tree_build(draft_logits: torch.Tensor, budget: int, root_token: torch.Tensor
 
 
 def tree_from_log_probs(lp: torch.Tensor, ids: torch.Tensor, budget: int, root_token: torch.Tensor | None = None,
-                        start: int = 0) -> DeviceTree:
-    """Best-first expansion alone from given [rows, topk] log-probs and ids."""
+                        start: int = 0, out: DeviceTree | None = None) -> DeviceTree:
+    """Best-first expansion alone from given [rows, topk] log-probs and ids
+    (into ``out``, a DeviceTree of the same rows / topk / budget, when given)."""
     require_cuda(lp, "lp")
     require_cuda(ids, "ids")
     lp = lp.to(torch.float32).contiguous()
     ids = ids.to(torch.int64).contiguous()
     rows, topk = lp.shape
-    out = DeviceTree.allocate(rows, topk, budget, lp.device)
+    if out is None:
+        out = DeviceTree.allocate(rows, topk, budget, lp.device)
+    elif out.budget != int(budget) or out.rows != rows or out.visibility.shape[1] < vis_words_for(int(budget) + 1):
+        raise ValueError("out was allocated for another tree shape")
     o = out.c_outputs()
     rc = _lib.load().ddt_tree_from_log_probs(ptr(lp), ptr(ids), rows, topk, int(budget), ptr(root_token), int(start),
                                              ctypes.byref(o), stream_of(lp.device))
@@ -140,7 +145,8 @@ _ATT_WS: dict = {}
 
 def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, past_length: int, visibility: torch.Tensor,
                    scale: float, out: torch.Tensor | None = None, key_lo: torch.Tensor | None = None,
-                   past_dev: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
+                   past_dev: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
+                   stable_dev: torch.Tensor | None = None) -> torch.Tensor:
     """Kernel (2): one layer of tree-masked attention.
 
     q [n_tokens, hq, 128], k / v [hkv, kv_rows, 128] (bf16, last dim
@@ -156,6 +162,9 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, past_lengt
     bound, and one captured launch serves any prefix up to it.  ``workspace``
     (uint8, 256-aligned) is the caller's own scratch, needed when the launch
     is captured into a graph that must outlive the shared scratch.
+    ``stable_dev`` (int32 device scalar, with ``past_dev``): keys below it are
+    written by nothing still running on the stream, so their K tiles may load
+    before the preceding kernel has finished.
 
     Called once per layer, so the host work is kept to one read of each
     tensor's shape and strides; the C entry point checks the rest."""
@@ -205,8 +214,10 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, past_lengt
         if key_lo is not None and (not key_lo.is_cuda or key_lo.dtype != torch.int64 or not key_lo.is_contiguous()
                                    or key_lo.numel() < n_tokens):
             raise ValueError("key_lo must be a contiguous int64 CUDA tensor with one entry per token")
-        check(lib.ddt_tree_attention_dev(ctypes.byref(a), ptr(key_lo), past_dev.data_ptr(), ws[1], ws[2],
-                                         _lib.raw_stream(dev_index)), "ddt_tree_attention_dev")
+        if stable_dev is not None and (not stable_dev.is_cuda or stable_dev.dtype != torch.int32):
+            raise ValueError("stable_dev must be an int32 CUDA tensor")
+        check(lib.ddt_tree_attention_dev(ctypes.byref(a), ptr(key_lo), past_dev.data_ptr(), ptr(stable_dev), ws[1],
+                                         ws[2], _lib.raw_stream(dev_index)), "ddt_tree_attention_dev")
         return out
     if key_lo is None:
         check(lib.ddt_tree_attention(ctypes.byref(a), ws[1], ws[2], _lib.raw_stream(dev_index)), "ddt_tree_attention")
@@ -394,6 +405,52 @@ def wgemm(x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor | None = None
                        ws.data_ptr(), ws.numel(), _lib.raw_stream(x.device.index))
     check(rc, "ddt_wgemm")
     return out
+
+
+def interleave_gate_up(w_gate: torch.Tensor, w_up: torch.Tensor) -> torch.Tensor:
+    """[Wg; Wu] packed for ``wgemm_gate_up``: blocks of 64 gate rows, each
+    followed by the same 64 up rows (I a multiple of 64)."""
+    inter, k = w_gate.shape
+    if w_up.shape != w_gate.shape or inter % 64:
+        raise ValueError("gate and up weights must share a [I, K] shape with I a multiple of 64")
+    return torch.stack([w_gate.reshape(inter // 64, 64, k), w_up.reshape(inter // 64, 64, k)], 1).reshape(2 * inter, k)
+
+
+def wgemm_gate_up(x: torch.Tensor, w_packed: torch.Tensor, out: torch.Tensor | None = None,
+                  splits: int = 0) -> torch.Tensor:
+    """act(x Wg^T) * (x Wu^T) with SiLU in one launch (``ddt_wgemm_gate_up``):
+    x [T <= 64, K] bf16, w_packed from ``interleave_gate_up`` [2I, K]; each
+    product, the SiLU and the final product rounded to bf16 in the order of
+    ``act_fn(gate_proj(x)) * up_proj(x)``.  Returns [T, I]."""
+    if not wgemm_supported(x, w_packed):
+        raise ValueError("wgemm_gate_up: unsupported shapes / layout (see wgemm_supported)")
+    T, K = x.shape
+    N2 = w_packed.shape[0]
+    if out is None:
+        out = torch.empty((T, N2 // 2), dtype=torch.bfloat16, device=x.device)
+    if out.dtype != torch.bfloat16 or out.stride(1) != 1 or tuple(out.shape) != (T, N2 // 2):
+        raise ValueError("out must be [T, I] bf16 with contiguous rows")
+    ws = _wgemm_workspace(x.device)
+    rc = _lib.load().ddt_wgemm_gate_up(x.data_ptr(), x.stride(0), T, w_packed.data_ptr(), w_packed.stride(0), N2, K,
+                                       out.data_ptr(), out.stride(0), int(splits), ws.data_ptr(), ws.numel(),
+                                       _lib.raw_stream(x.device.index))
+    check(rc, "ddt_wgemm_gate_up")
+    return out
+
+
+@contextmanager
+def pdl(enabled: bool = True):
+    """Launch this library's decode-layer kernels as programmatic dependent
+    launches (``ddt_set_pdl``) inside the block: each may start while the
+    kernel before it is still running, and the weight-streaming GEMMs load
+    their first weight tiles before it completes.  Weights must not be
+    written by work queued in the block."""
+    lib = _lib.load()
+    prev = lib.ddt_set_pdl(1 if enabled else 0)
+    try:
+        yield
+    finally:
+        lib.ddt_set_pdl(prev)
 
 
 def wgemm_status(device: torch.device) -> int:

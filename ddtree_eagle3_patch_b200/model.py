@@ -166,8 +166,9 @@ class DFlashAttention(nn.Module):
         cache.update_at(k[:, :, :ctx_len], v[:, :, :ctx_len], self.layer_idx, rs[1:2], rs[2:3])
         kf, vf = cache.update_at(k[:, :, ctx_len:], v[:, :, ctx_len:], self.layer_idx, rs[0:1])
         bits = _all_visible_bits(q_len, q.device)
+        # keys before this round's context rows (at rs[1]) are stable
         out = kernels.tree_attention(q[0], kf[0], vf[0], past_max, bits, self.scaling, past_dev=rs[0:1],
-                                     workspace=workspace)
+                                     workspace=workspace, stable_dev=rs[1:2])
         return self.o_proj(out.reshape(1, q_len, self.num_heads * hd))
 
 
@@ -197,7 +198,7 @@ class DFlashDecoderLayer(nn.Module):
             h = hidden_states + self.self_attn.forward_static(self.input_layernorm(hidden_states), target_hidden,
                                                               position_embeddings, cache, rs, past_max, workspace)
             return h + self.mlp(self.post_attention_layernorm(h))
-        from .fused_layers import packed_weights, residual_linear
+        from .fused_layers import gate_up_act, linear_rows, packed_weights, residual_linear
         attn, mlp = self.self_attn, self.mlp
         x, c = hidden_states[0], target_hidden[0]
         T = x.shape[0]
@@ -205,9 +206,9 @@ class DFlashDecoderLayer(nn.Module):
         h = kernels.rms_norm(x, self.input_layernorm.weight, self.input_layernorm.variance_epsilon)
         packed = packed_weights(self)
         if packed is not None:
-            qkv = F.linear(h, packed[0])
+            qkv = linear_rows(h, packed[0], "draft_qkv")
             q, k_n, v_n = qkv[:, :nq], qkv[:, nq: nq + nk], qkv[:, nq + nk:]
-            kv = F.linear(c, packed[0][nq:])
+            kv = linear_rows(c, packed[0][nq:], "draft_qkv")
             k_c, v_c = kv[:, :nk], kv[:, nk:]
         else:
             q = F.linear(h, attn.q_proj.weight)
@@ -223,17 +224,17 @@ class DFlashDecoderLayer(nn.Module):
                                          layer_cache._k, layer_cache._v, rs, attn.num_heads, attn.num_kv_heads,
                                          ctx_k=k_c, ctx_v=v_c)
         bits = _all_visible_bits(T, x.device)
+        # the append above wrote the context rows at rs[1] and the block at
+        # rs[0]: keys before rs[1] are stable
         o = kernels.tree_attention(qr, layer_cache._k[0], layer_cache._v[0], past_max, bits, attn.scaling,
-                                   past_dev=rs[0:1], workspace=workspace)
-        x2 = residual_linear(o.view(T, -1), attn.o_proj.weight, x)
+                                   past_dev=rs[0:1], workspace=workspace, stable_dev=rs[1:2])
+        x2 = residual_linear(o.view(T, -1), attn.o_proj.weight, x, "o")
         h2 = kernels.rms_norm(x2, self.post_attention_layernorm.weight, self.post_attention_layernorm.variance_epsilon)
         if packed is not None:
-            gu = F.linear(h2, packed[1])
-            inter = gu.shape[1] // 2
-            a = kernels.silu_mul(gu[:, :inter], gu[:, inter:])
+            a = gate_up_act(h2, packed[1])
         else:
             a = kernels.silu_mul(F.linear(h2, mlp.gate_proj.weight), F.linear(h2, mlp.up_proj.weight))
-        return residual_linear(a, mlp.down_proj.weight, x2).unsqueeze(0)
+        return residual_linear(a, mlp.down_proj.weight, x2, "down").unsqueeze(0)
 
 
 class DFlashDraftModel(Qwen3PreTrainedModel):

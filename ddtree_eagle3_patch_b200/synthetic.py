@@ -114,6 +114,10 @@ TARGET_SHAPES = {
     # Qwen3-8B: 36 layers, hidden 4096, intermediate 12288, 32 q / 8 kv heads
     "qwen3-8b": dict(hidden_size=4096, intermediate_size=12288, num_hidden_layers=36, num_attention_heads=32,
                      num_key_value_heads=8, head_dim=128, vocab_size=V_QWEN3, tie_word_embeddings=False),
+    # a small model whose every projection takes the decode kernels' fast
+    # paths (multiples of 128 rows and 64 columns): for tests
+    "qwen3-small": dict(hidden_size=256, intermediate_size=512, num_hidden_layers=4, num_attention_heads=4,
+                        num_key_value_heads=2, head_dim=128, vocab_size=1024, tie_word_embeddings=False),
 }
 
 

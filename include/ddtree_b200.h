@@ -51,6 +51,18 @@ DDT_API int ddt_sm_count(int device);
 /* Kernels this library has launched since it was loaded (all devices and
  * threads; a launch recorded into a CUDA graph counts once, at capture). */
 DDT_API uint64_t ddt_launch_count(void);
+/* Launch the decode-layer kernels (ddt_rms_norm, ddt_qk_norm_rope_append,
+ * ddt_silu_mul*, ddt_kv_append, ddt_wgemm*) as programmatic dependent
+ * launches: each may start while the kernel before it in the stream is
+ * still running and waits (griddepcontrol.wait) before touching anything
+ * that kernel may write, so launch latency and prologues overlap.  (The
+ * split-key attention kernels are always launched that way; with this on,
+ * host-length attention calls load no key before that wait.)  While on,
+ * the WEIGHT operand of ddt_wgemm / ddt_wgemm_gate_up is read before the
+ * preceding kernels complete: it must not be written by work still queued
+ * on the stream.  Off at load.  Returns the previous setting.  Reference
+ * counterpart: none (the reference launches cuBLAS / SDPA through torch). */
+DDT_API int ddt_set_pdl(int enabled);
 
 /* ---------------------------------------------------------------------------
  * (1) Tree build.
@@ -181,9 +193,14 @@ DDT_API int ddt_tree_attention_window(const ddt_attention_args* args, const int6
  * nullable (sliding window as in ddt_tree_attention_window).  Workspace as
  * for ddt_tree_attention at past_length.  Shapes whose rows do not fit the
  * split-key kernel (more than 147 128-row tiles x KV heads) return
- * DDT_EUNSUPPORTED. */
+ * DDT_EUNSUPPORTED.  stable_dev (nullable device int32): keys [0, *stable_dev)
+ * are written by nothing still running on the stream, so their K tiles may
+ * load before the preceding kernel completes (the target verify: the whole
+ * prefix; the draft: the keys before this round's context rows).  Null: every
+ * key loads after it. */
 DDT_API int ddt_tree_attention_dev(const ddt_attention_args* args, const int64_t* key_lo, const int32_t* past_dev,
-                                   void* workspace, size_t workspace_bytes, ddt_stream_t stream);
+                                   const int32_t* stable_dev, void* workspace, size_t workspace_bytes,
+                                   ddt_stream_t stream);
 
 /* The same attention call for float32 targets (the reference's SDPA in the
  * target's dtype, ddtree.py:523-531): q, k, v and out are float32 with the
@@ -340,6 +357,16 @@ DDT_API size_t ddt_wgemm_workspace_size(int64_t T, int64_t N, int64_t K);
 DDT_API int ddt_wgemm(const void* x, int64_t x_stride, int64_t T, const void* w, int64_t w_stride, int64_t N,
                       int64_t K, const void* residual /* nullable */, int64_t r_stride, void* y, int64_t y_stride,
                       int64_t splits, void* workspace, size_t workspace_bytes, ddt_stream_t stream);
+/* The MLP's first half, act(x Wg^T) * (x Wu^T) with SiLU, in one launch.
+ * w_gate_up: [N2, K] bf16 with the gate and up rows interleaved in blocks
+ * of 64 (rows 128b .. 128b+63 = gate rows 64b .., rows 128b+64 .. = the same
+ * up rows); N2 a multiple of 128.  y: [T, N2 / 2].  Each product is rounded
+ * to bf16, the SiLU is rounded, then the product (the order of
+ * act_fn(gate_proj(x)) * up_proj(x) in bf16, model/dflash.py and the HF
+ * Qwen3 MLP).  Same limits and workspace as ddt_wgemm. */
+DDT_API int ddt_wgemm_gate_up(const void* x, int64_t x_stride, int64_t T, const void* w_gate_up, int64_t w_stride,
+                              int64_t N2, int64_t K, void* y, int64_t y_stride, int64_t splits, void* workspace,
+                              size_t workspace_bytes, ddt_stream_t stream);
 
 /* ---------------------------------------------------------------------------
  * EAGLE3 path acceptance.  Replaces evaluate_eagle3_posterior

@@ -187,3 +187,44 @@ def test_ddtree_generate_is_lossless_in_bf16():
     out = hot.output_ids[0, plen:]
     assert out.numel() > 0 and int(out.max()) < vocab and int(out.min()) >= 0
     assert sum(hot.acceptance_lengths) >= 16
+
+
+@pytest.mark.gpu
+def test_bf16_decode_identical_across_launch_forms(monkeypatch):
+    """A bf16 model whose projections all take the weight-streaming GEMM
+    (fused gate/up included): the captured forwards with programmatic
+    dependent launches, without them, and every round eager run the same
+    kernels on the same data and so emit identical ids and acceptances;
+    the cuBLAS projections (DDTREE_WGEMM=0) sum in another order and are
+    held to a near-tie at their first divergence."""
+    from ddtree_eagle3_patch_b200.ddtree import ddtree_generate
+    from ddtree_eagle3_patch_b200.synthetic import build_decode_models, random_prompt
+    tgt, drf = build_decode_models("qwen3-small", DEV, torch.bfloat16, seed=4, draft_layers=2, block_size=8)
+    ids = random_prompt(40, vocab=1024, seed=2, exclude=drf.mask_token_id).to(DEV)
+
+    def run(**env):
+        for k in ("DDTREE_PDL", "DDTREE_EAGER", "DDTREE_WGEMM"):
+            monkeypatch.delenv(k, raising=False)
+        for k, v in env.items():
+            monkeypatch.setenv(k, v)
+        return ddtree_generate(drf, tgt, ids, mask_token_id=drf.mask_token_id, max_new_tokens=48, block_size=8,
+                               stop_token_ids=None, temperature=0.0, tree_budget=16)
+
+    base = run()
+    assert base.graph_rounds > 0
+    for env in ({"DDTREE_PDL": "0"}, {"DDTREE_EAGER": "1"}):
+        other = run(**env)
+        assert other.output_ids.tolist() == base.output_ids.tolist(), env
+        assert other.acceptance_lengths == base.acceptance_lengths, env
+    from ddtree_eagle3_patch_b200 import kernels
+    assert kernels.wgemm_status(DEV) == 0
+    cub = run(DDTREE_WGEMM="0")
+    a, b = base.output_ids[0], cub.output_ids[0]
+    n = min(a.numel(), b.numel())
+    diff = (a[:n] != b[:n]).nonzero()
+    if diff.numel():
+        i = int(diff[0])
+        with torch.inference_mode():
+            row = tgt(a[:i].unsqueeze(0)).logits[0, -1].float()
+        gap = abs(float(row[int(a[i])] - row[int(b[i])]))
+        assert gap <= 0.05 * float(row.abs().max()), (i, gap)

@@ -258,3 +258,53 @@ def test_candidate_overflow_rows_match_oracle():
     assert np.all(np.abs(lp_g - o_lp) <= tol), np.abs(lp_g - o_lp).max()
     o = O.tree_from_lp(lp_g, ids_g, budget)
     _assert_tree_equal(g, o["node_token_ids"], o["node_depths"], o["parents"], o["visibility"], "overflow")
+
+
+def _random_table(rng, kind, L, V):
+    if kind == 0:      # continuous values
+        return rng.standard_normal((L, V)).astype(np.float32)
+    if kind == 1:      # values on a coarse grid: many exact ties
+        return (np.round(rng.standard_normal((L, V)) * 8) / 8).astype(np.float32)
+    if kind == 2:      # one confident token per row
+        x = rng.standard_normal((L, V)).astype(np.float32)
+        x[np.arange(L), rng.integers(0, V, L)] += rng.uniform(2, 20)
+        return x
+    return rng.integers(0, 3, (L, V)).astype(np.float32)   # three values only
+
+
+@pytest.mark.parametrize("kind", [0, 1, 2, 3])
+def test_expansion_random_tables_match_oracle(kind):
+    """The expansion (parallel for budget <= 64 and <= 16 rows, else the
+    serial loop, which also takes over when a check fails) on random
+    log-prob tables: continuous, tied on a coarse grid, peaked, and
+    three-valued, at random depths, budgets and widths."""
+    K = _kernels()
+    rng = np.random.default_rng(100 + kind)
+    for trial in range(50):
+        L = int(rng.integers(1, 17))
+        B = int(rng.integers(1, 80))
+        V = int(rng.integers(2, 3000))
+        k = min(B, V)
+        ids, vals, logz = O.topk_logz(_random_table(rng, kind, L, V), k)
+        lp = O.log_probs(vals, logz)
+        ref = O.tree_from_lp(lp, ids, B)
+        tree = K.tree_from_log_probs(torch.from_numpy(lp).cuda(), torch.from_numpy(ids).cuda(), B)
+        got = _tree_np(tree)
+        _assert_tree_equal(got, ref["node_token_ids"], ref["node_depths"], ref["parents"], ref["visibility"],
+                           msg=(kind, trial, L, B, V))
+
+
+def test_full_build_bf16_ties_match_oracle():
+    """bf16 draft logits at the vocabulary width (many exact value ties in
+    every row's top-k) through the whole kernel, budgets 8 / 32 / 64."""
+    K = _kernels()
+    g = torch.Generator().manual_seed(7)
+    for budget in (8, 32, 64):
+        for peak in (0.0, 6.0, 16.0):
+            x = torch.randn(15, 151936, generator=g)
+            x[torch.arange(15), torch.randint(0, 151936, (15,), generator=g)] += peak
+            x = x.to(torch.bfloat16)
+            ref = O.build_tree(x.float().numpy(), budget)
+            got = _tree_np(K.tree_build(x.cuda(), budget))
+            _assert_tree_equal(got, ref["node_token_ids"], ref["node_depths"], ref["parents"], ref["visibility"],
+                               msg=(budget, peak))
