@@ -189,7 +189,7 @@ __device__ unsigned long long block_kth_largest(const unsigned long long* keys, 
 
 // Same, over keys produced by key_at(j), j < kValsPerThread, per thread (0 = empty).
 template <typename KeyAt>
-__device__ unsigned long long block_kth_largest_regs(KeyAt key_at, int K, SelectScratch* s) {
+__device__ __forceinline__ unsigned long long block_kth_largest_regs(KeyAt key_at, int K, SelectScratch* s) {
     if (threadIdx.x == 0) {
         s->prefix = 0ull;
         s->need = K;
@@ -963,69 +963,58 @@ tree_build_kernel(const T* __restrict__ logits, int rows, int64_t vocab, int64_t
     const int64_t c0 = (int64_t)c * chunk_len;
     const int64_t c1 = min(c0 + chunk_len, vocab);
 
-    // ---- load the chunk into shared memory ----------------------------
+    // ---- load the chunk into registers -----------------------------------
     // Thread tid holds the 16-byte vectors tid, tid + kThreads, ... of the
-    // chunk; its values stay in shared memory (chunk-local index) rather
-    // than registers, and each thread only ever reads back its own.
+    // chunk: value j of the thread has chunk-local index loc_of(j), and every
+    // loop below runs over j in that (index) order, fully unrolled so the
+    // values never leave registers.  Slots past the chunk hold -inf.
     constexpr int kEpv = 16 / sizeof(T);  // elements per 16-byte vector
-    unsigned long long* maxkeys = reinterpret_cast<unsigned long long*>(smem);
-    unsigned long long* cand = maxkeys + kThreads;
+    unsigned long long* cand = reinterpret_cast<unsigned long long*>(smem);
     unsigned long long* top = cand + kCandCap;
-    float* cv = reinterpret_cast<float*>(top + kMaxBudget);
     const int n_valid = (int)(c1 - c0);
+    float v[kValsPerThread];
 #pragma unroll
     for (int j = 0; j < kValsPerThread / kEpv; ++j) {
         const int loc = (j * kThreads + tid) * kEpv;
-        float v[kEpv];
         if (kVec && loc + kEpv <= n_valid) {
             const uint4 raw = __ldcs(reinterpret_cast<const uint4*>(rowp + c0 + loc));
             const T* pv = reinterpret_cast<const T*>(&raw);
 #pragma unroll
-            for (int e = 0; e < kEpv; ++e) v[e] = to_f32<T>(pv[e]);
+            for (int e = 0; e < kEpv; ++e) v[j * kEpv + e] = to_f32<T>(pv[e]);
         } else {
 #pragma unroll
-            for (int e = 0; e < kEpv; ++e) v[e] = loc + e < n_valid ? to_f32<T>(rowp[c0 + loc + e]) : -INFINITY;
+            for (int e = 0; e < kEpv; ++e)
+                v[j * kEpv + e] = loc + e < n_valid ? to_f32<T>(rowp[c0 + loc + e]) : -INFINITY;
         }
-#pragma unroll
-        for (int e = 0; e < kEpv; e += 4)
-            *reinterpret_cast<float4*>(cv + loc + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
     }
     auto loc_of = [&](int j) -> int { return ((j / kEpv) * kThreads + tid) * kEpv + (j % kEpv); };
-    // visits this thread's values in index order with 16-byte shared loads
-    // (a warp reads 512 consecutive bytes: no bank conflicts)
-    auto for_vals = [&](auto&& f) {
-#pragma unroll 2
-        for (int jv = 0; jv < kValsPerThread / kEpv; ++jv) {
-            const int loc = (jv * kThreads + tid) * kEpv;
-#pragma unroll
-            for (int h = 0; h < kEpv; h += 4) {
-                const float4 q = *reinterpret_cast<const float4*>(cv + loc + h);
-                f(q.x, loc + h);
-                f(q.y, loc + h + 1);
-                f(q.z, loc + h + 2);
-                f(q.w, loc + h + 3);
-            }
-        }
-    };
 
     // ---- max and sum of exp (logsumexp pieces, ddtree.py:138) ----------
-    float m = -INFINITY;
+    // (a slot past the chunk adds exp(-inf) = +0 to the sum: no change)
+    // The same pass keeps the thread's largest value and its first slot
+    // (slots run in index order, so the lowest index among equal values).
+    float m = -INFINITY, best = -INFINITY;
+    int bj = -1;
     bool nan_seen = false;
-    for_vals([&](float v, int loc) {
-        if (loc < n_valid) {
-            nan_seen |= (v != v);
-            m = fmaxf(m, v);
+#pragma unroll
+    for (int j = 0; j < kValsPerThread; ++j) {
+        nan_seen |= (v[j] != v[j]);
+        m = fmaxf(m, v[j]);
+        if (v[j] > best) {
+            best = v[j];
+            bj = j;
         }
-    });
+    }
     if (tid == 0) s_flag = 0;
     __syncthreads();
     if (nan_seen) s_flag = 1;
     m = block_max(m, red_f);
+    const bool any_nan = s_flag != 0;   // (set before block_max's barriers)
     float sum_t = 0.f;
-    if (m != -INFINITY && m == m)
-        for_vals([&](float v, int loc) {
-            if (loc < n_valid) sum_t += expf(v - m);
-        });
+    if (m != -INFINITY && m == m) {
+#pragma unroll
+        for (int j = 0; j < kValsPerThread; ++j) sum_t += expf(v[j] - m);
+    }
     const double sum_c = block_sum_d((double)sum_t, red_d);
 
     // ---- chunk top-k candidates ----------------------------------------
@@ -1038,17 +1027,21 @@ tree_build_kernel(const T* __restrict__ logits, int rows, int64_t vocab, int64_t
                                 (unsigned long long)(0xffffffffu - (uint32_t)(c0 + loc)))
                              : 0ull;
     };
-    auto key_at = [&](int j) -> unsigned long long {
-        const int loc = loc_of(j);
-        return key_of(cv[loc], loc);
-    };
+    auto key_at = [&](int j) -> unsigned long long { return key_of(v[j], loc_of(j)); };   // j: unrolled index
+    // The thread's largest key.  Without NaN it is that of its first largest
+    // value (up to the order of +0 and -0, which only lowers it: the bound
+    // below stays a lower bound, built from keys the thread holds).
     unsigned long long tmax = 0ull;
-    for_vals([&](float v, int loc) {
-        const unsigned long long k = key_of(v, loc);
-        tmax = k > tmax ? k : tmax;
-    });
+    if (!any_nan) {
+        if (bj >= 0) tmax = key_of(best, loc_of(bj));
+    } else {
+#pragma unroll
+        for (int j = 0; j < kValsPerThread; ++j) {
+            const unsigned long long k = key_at(j);
+            tmax = k > tmax ? k : tmax;
+        }
+    }
     unsigned long long* dst = part_keys + ((int64_t)d * chunks + c) * topk;
-    maxkeys[tid] = tmax;
     if (tid == 0) sel.count = 0;
     __syncthreads();
     // A lower bound t0 on the kc-th largest key: each warp sorts its 32
@@ -1075,21 +1068,47 @@ tree_build_kernel(const T* __restrict__ logits, int rows, int64_t vocab, int64_t
 #pragma unroll
         for (int w = 1; w < kWarps; ++w) t0 = s_offer[w] < t0 ? s_offer[w] : t0;
     }
-    // gather keys >= t0 (warp-aggregated slots)
-    for_vals([&](float v, int loc) {
-        const unsigned long long kj = key_of(v, loc);
-        const bool take = kj != 0ull && kj >= t0;
-        const uint32_t b = __ballot_sync(DDT_FULL_MASK, take);
-        if (b) {
-            int base = 0;
-            if (lane == __ffs(b) - 1) base = atomicAdd(&sel.count, __popc(b));
-            base = __shfl_sync(DDT_FULL_MASK, base, __ffs(b) - 1);
-            if (take) {
-                const int pos = base + __popc(b & ((1u << lane) - 1u));
-                if (pos < kCandCap) cand[pos] = kj;
+    // gather keys >= t0: each thread counts its own, a warp scan places them,
+    // one atomic per warp reserves the warp's slots.  Without NaN and with a
+    // bound, the test is on the float value (greater: taken; equal: the key
+    // decides, which also orders +0 / -0); else on the key.
+    const bool by_value = !any_nan && t0 != 0ull;
+    const float t0v = key_value(t0);
+    auto take = [&](int j) -> bool {
+        if (by_value) return v[j] > t0v || (v[j] == t0v && key_at(j) >= t0);
+        const unsigned long long kj = key_at(j);
+        return kj != 0ull && kj >= t0;
+    };
+    int cnt = 0;
+    if (by_value) {
+#pragma unroll
+        for (int j = 0; j < kValsPerThread; ++j) cnt += (v[j] > t0v || (v[j] == t0v && key_at(j) >= t0)) ? 1 : 0;
+    } else {
+#pragma unroll
+        for (int j = 0; j < kValsPerThread; ++j) {
+            const unsigned long long kj = key_at(j);
+            cnt += (kj != 0ull && kj >= t0) ? 1 : 0;
+        }
+    }
+    int incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(DDT_FULL_MASK, incl, o);
+        if (lane >= o) incl += t;
+    }
+    int wbase = 0;
+    if (lane == 31 && incl > 0) wbase = atomicAdd(&sel.count, incl);
+    wbase = __shfl_sync(DDT_FULL_MASK, wbase, 31);
+    if (cnt > 0) {
+        int pos = wbase + incl - cnt;
+#pragma unroll
+        for (int j = 0; j < kValsPerThread; ++j) {
+            if (take(j)) {
+                if (pos < kCandCap) cand[pos] = key_at(j);
+                ++pos;
             }
         }
-    });
+    }
     __syncthreads();
     const int ncand = sel.count;
     __syncthreads();
@@ -1116,6 +1135,7 @@ tree_build_kernel(const T* __restrict__ logits, int rows, int64_t vocab, int64_t
             }
         } else {
             const unsigned long long t1 = block_kth_largest_regs(key_at, kc, &sel);
+#pragma unroll
             for (int j = 0; j < kValsPerThread; ++j) {
                 const unsigned long long kj = key_at(j);
                 if (kj != 0ull && kj >= t1) {
@@ -1139,79 +1159,65 @@ tree_build_kernel(const T* __restrict__ logits, int rows, int64_t vocab, int64_t
     }
 
     // ---- hand-off to the row merge ---------------------------------------
-    __threadfence();
+    // The barrier orders every thread's writes before thread 0's fence and
+    // count (the grid-barrier pattern: one fence per CTA, cumulative through
+    // the barrier); the CTA that completes the count fences once more
+    // before its threads read the other chunks' results.
     __syncthreads();
-    if (tid == 0) s_flag = (atomicAdd(&row_cnt[d], 1u) == (uint32_t)(chunks - 1)) ? 1 : 0;
+    if (tid == 0) {
+        __threadfence();
+        s_flag = (atomicAdd(&row_cnt[d], 1u) == (uint32_t)(chunks - 1)) ? 1 : 0;
+        if (s_flag) __threadfence();
+    }
     __syncthreads();
     if (!s_flag) return;
-    __threadfence();
 
     // ---- phase B: merge the row ------------------------------------------
     // Every chunk list is sorted (descending, zero-padded) and the nonzero
-    // keys of a row are distinct.  Each list lies entirely at or above its
-    // last entry, so the largest last entry is at most the row's topk-th
-    // key: the keys at or above it are gathered and ranked by counting (a
-    // radix select first when they are many); the topk best land in order.
+    // keys of a row are distinct, so a key's rank in the row is its index in
+    // its own list plus, for each other list, the number of its keys above
+    // it (a binary search).  Each list lies entirely at or above its last
+    // entry, so the largest last entry is at most the row's topk-th key and
+    // only keys at or above it are ranked.  Warps 1.. rank; warp 0 computes
+    // the log-normaliser meanwhile.
     {
         const int n = chunks * topk;
         unsigned long long* mk = reinterpret_cast<unsigned long long*>(smem);
         unsigned long long* sk = mk + n;
-        unsigned long long* bc = sk + topk;   // gathered keys (at most n)
         const unsigned long long* src = part_keys + (int64_t)d * chunks * topk;
         for (int i = tid; i < n; i += kThreads) mk[i] = __ldcg(src + i);
         for (int i = tid; i < topk; i += kThreads) sk[i] = 0ull;
-        if (tid == 0) sel.count = 0;
         __syncthreads();
-        unsigned long long lb = 0ull;
-        for (int q = 0; q < chunks; ++q) {
-            const unsigned long long e = mk[q * topk + topk - 1];
-            lb = e > lb ? e : lb;
-        }
         const int lane_b = tid & 31;
-        for (int i0 = 0; i0 < n; i0 += kThreads) {
-            const int i = i0 + tid;
-            const unsigned long long x = i < n ? mk[i] : 0ull;
-            const bool take = x != 0ull && x >= lb;
-            const uint32_t bm = __ballot_sync(DDT_FULL_MASK, take);
-            if (bm) {
-                int base = 0;
-                if (lane_b == __ffs(bm) - 1) base = atomicAdd(&sel.count, __popc(bm));
-                base = __shfl_sync(DDT_FULL_MASK, base, __ffs(bm) - 1);
-                if (take) bc[base + __popc(bm & ((1u << lane_b) - 1u))] = x;
+        __shared__ float s_logz;
+        if (tid >= 32) {
+            unsigned long long lb = 0ull;
+            for (int q = 0; q < chunks; ++q) {
+                const unsigned long long e = mk[q * topk + topk - 1];
+                lb = e > lb ? e : lb;
             }
-        }
-        __syncthreads();
-        const int nb = sel.count;
-        __syncthreads();
-        if (nb <= kRankCap) {
-            for (int i = tid; i < nb; i += kThreads) {
-                const unsigned long long x = bc[i];
-                int r = 0;
-                for (int q = 0; q < nb; ++q) r += bc[q] > x ? 1 : 0;
+            for (int i = tid - 32; i < n; i += kThreads - 32) {
+                const unsigned long long x = mk[i];
+                if (x == 0ull || x < lb) continue;
+                const int qx = i / topk;
+                int r = i - qx * topk;
+                for (int q = 0; q < chunks; ++q) {
+                    if (q == qx) continue;
+                    const unsigned long long* lst = mk + q * topk;
+                    int lo = 0, hi = topk;   // keys of list q above x: a prefix
+                    while (lo < hi) {
+                        const int mid = (lo + hi) >> 1;
+                        if (lst[mid] > x)
+                            lo = mid + 1;
+                        else
+                            hi = mid;
+                    }
+                    r += lo;
+                    if (r >= topk) break;
+                }
                 if (r < topk) sk[r] = x;
             }
         } else {
-            if (tid == 0) sel.count = 0;
-            const int kt = min(topk, nb);
-            const unsigned long long t = block_kth_largest(bc, nb, kt, &sel);
-            for (int i = tid; i < nb; i += kThreads) {
-                const unsigned long long x = bc[i];
-                if (x >= t) {
-                    const int pos = atomicAdd(&sel.count, 1);
-                    if (pos < kt) mk[pos] = x;   // the chunk lists are no longer needed
-                }
-            }
-            __syncthreads();
-            for (int i = tid; i < kt; i += kThreads) {
-                const unsigned long long x = mk[i];
-                int r = 0;
-                for (int q = 0; q < kt; ++q) r += mk[q] > x ? 1 : 0;
-                sk[r] = x;
-            }
-        }
-        // log-normaliser: warp 0 combines the chunks' (max, sum of exp)
-        __shared__ float s_logz;
-        if (tid < 32) {
             float M = -INFINITY;
             bool nan_row = false;
             for (int q = lane_b; q < chunks; q += 32) {
@@ -1260,15 +1266,15 @@ tree_build_kernel(const T* __restrict__ logits, int rows, int64_t vocab, int64_t
         }
         if (bad) atomicOr(&done_cnt[1], DDT_INFO_NONFINITE);
     }
-    __threadfence();
-    __syncthreads();
+    __syncthreads();   // (the same one-fence hand-off as above)
     if (tid == 0) {
         row_cnt[d] = 0u;
+        __threadfence();
         s_flag = (atomicAdd(&done_cnt[0], 1u) == (uint32_t)(rows - 1)) ? 1 : 0;
+        if (s_flag) __threadfence();
     }
     __syncthreads();
     if (!s_flag) return;
-    __threadfence();
 
     // ---- phase C: expansion on the last CTA --------------------------------
     ExpandSmem e = carve_expand(smem, rows, topk, budget);
@@ -1319,7 +1325,7 @@ using namespace ddt;
 using namespace ddt::tree;
 
 static size_t phase_smem(int64_t rows, int64_t chunks, int64_t topk, int64_t budget) {
-    size_t a = sizeof(uint64_t) * (kThreads + kCandCap + kMaxBudget) + sizeof(float) * kMaxChunk;
+    size_t a = sizeof(uint64_t) * (kCandCap + kMaxBudget);   // phase A: candidates, selected keys
     size_t b = sizeof(uint64_t) * (2 * chunks * topk + topk);
     size_t c = expand_smem_bytes(rows, topk, budget);
     size_t m = a > b ? a : b;
