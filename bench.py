@@ -75,7 +75,10 @@ def parse():
     ap.add_argument("--warmup", type=int, default=None, help="untimed steps (default 3 / 5)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--kernel", choices=["attention", "tree_build", "expand", "accept", "compact", "sample"],
+    ap.add_argument("--cuda-profiler-range", action="store_true",
+                    help="decode: bracket the timed calls with cudaProfilerStart/Stop (for "
+                         "ncu --profile-from-start off launch lists of exactly the timed rounds)")
+    ap.add_argument("--kernel", choices=["attention", "tree_build", "expand", "accept", "compact", "sample", "gemm"],
                     default=None,
                     help="launch only this kernel of the step (warmup + steps times, eager) and print its "
                          "average CUDA-event time; used for small profiler captures")
@@ -430,18 +433,24 @@ def _peaks():
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 
 
-def _profiled_traffic():
-    """DRAM bytes per attention launch from the committed ncu summary, or None."""
-    f = ROOT / "profiles" / "tree_attn_split_kernel_qwen3_4b_verify.md"
+def _profile_traffic(f: Path, field: str = "traffic_bytes_per_launch:"):
+    """DRAM bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum)
+    from a committed profile summary's ``field`` line, or None."""
     if not f.exists():
         return None
     for line in f.read_text().splitlines():
-        if line.startswith("traffic_bytes_per_layer:"):
+        if line.startswith(field):
             try:
                 return int(line.split(":", 1)[1].strip().split()[0])
             except ValueError:
                 return None
     return None
+
+
+def _profiled_traffic():
+    """DRAM bytes per attention launch from the committed ncu summary, or None."""
+    return _profile_traffic(ROOT / "profiles" / "tree_attn_split_kernel_qwen3_4b_verify.md",
+                            "traffic_bytes_per_layer:")
 
 
 # ----------------------------------------------------------------------------
@@ -523,9 +532,19 @@ def run_kernel_only(args, local):
                                           max_accept=ROWS + 1)
     tensors = [t for pair in zip(w.ks, w.vs) for t in pair]
     acc_bufs_sample = torch.empty(N_VERIFY, dtype=torch.int64, device=device)
+    if args.kernel == "gemm":
+        # the decode round's gate/up GEMM: 33 verify rows x [2 * 9728, 2560]
+        # bf16, 36 different weights in turn (3.6 GB: every launch from HBM)
+        gg = torch.Generator(device=device).manual_seed(21)
+        gws = [(torch.randn((2 * 9728, 2560), generator=gg, device=device) * 0.02).to(torch.bfloat16)
+               for _ in range(LAYERS)]
+        gxs = [torch.randn((33, 2560), generator=gg, device=device).to(torch.bfloat16) for _ in range(LAYERS)]
+        gys = [torch.empty((33, 9728), dtype=torch.bfloat16, device=device) for _ in range(LAYERS)]
 
     def once(i):
-        if args.kernel == "attention":
+        if args.kernel == "gemm":
+            kernels.wgemm_gate_up(gxs[i % LAYERS], gws[i % LAYERS], out=gys[i % LAYERS])
+        elif args.kernel == "attention":
             layer = i % LAYERS
             kernels.tree_attention(w.qs[layer], w.ks[layer], w.vs[layer], PAST, tree.visibility, w.scale,
                                    out=w.outs[layer])
@@ -640,6 +659,67 @@ def _attention_roofline_at(device, past: int, n: int, reps: int = 20):
             "us_per_launch": round(us, 3)}
 
 
+def _gemm_roofline(target, device, rows: int, reps: int = 20):
+    """The decode round's dominant kernel: the weight-streaming gate/up GEMM
+    with the SiLU product in its epilogue (ddt_wgemm_gate_up), at the verify
+    rows, over the 36 layers' own packed weights in turn (3.6 GB per graph
+    replay, so every launch streams its 100 MB from HBM).  Algorithmic
+    bytes per launch: the weight, the activations in and the product out."""
+    from ddtree_eagle3_patch_b200 import kernels
+    from ddtree_eagle3_patch_b200.fused_layers import packed_weights
+    layers = list(target.model.layers)
+    wps = [packed_weights(layer)[1] for layer in layers]
+    H = wps[0].shape[1]
+    inter = wps[0].shape[0] // 2
+    g = torch.Generator(device=device).manual_seed(11)
+    xs = [torch.randn((rows, H), generator=g, device=device).to(torch.bfloat16) for _ in layers]
+    outs = [torch.empty((rows, inter), dtype=torch.bfloat16, device=device) for _ in layers]
+    stream = torch.cuda.Stream(device)
+    stream.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(stream), kernels.pdl(False):
+        for x, w, o in zip(xs, wps, outs):
+            kernels.wgemm_gate_up(x, w, out=o)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for x, w, o in zip(xs, wps, outs):
+                kernels.wgemm_gate_up(x, w, out=o)
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (reps * len(layers))
+    alg = wps[0].numel() * 2 + rows * H * 2 + rows * inter * 2
+    peaks = _peaks()
+    achieved = alg / (us * 1e-6) / 1e9
+    del graph
+    prof = ROOT / "profiles" / "wgemm_gate_up_qwen3_4b_verify.md"
+    traffic = _profile_traffic(prof)
+    return {"bound": "hbm", "kernel": f"wgemm_kernel gate/up + SiLU (ddt_wgemm_gate_up), {rows} rows x "
+                                      f"[{2 * inter} x {H}] bf16 weight",
+            "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "peak_source": peaks["source"],
+            "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4), "algorithmic_bytes": alg,
+            "us_per_launch": round(us, 3), "timing": "CUDA events over 36-launch graph replays, serial launches",
+            "traffic": traffic, "traffic_source": (f"profiles/{prof.name} (ncu, not this run)" if traffic else None)}
+
+
+def _round_bytes(target, draft, context: int) -> int:
+    """Algorithmic bytes of one decode round: every projection weight the
+    verify and draft forwards stream (the draft reuses the target's lm_head,
+    read again), and the K/V rows the attention reads at ``context``."""
+    lin = lambda m: sum(x.weight.numel() * x.weight.element_size() for x in m.modules()
+                        if isinstance(x, torch.nn.Linear))
+    cfg = target.config
+    kv = 2 * cfg.num_hidden_layers * cfg.num_key_value_heads * cfg.head_dim * 2 * context
+    dkv = 2 * len(draft.layers) * cfg.num_key_value_heads * cfg.head_dim * 2 * context
+    return lin(target) + lin(draft) + target.lm_head.weight.numel() * 2 + kv + dkv
+
+
 def run_decode(args, rank, world, local):
     from ddtree_eagle3_patch_b200 import _lib, kernels
     from ddtree_eagle3_patch_b200 import distributed as D
@@ -674,10 +754,14 @@ def run_decode(args, rank, world, local):
     with ClockSampler(_physical_index(local)) as clocks:
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if args.cuda_profiler_range:
+            torch.cuda.profiler.start()
         e0.record()
         results = [gen(dev_prompts[args.warmup + i]) for i in range(args.steps)]
         e1.record()
         barrier()
+        if args.cuda_profiler_range:
+            torch.cuda.profiler.stop()
     # this library's kernels run in the timed calls: eager launches plus every
     # replay of the ones captured in the per-call graphs
     launches = sum(r.native_launches for r in results)
@@ -709,9 +793,20 @@ def run_decode(args, rank, world, local):
     e2e_c = D.gather_counters([h0.elapsed_time(h1) / 1e3, e2e_tokens], device=device)
     e2e_value = float(e2e_c[:, 1].sum()) / float(e2e_c[:, 0].max())
 
-    # roofline of this package's dominant kernel in the round: the tree
-    # attention at the verify shape of mid-generation (prefix 512 + 512, 33 rows)
-    roof = _attention_roofline_at(device, DEC_PROMPT + args.new_tokens // 2, DEC_BUDGET + 1)
+    # roofline of the round's dominant kernel (the weight-streaming GEMMs hold
+    # about half of a round; the gate/up one is the largest), the tree
+    # attention at the verify shape of mid-generation (prefix 512 + 512, 33
+    # rows) beside it, and the round as a whole: algorithmic bytes per round
+    # over the measured decode time per round
+    roof = _gemm_roofline(target, device, DEC_BUDGET + 1)
+    roof_attn = _attention_roofline_at(device, DEC_PROMPT + args.new_tokens // 2, DEC_BUDGET + 1)
+    peaks = _peaks()
+    round_s = decode_s / max(rounds, 1)
+    round_bytes = _round_bytes(target, draft, DEC_PROMPT + args.new_tokens // 2)
+    roof_round = {"bound": "hbm", "algorithmic_bytes_per_round": round_bytes, "ms_per_round": round(round_s * 1e3, 4),
+                  "achieved": round(round_bytes / round_s / 1e9, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                  "frac": round(round_bytes / round_s / 1e9 / peaks["hbm_gbs"], 4),
+                  "bytes": "verify + draft projection weights (lm_head read twice) + K/V at the mean context"}
     status = kernels.attention_status(device)
     out = None
     if rank == 0:
@@ -730,7 +825,7 @@ def run_decode(args, rank, world, local):
             "tokens_per_round": round(tokens / max(rounds, 1), 4),
             "acceptance_histogram": {str(k): acc.count(k) for k in sorted(set(acc))},
             "stage_ms_per_round": per_round_ms,
-            "roofline": roof,
+            "roofline": roof, "roofline_attention": roof_attn, "roofline_round": roof_round,
             "e2e": {"value": round(e2e_value, 2), "unit": DEC_UNIT, "h2d_bytes_per_step": DEC_PROMPT * 8,
                     "d2h_bytes_per_step": (DEC_PROMPT + args.new_tokens) * 8,
                     "api": "ddtree_eagle3_patch_b200.ddtree.ddtree_generate (host prompt in, host ids out)"},
