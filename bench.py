@@ -70,7 +70,11 @@ WORKLOAD = (f"tree build [{ROWS}x{VOCAB}] fp32 budget {BUDGET} + tree-verify att
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--workload", choices=["decode", "step"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "decode-dp", "step"], default="decode",
+                    help="decode: Qwen3-4B, 512-token prompt, 1024 tokens, budget 32 (the headline); decode-dp: "
+                         "Qwen3-8B, --prompts prompts of 256-2048 tokens sharded over the GPUs, 512 tokens, "
+                         "budget 64; step: the per-round hot path alone")
+    ap.add_argument("--prompts", type=int, default=0, help="decode-dp: prompts in the list (default 64)")
     ap.add_argument("--steps", type=int, default=None, help="timed steps (decode: 3 calls; step: 200)")
     ap.add_argument("--warmup", type=int, default=None, help="untimed steps (default 3 / 5)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
@@ -841,6 +845,75 @@ def run_decode(args, rank, world, local):
     return out
 
 
+DP_SHAPE, DP_PROMPTS, DP_NEW_TOKENS, DP_BUDGET, DP_LEN = "qwen3-8b", 64, 512, 64, (256, 2048)
+
+
+def run_decode_dp(args, rank, world, local):
+    """Data-parallel decoding over prompts at the Qwen3-8B shape: a seeded
+    list of ``--prompts`` (default 64) uniform random prompts with lengths
+    uniform in [256, 2048], 512 new tokens each, node budget 64, block 16;
+    rank r decodes prompts r, r + N, ... (the reference shards its prompt
+    list the same way, benchmark.py:175) and one NCCL all-gather of a fixed
+    counter vector collects tokens and times.  ``value`` = every rank's
+    generated tokens / the slowest rank's time."""
+    from ddtree_eagle3_patch_b200 import distributed as D
+    from ddtree_eagle3_patch_b200.ddtree import ddtree_generate
+    from ddtree_eagle3_patch_b200.synthetic import build_decode_models, random_prompt
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    dist = init_dist(world, "nccl")
+    target, draft = build_decode_models(DP_SHAPE, device, torch.bfloat16, seed=0, draft_layers=DEC_DRAFT_LAYERS,
+                                        block_size=DEC_BLOCK)
+    mask_id = draft.mask_token_id
+    n_prompts = args.prompts or DP_PROMPTS
+    lens = np.random.RandomState(8000).randint(DP_LEN[0], DP_LEN[1] + 1, size=n_prompts)
+    mine = [random_prompt(int(lens[i]), seed=9000 + i, exclude=mask_id).to(device)
+            for i in range(rank, n_prompts, world)]
+
+    def gen(ids):
+        return ddtree_generate(draft, target, ids, mask_token_id=mask_id, max_new_tokens=DP_NEW_TOKENS,
+                               block_size=DEC_BLOCK, stop_token_ids=None, temperature=0.0, tree_budget=DP_BUDGET)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    gen(random_prompt(DP_LEN[1], seed=1, exclude=mask_id).to(device))   # capture at the longest prompt
+    barrier()
+    with ClockSampler(_physical_index(local)) as clocks:
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        results = [gen(p) for p in mine]
+        e1.record()
+        barrier()
+    elapsed = e0.elapsed_time(e1) / 1e3
+    tokens = sum(r.num_output_tokens for r in results)
+    rounds = sum(r.decode_rounds for r in results)
+    c = D.gather_counters([elapsed, tokens, rounds, len(results)], device=device)
+    wall = float(c[:, 0].max())
+    out = None
+    if rank == 0:
+        out = {"metric": "decode tok/s (Qwen3-8B shape, prompts sharded over GPUs)",
+               "value": round(float(c[:, 1].sum()) / wall, 2), "unit": DEC_UNIT, "n_gpus": world,
+               "steps": int(c[:, 3].sum()), "warmup": 1, "ms_per_step": round(wall / max(len(results), 1) * 1e3, 2),
+               "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+               "data": "synthetic (random-init weights, seeded uniform random prompt ids)",
+               "config": {"workload": (f"DDTree decode, random-init {DP_SHAPE} target + {DEC_DRAFT_LAYERS}-layer "
+                                       f"DFlash draft, block {DEC_BLOCK}, budget {DP_BUDGET}, {n_prompts} prompts of "
+                                       f"U[{DP_LEN[0]}, {DP_LEN[1]}] random ids, {DP_NEW_TOKENS} new tokens each, "
+                                       f"greedy, batch 1 per GPU"),
+                          "global_batch": world, "parallelism": f"data parallel x{world} over prompts"},
+               "per_rank_tokens": [int(x) for x in c[:, 1].tolist()],
+               "per_rank_s": [round(float(x), 3) for x in c[:, 0].tolist()],
+               "tokens_per_round": round(float(c[:, 1].sum()) / max(float(c[:, 2].sum()), 1.0), 4),
+               "clocks": clocks.summary()}
+    if world > 1:
+        dist.barrier()
+    return out
+
+
 def _cpu_decode_models():
     from ddtree_eagle3_patch_b200.synthetic import dflash_config, target_config
     from oracle.cpu_decode import build_cpu_models
@@ -920,7 +993,11 @@ def main():
     if args.kernel:
         run_kernel_only(args, local)
         return
-    if args.workload == "decode":
+    if args.workload == "decode-dp":
+        out = {"impl": "reference", "unavailable": "the Qwen3-8B data-parallel workload has no CPU arm (hours of "
+                                                   "CPU time per prompt); its reference arm is the decode workload's"} \
+            if args.impl == "reference" else run_decode_dp(args, rank, world, local)
+    elif args.workload == "decode":
         out = run_decode_reference(args, rank, world, local) if args.impl == "reference" else \
             run_decode(args, rank, world, local)
     elif args.impl == "reference":
