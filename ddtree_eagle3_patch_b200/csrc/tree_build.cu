@@ -223,6 +223,32 @@ __device__ __forceinline__ int64_t key_index(unsigned long long k) {
     return (int64_t)(0xffffffffu - (uint32_t)(k & 0xffffffffull));
 }
 __device__ __forceinline__ float key_value(unsigned long long k) { return unord_f32((uint32_t)(k >> 32)); }
+// Key of a chunk value at chunk-local index loc (0 past the chunk).
+__device__ __forceinline__ unsigned long long chunk_key(float v, int loc, int n_valid, int64_t c0) {
+    return loc < n_valid ? make_key(v, c0 + loc) : 0ull;
+}
+
+// Runs BODY with X = each value this thread holds in the staged chunk `cv`,
+// LOC = its chunk-local index and J = its slot (0 .. kValsPerThread-1), in
+// index order: a rolled loop over the thread's 16-byte vectors, unrolled
+// within one.  Each CTA runs a pass over ~17K values, so every instruction
+// per value costs ~130 issue cycles of its SM: the bodies are kept to a few.
+#define DDT_FOR_VALS(X, LOC, J, BODY)                                                             \
+    _Pragma("unroll 1") for (int jv_ = 0; jv_ < kNv; ++jv_) {                                     \
+        const int l0_ = (jv_ * kThreads + tid) * kEpv;                                            \
+        _Pragma("unroll") for (int h_ = 0; h_ < kEpv; h_ += 4) {                                  \
+            const float4 q_ = *reinterpret_cast<const float4*>(cv + l0_ + h_);                   \
+            const float qv_[4] = {q_.x, q_.y, q_.z, q_.w};                                       \
+            _Pragma("unroll") for (int e_ = 0; e_ < 4; ++e_) {                                    \
+                const float X = qv_[e_];                                                          \
+                const int LOC = l0_ + h_ + e_;                                                    \
+                const int J = jv_ * kEpv + h_ + e_;                                               \
+                (void)LOC;                                                                        \
+                (void)J;                                                                          \
+                BODY                                                                              \
+            }                                                                                     \
+        }                                                                                         \
+    }
 
 // ---------------------------------------------------------------------------
 // phase C: best-first expansion (ddtree.py:146-189)
@@ -963,48 +989,54 @@ tree_build_kernel(const T* __restrict__ logits, int rows, int64_t vocab, int64_t
     const int64_t c0 = (int64_t)c * chunk_len;
     const int64_t c1 = min(c0 + chunk_len, vocab);
 
-    // ---- load the chunk into registers -----------------------------------
+    // ---- load the chunk into shared memory -------------------------------
     // Thread tid holds the 16-byte vectors tid, tid + kThreads, ... of the
-    // chunk: value j of the thread has chunk-local index loc_of(j), and every
-    // loop below runs over j in that (index) order, fully unrolled so the
-    // values never leave registers.  Slots past the chunk hold -inf.
-    constexpr int kEpv = 16 / sizeof(T);  // elements per 16-byte vector
+    // chunk; the values stay in shared memory (chunk-local index) and each
+    // thread reads back only its own, in index order, with 16-byte loads (a
+    // warp reads 512 consecutive bytes: no bank conflicts).  The passes are
+    // rolled loops: this code runs once per CTA, and the same passes fully
+    // unrolled over register-held values spent most of their time waiting
+    // for instruction fetch.  Slots past the chunk hold -inf.
+    constexpr int kEpv = 16 / sizeof(T);          // elements per 16-byte vector
+    constexpr int kNv = kValsPerThread / kEpv;    // vectors per thread
     unsigned long long* cand = reinterpret_cast<unsigned long long*>(smem);
     unsigned long long* top = cand + kCandCap;
+    float* cv = reinterpret_cast<float*>(top + kMaxBudget);
     const int n_valid = (int)(c1 - c0);
-    float v[kValsPerThread];
 #pragma unroll
-    for (int j = 0; j < kValsPerThread / kEpv; ++j) {
+    for (int j = 0; j < kNv; ++j) {
         const int loc = (j * kThreads + tid) * kEpv;
+        float x[kEpv];
         if (kVec && loc + kEpv <= n_valid) {
             const uint4 raw = __ldcs(reinterpret_cast<const uint4*>(rowp + c0 + loc));
             const T* pv = reinterpret_cast<const T*>(&raw);
 #pragma unroll
-            for (int e = 0; e < kEpv; ++e) v[j * kEpv + e] = to_f32<T>(pv[e]);
+            for (int e = 0; e < kEpv; ++e) x[e] = to_f32<T>(pv[e]);
         } else {
 #pragma unroll
-            for (int e = 0; e < kEpv; ++e)
-                v[j * kEpv + e] = loc + e < n_valid ? to_f32<T>(rowp[c0 + loc + e]) : -INFINITY;
+            for (int e = 0; e < kEpv; ++e) x[e] = loc + e < n_valid ? to_f32<T>(rowp[c0 + loc + e]) : -INFINITY;
         }
+#pragma unroll
+        for (int e = 0; e < kEpv; e += 4)
+            *reinterpret_cast<float4*>(cv + loc + e) = make_float4(x[e], x[e + 1], x[e + 2], x[e + 3]);
     }
     auto loc_of = [&](int j) -> int { return ((j / kEpv) * kThreads + tid) * kEpv + (j % kEpv); };
 
     // ---- max and sum of exp (logsumexp pieces, ddtree.py:138) ----------
     // (a slot past the chunk adds exp(-inf) = +0 to the sum: no change)
-    // The same pass keeps the thread's largest value and its first slot
-    // (slots run in index order, so the lowest index among equal values).
+    // The same pass keeps the thread's largest value and its first index
+    // (values run in index order, so the lowest index among equal values).
     float m = -INFINITY, best = -INFINITY;
-    int bj = -1;
+    int bloc = -1;
     bool nan_seen = false;
-#pragma unroll
-    for (int j = 0; j < kValsPerThread; ++j) {
-        nan_seen |= (v[j] != v[j]);
-        m = fmaxf(m, v[j]);
-        if (v[j] > best) {
-            best = v[j];
-            bj = j;
+    DDT_FOR_VALS(x, loc, j, {
+        nan_seen |= (x != x);
+        m = fmaxf(m, x);
+        if (x > best) {
+            best = x;
+            bloc = loc;
         }
-    }
+    })
     if (tid == 0) s_flag = 0;
     __syncthreads();
     if (nan_seen) s_flag = 1;
@@ -1012,8 +1044,7 @@ tree_build_kernel(const T* __restrict__ logits, int rows, int64_t vocab, int64_t
     const bool any_nan = s_flag != 0;   // (set before block_max's barriers)
     float sum_t = 0.f;
     if (m != -INFINITY && m == m) {
-#pragma unroll
-        for (int j = 0; j < kValsPerThread; ++j) sum_t += expf(v[j] - m);
+        DDT_FOR_VALS(x, loc, j, { sum_t += expf(x - m); })
     }
     const double sum_c = block_sum_d((double)sum_t, red_d);
 
@@ -1022,24 +1053,21 @@ tree_build_kernel(const T* __restrict__ logits, int rows, int64_t vocab, int64_t
     // top kc keys go to part_keys in descending order, padded with zeros.
     const int kc = min(topk, n_valid);
     const int lane = tid & 31, warp = tid >> 5;
-    auto key_of = [&](float v, int loc) -> unsigned long long {
-        return loc < n_valid ? (((unsigned long long)ord_f32(v) << 32) |
-                                (unsigned long long)(0xffffffffu - (uint32_t)(c0 + loc)))
-                             : 0ull;
+    auto key_at = [&](int j) -> unsigned long long {   // (the rare radix-select path)
+        const int loc = loc_of(j);
+        return chunk_key(cv[loc], loc, n_valid, c0);
     };
-    auto key_at = [&](int j) -> unsigned long long { return key_of(v[j], loc_of(j)); };   // j: unrolled index
     // The thread's largest key.  Without NaN it is that of its first largest
     // value (up to the order of +0 and -0, which only lowers it: the bound
     // below stays a lower bound, built from keys the thread holds).
     unsigned long long tmax = 0ull;
     if (!any_nan) {
-        if (bj >= 0) tmax = key_of(best, loc_of(bj));
+        if (bloc >= 0) tmax = chunk_key(best, bloc, n_valid, c0);
     } else {
-#pragma unroll
-        for (int j = 0; j < kValsPerThread; ++j) {
-            const unsigned long long k = key_at(j);
+        DDT_FOR_VALS(x, loc, j, {
+            const unsigned long long k = chunk_key(x, loc, n_valid, c0);
             tmax = k > tmax ? k : tmax;
-        }
+        })
     }
     unsigned long long* dst = part_keys + ((int64_t)d * chunks + c) * topk;
     if (tid == 0) sel.count = 0;
@@ -1072,24 +1100,29 @@ tree_build_kernel(const T* __restrict__ logits, int rows, int64_t vocab, int64_t
     // one atomic per warp reserves the warp's slots.  Without NaN and with a
     // bound, the test is on the float value (greater: taken; equal: the key
     // decides, which also orders +0 / -0); else on the key.
+    // The thread's candidates are bits of a 64-bit mask over its slots; the
+    // write below visits only the set bits.
     const bool by_value = !any_nan && t0 != 0ull;
     const float t0v = key_value(t0);
-    auto take = [&](int j) -> bool {
-        if (by_value) return v[j] > t0v || (v[j] == t0v && key_at(j) >= t0);
-        const unsigned long long kj = key_at(j);
-        return kj != 0ull && kj >= t0;
-    };
-    int cnt = 0;
+    unsigned long long cmask = 0ull;
     if (by_value) {
-#pragma unroll
-        for (int j = 0; j < kValsPerThread; ++j) cnt += (v[j] > t0v || (v[j] == t0v && key_at(j) >= t0)) ? 1 : 0;
-    } else {
-#pragma unroll
-        for (int j = 0; j < kValsPerThread; ++j) {
-            const unsigned long long kj = key_at(j);
-            cnt += (kj != 0ull && kj >= t0) ? 1 : 0;
+        bool eq = false;
+        DDT_FOR_VALS(x, loc, j, {
+            cmask |= (unsigned long long)(x > t0v) << j;
+            eq |= (x == t0v);
+        })
+        if (eq) {   // values equal to the bound's: the key decides
+            DDT_FOR_VALS(x, loc, j, {
+                if (x == t0v && chunk_key(x, loc, n_valid, c0) >= t0) cmask |= 1ull << j;
+            })
         }
+    } else {
+        DDT_FOR_VALS(x, loc, j, {
+            const unsigned long long kx = chunk_key(x, loc, n_valid, c0);
+            if (kx != 0ull && kx >= t0) cmask |= 1ull << j;
+        })
     }
+    const int cnt = __popcll(cmask);
     int incl = cnt;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -1099,15 +1132,10 @@ tree_build_kernel(const T* __restrict__ logits, int rows, int64_t vocab, int64_t
     int wbase = 0;
     if (lane == 31 && incl > 0) wbase = atomicAdd(&sel.count, incl);
     wbase = __shfl_sync(DDT_FULL_MASK, wbase, 31);
-    if (cnt > 0) {
-        int pos = wbase + incl - cnt;
-#pragma unroll
-        for (int j = 0; j < kValsPerThread; ++j) {
-            if (take(j)) {
-                if (pos < kCandCap) cand[pos] = key_at(j);
-                ++pos;
-            }
-        }
+    int pos = wbase + incl - cnt;
+    for (unsigned long long mk = cmask; mk; mk &= mk - 1, ++pos) {
+        const int loc = loc_of(__ffsll((long long)mk) - 1);
+        if (pos < kCandCap) cand[pos] = chunk_key(cv[loc], loc, n_valid, c0);
     }
     __syncthreads();
     const int ncand = sel.count;
@@ -1325,7 +1353,8 @@ using namespace ddt;
 using namespace ddt::tree;
 
 static size_t phase_smem(int64_t rows, int64_t chunks, int64_t topk, int64_t budget) {
-    size_t a = sizeof(uint64_t) * (kCandCap + kMaxBudget);   // phase A: candidates, selected keys
+    // phase A: candidates, selected keys, the chunk's values
+    size_t a = sizeof(uint64_t) * (kCandCap + kMaxBudget) + sizeof(float) * kMaxChunk;
     size_t b = sizeof(uint64_t) * (2 * chunks * topk + topk);
     size_t c = expand_smem_bytes(rows, topk, budget);
     size_t m = a > b ? a : b;

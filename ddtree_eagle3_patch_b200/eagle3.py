@@ -50,10 +50,11 @@ def evaluate_eagle3_posterior(logits: torch.Tensor, draft_tokens: torch.Tensor, 
         accepted_indices = accepted[: accept_length + 1].cpu().tolist()
         sample_token = torch.full((1, 1), tok, dtype=torch.long, device=device)
         return best, accept_length, sample_token, candidates, accepted_indices
-    # temperature > 0 keeps the reference's sampling semantics (model/utils.py:31-35)
-    bsz, seq_len, vocab = logits.shape
-    probs = torch.softmax(logits.view(-1, vocab) / temperature, dim=-1)
-    node_posterior = torch.multinomial(probs, num_samples=1).view(bsz, seq_len)[0]
+    # temperature > 0: the reference draws every row once from
+    # softmax(logits / T) (sample, model/utils.py:31-35), then the bonus
+    # token once more from the last accepted row; both draws run on the
+    # sampling kernel (Gumbel-max, seeded from torch's generator)
+    node_posterior = kernels.sample(logits, temperature)[0]
     gather = retrieve_indices.clamp(min=0)
     paths = node_posterior[gather[:, :-1]]
     valid = retrieve_indices[:, 1:] >= 0
@@ -63,8 +64,7 @@ def evaluate_eagle3_posterior(logits: torch.Tensor, draft_tokens: torch.Tensor, 
     best = 0 if accept_length == 0 else int(torch.argmax(lengths).item())
     accepted_indices = [int(i) for i in retrieve_indices[best, : accept_length + 1].tolist()]
     last = accepted_indices[-1]
-    p_last = torch.softmax(logits[:, last, :] / temperature, dim=-1)
-    sample_token = torch.multinomial(p_last, num_samples=1).view(1, 1)
+    sample_token = kernels.sample(logits[:, last: last + 1, :], temperature).view(1, 1)
     return best, accept_length, sample_token, candidates, accepted_indices
 
 

@@ -105,3 +105,41 @@ def test_tiny_temperature_is_argmax_and_sample_mirror():
     torch.manual_seed(123)
     s2 = K.sample(x[None], 1.0)
     assert s1.shape == (1, 65) and torch.equal(s1, s2)
+
+
+@pytest.mark.gpu
+def test_eagle3_posterior_at_temperature_matches_reference_distribution():
+    """evaluate_eagle3_posterior at T > 0 (eagle3.py:46-79): every verify row
+    draws once from softmax(logits / T), the accepted length is the longest
+    matching prefix of the path, and the bonus token is a second draw from
+    the last accepted row.  On a three-node path with P(row 0 -> a) = 0.6
+    and P(row 1 -> b) = 0.5, the lengths 0 / 1 / 2 come out with
+    probabilities 0.4 / 0.3 / 0.3, and after length 0 the bonus token follows
+    row 0's distribution; both within 5 standard errors over 4000 calls."""
+    from ddtree_eagle3_patch_b200.eagle3 import evaluate_eagle3_posterior
+    dev = torch.device("cuda", 0)
+    V, t = 8, 0.7
+    a, b = 3, 5
+    p0 = np.full(V, 0.4 / (V - 1))
+    p0[a] = 0.6
+    p1 = np.full(V, 0.5 / (V - 1))
+    p1[b] = 0.5
+    p2 = np.full(V, 1.0 / V)
+    logits = torch.tensor(np.log(np.stack([p0, p1, p2])) * t, dtype=torch.float32, device=dev)[None]
+    draft = torch.tensor([[1, a, b]], dtype=torch.long, device=dev)
+    retrieve = torch.tensor([[0, 1, 2]], dtype=torch.long, device=dev)
+    torch.manual_seed(123)
+    n = 4000
+    lengths, bonus0 = np.zeros(3, np.int64), []
+    for _ in range(n):
+        best, length, tok, cand, acc = evaluate_eagle3_posterior(logits, draft, retrieve, t)
+        assert best == 0 and acc == [0, 1, 2][: length + 1]
+        lengths[length] += 1
+        if length == 0:
+            bonus0.append(int(tok.item()))
+    expect = np.array([0.4, 0.3, 0.3])
+    se = np.sqrt(expect * (1 - expect) / n)
+    assert np.all(np.abs(lengths / n - expect) <= 5 * se), lengths
+    m = len(bonus0)
+    freq = np.bincount(bonus0, minlength=V) / m
+    assert np.all(np.abs(freq - p0) <= 5 * np.sqrt(p0 * (1 - p0) / m) + 1e-12), freq
