@@ -65,7 +65,8 @@ struct Cfg {
     static constexpr uint32_t kStage = kWTile + kXTile;
     static constexpr uint32_t kBars = kStages * kStage;          // barriers after the ring
     static constexpr uint32_t kSmem = kBars + 256 + 1024;        // + alignment slack
-    static constexpr uint32_t kTmemCols = TP <= 32 ? 32 : 64;
+    static constexpr uint32_t kTmemCols = TP <= 32 ? 32 : TP <= 64 ? 64 : 128;   // a power of two >= TP
+    static_assert(TP % 16 == 0 && TP <= 128, "token tile: a multiple of 16 up to 128");
     static constexpr uint32_t kIdesc = idesc_bf16_f32(128, TP, false, false);
 };
 
@@ -197,26 +198,22 @@ wgemm_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUt
     const int n = n0 + row;
     float acc[TP];
     {
+        // TP columns: 32-column loads, then a 16-column one when TP % 32 == 16
         const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
-        uint32_t r[32];
-        if (TP >= 32) {
-            tmem_ld32(taddr, r);
+#pragma unroll
+        for (int c0 = 0; c0 + 32 <= TP; c0 += 32) {
+            uint32_t r[32];
+            tmem_ld32(taddr + c0, r);
             tmem_wait_ld();
 #pragma unroll
-            for (int c = 0; c < 32; ++c) acc[c] = __uint_as_float(r[c]);
+            for (int c = 0; c < 32; ++c) acc[c0 + c] = __uint_as_float(r[c]);
         }
-        if (TP == 16 || TP == 48) {
+        if (TP % 32 == 16) {
             uint32_t r16[16];
-            tmem_ld16(taddr + (TP == 48 ? 32 : 0), r16);
+            tmem_ld16(taddr + (TP - 16), r16);
             tmem_wait_ld();
 #pragma unroll
-            for (int c = 0; c < 16; ++c) acc[(TP == 48 ? 32 : 0) + c] = __uint_as_float(r16[c]);
-        }
-        if (TP == 64) {
-            tmem_ld32(taddr + 32, r);
-            tmem_wait_ld();
-#pragma unroll
-            for (int c = 0; c < 32; ++c) acc[32 + c] = __uint_as_float(r[c]);
+            for (int c = 0; c < 16; ++c) acc[TP - 16 + c] = __uint_as_float(r16[c]);
         }
     }
     if (p.splits == 1 && p.gate_up) {
@@ -383,7 +380,7 @@ static int wgemm_run(const void* x, int64_t x_stride, int64_t T, const void* w, 
                      int64_t splits_hint, void* workspace, size_t workspace_bytes, ddt_stream_t stream) {
     using namespace ddt::wgemm;
     if (!x || !w || !y) return set_error(DDT_EINVAL, "null argument");
-    if (T <= 0 || T > 64) return set_error(DDT_EUNSUPPORTED, "T=%lld outside [1, 64]", (long long)T);
+    if (T <= 0 || T > 128) return set_error(DDT_EUNSUPPORTED, "T=%lld outside [1, 128]", (long long)T);
     if (N <= 0 || N % BN || K <= 0 || K % BK)
         return set_error(DDT_EUNSUPPORTED, "N=%lld must be a multiple of 128 and K=%lld of 64", (long long)N,
                          (long long)K);
@@ -404,7 +401,9 @@ static int wgemm_run(const void* x, int64_t x_stride, int64_t T, const void* w, 
         splits = (int)(splits_hint < kMaxSplits ? splits_hint : kMaxSplits);
         if (splits > K / BK) splits = (int)(K / BK);
     }
-    const int TP = T <= 16 ? 16 : T <= 32 ? 32 : T <= 48 ? 48 : 64;
+    // token tile: the decode shapes (15 / 16 draft rows, 33 and 65 verify rows)
+    // pad to 16 / 48 / 80; others to the next of 16, 32, 48, 64, 80, 128
+    const int TP = T <= 16 ? 16 : T <= 32 ? 32 : T <= 48 ? 48 : T <= 64 ? 64 : T <= 80 ? 80 : 128;
     CUtensorMap tw, tx;
     int rc = make_map_2d(&tw, w, (uint64_t)K, (uint64_t)N, (uint64_t)w_stride * 2, BN);
     if (!rc) rc = make_map_2d(&tx, x, (uint64_t)K, (uint64_t)T, (uint64_t)x_stride * 2, (uint32_t)TP);
@@ -427,7 +426,9 @@ static int wgemm_run(const void* x, int64_t x_stride, int64_t T, const void* w, 
         case 16: return launch<16>(tw, tx, p, nblocks, st);
         case 32: return launch<32>(tw, tx, p, nblocks, st);
         case 48: return launch<48>(tw, tx, p, nblocks, st);
-        default: return launch<64>(tw, tx, p, nblocks, st);
+        case 64: return launch<64>(tw, tx, p, nblocks, st);
+        case 80: return launch<80>(tw, tx, p, nblocks, st);
+        default: return launch<128>(tw, tx, p, nblocks, st);
     }
 }
 

@@ -371,10 +371,10 @@ def _wgemm_workspace(device: torch.device) -> torch.Tensor:
 
 
 def wgemm_supported(x: torch.Tensor, w: torch.Tensor) -> bool:
-    """Shapes the weight-streaming GEMM takes: bf16, 1-64 rows of x, weight
+    """Shapes the weight-streaming GEMM takes: bf16, 1-128 rows of x, weight
     rows a multiple of 128, K a multiple of 64, 16-byte aligned rows."""
     return (x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and x.dim() == 2 and w.dim() == 2
-            and 1 <= x.shape[0] <= 64 and w.shape[0] % 128 == 0 and w.shape[1] % 64 == 0 and x.shape[1] == w.shape[1]
+            and 1 <= x.shape[0] <= 128 and w.shape[0] % 128 == 0 and w.shape[1] % 64 == 0 and x.shape[1] == w.shape[1]
             and x.stride(1) == 1 and w.stride(1) == 1 and x.stride(0) % 8 == 0 and w.stride(0) % 8 == 0
             and x.data_ptr() % 16 == 0 and w.data_ptr() % 16 == 0 and x.is_cuda and w.is_cuda)
 
@@ -382,7 +382,7 @@ def wgemm_supported(x: torch.Tensor, w: torch.Tensor) -> bool:
 def wgemm(x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor | None = None,
           out: torch.Tensor | None = None, splits: int = 0) -> torch.Tensor:
     """y = x @ w.T (+ residual) on the weight-streaming tcgen05 GEMM
-    (``ddt_wgemm``): x [T <= 64, K], w [N, K] bf16; the residual is added in
+    (``ddt_wgemm``): x [T <= 128, K], w [N, K] bf16; the residual is added in
     fp32 before the one rounding, as ``torch.addmm`` does."""
     if not wgemm_supported(x, w):
         raise ValueError("wgemm: unsupported shapes / layout (see wgemm_supported)")
@@ -419,7 +419,7 @@ def interleave_gate_up(w_gate: torch.Tensor, w_up: torch.Tensor) -> torch.Tensor
 def wgemm_gate_up(x: torch.Tensor, w_packed: torch.Tensor, out: torch.Tensor | None = None,
                   splits: int = 0) -> torch.Tensor:
     """act(x Wg^T) * (x Wu^T) with SiLU in one launch (``ddt_wgemm_gate_up``):
-    x [T <= 64, K] bf16, w_packed from ``interleave_gate_up`` [2I, K]; each
+    x [T <= 128, K] bf16, w_packed from ``interleave_gate_up`` [2I, K]; each
     product, the SiLU and the final product rounded to bf16 in the order of
     ``act_fn(gate_proj(x)) * up_proj(x)``.  Returns [T, I]."""
     if not wgemm_supported(x, w_packed):

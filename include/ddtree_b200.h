@@ -343,7 +343,7 @@ DDT_API int ddt_silu_mul_rows(const void* gate, const void* up, int64_t in_row_s
 /* Weight-streaming GEMM for the projections of the verify and draft
  * forwards (the target's and the draft's linear layers and lm_head run by
  * ddtree.py:476-486 and :523-531), at decode sizes:
- *   y[t, n] = sum_k x[t, k] * w[n, k] (+ residual[t, n]),   0 < T <= 64,
+ *   y[t, n] = sum_k x[t, k] * w[n, k] (+ residual[t, n]),   0 < T <= 128,
  * bf16 in and out, fp32 accumulation on the tensor cores, the residual added
  * in fp32 before the single rounding (torch.addmm).  N a multiple of 128, K
  * of 64; x and w 16-byte aligned with row strides of multiples of 8

@@ -40,6 +40,10 @@ def _case(T, N, K, seed, residual=False, x_pad=0):
     (64, 384, 640),
     (48, 256, 128),
     (17, 1024, 4096),
+    (65, 2560, 4096),     # budget-64 verify rows (token tile 80)
+    (65, 19456, 2560),
+    (100, 384, 640),      # token tile 128
+    (128, 256, 512),
 ])
 def test_wgemm_matches_float32(T, N, K):
     x, w, _, ref = _case(T, N, K, seed=T * 7 + N)
@@ -51,7 +55,8 @@ def test_wgemm_matches_float32(T, N, K):
     assert torch.equal(y, _k().wgemm(x, w))          # split-K order is fixed
 
 
-@pytest.mark.parametrize("T,N,K", [(33, 2560, 4096), (33, 2560, 9728), (16, 256, 512)])
+@pytest.mark.parametrize("T,N,K", [(33, 2560, 4096), (33, 2560, 9728), (16, 256, 512), (65, 2560, 9728),
+                                   (128, 2560, 4096)])
 def test_wgemm_residual_and_strided_rows(T, N, K):
     x, w, r, ref = _case(T, N, K, seed=N + K, residual=True, x_pad=64)
     assert x.stride(0) == K + 64
@@ -65,7 +70,7 @@ def test_wgemm_residual_and_strided_rows(T, N, K):
 
 def test_wgemm_rejects_unsupported_shapes():
     K = _k()
-    x = torch.zeros(65, 128, dtype=torch.bfloat16, device=DEV)
+    x = torch.zeros(129, 128, dtype=torch.bfloat16, device=DEV)
     w = torch.zeros(128, 128, dtype=torch.bfloat16, device=DEV)
     assert not K.wgemm_supported(x, w)
     assert not K.wgemm_supported(x[:4], torch.zeros(100, 128, dtype=torch.bfloat16, device=DEV))
@@ -79,6 +84,9 @@ def test_wgemm_rejects_unsupported_shapes():
     (16, 9728, 2560, 0),    # draft rows, automatic split
     (5, 128, 256, 4),
     (64, 256, 512, 0),
+    (65, 9728, 2560, 1),    # budget-64 verify rows, token tile 80
+    (65, 9728, 2560, 2),
+    (128, 512, 1024, 3),    # token tile 128 through the cluster reduction
 ])
 def test_wgemm_gate_up_equals_separate_products(T, I, K, splits):
     """The fused epilogue rounds gate and up to bf16, then SiLU, then the
