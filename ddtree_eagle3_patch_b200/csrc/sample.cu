@@ -11,7 +11,8 @@
 // the same draws on every run and a new offset gives fresh ones.  The draws
 // follow the same distribution as torch's, not torch's generator stream.
 //
-// Bound: HBM, one read of the logits (n_rows x vocab elements).  Two launches:
+// Bound: compute (a quarter of a Philox block and two logarithms per
+// element), over one read of the logits (n_rows x vocab).  Two launches:
 // (rows x chunks) CTAs each reduce a chunk to its best 64-bit key (ordered
 // value, then the complement of the index, so ties go to the lower index)
 // into the workspace; one warp per row then reduces its chunks.

@@ -183,6 +183,22 @@ def _fused_forward(self, hidden_states, attention_mask=None, position_ids=None, 
     return residual_linear(a, mlp.down_proj.weight, x2, "down").unsqueeze(0)
 
 
+def rms_norm_rows(norm, x: torch.Tensor) -> torch.Tensor:
+    """``norm(x)`` for a Qwen3RMSNorm over the last dimension: one launch of
+    the fused RMSNorm kernel (the stock module's rounding order) for a CUDA
+    tensor with contiguous rows in the weight's dtype, else the module's own
+    forward."""
+    if not x.is_cuda or x.stride(-1) != 1 or x.dtype != norm.weight.dtype \
+            or x.dtype not in (torch.bfloat16, torch.float16, torch.float32):
+        return type(norm).forward(norm, x)
+    rows = x.reshape(-1, x.shape[-1])
+    return kernels.rms_norm(rows, norm.weight, norm.variance_epsilon).view(x.shape)
+
+
+def _norm_forward(self, hidden_states):
+    return rms_norm_rows(self, hidden_states)
+
+
 def _decoder_layers(model):
     inner = getattr(model, "model", model)
     layers = getattr(inner, "layers", None)
@@ -199,7 +215,12 @@ def fused_decoder_layers(target):
             if supported_layer(layer) and "forward" not in layer.__dict__:
                 layer.forward = types.MethodType(_fused_forward, layer)
                 patched.append(layer)
+        # the final norm before the lm_head, as one launch
+        norm = getattr(getattr(target, "model", target), "norm", None)
+        if patched and norm is not None and hasattr(norm, "variance_epsilon") and "forward" not in norm.__dict__:
+            norm.forward = types.MethodType(_norm_forward, norm)
+            patched.append(norm)
         yield len(patched)
     finally:
-        for layer in patched:
-            layer.__dict__.pop("forward", None)
+        for module in patched:
+            module.__dict__.pop("forward", None)

@@ -286,9 +286,16 @@ class DFlashDraftModel(Qwen3PreTrainedModel):
         ctx_count] (see DFlashAttention.forward_static); ``position_ids``
         cover the context rows then the block rows.  ``past_max`` bounds
         start."""
+        from .fused_layers import linear_rows, rms_norm_rows
+        fused = os.environ.get("DDTREE_FUSED", "1") != "0"
+        norm = (lambda m, x: rms_norm_rows(m, x)) if fused else (lambda m, x: m(x))
         hidden_states = noise_embedding
-        ctx = self.hidden_norm(self.fc(target_hidden))
+        if fused and target_hidden.shape[0] == 1 and self.fc.bias is None:   # on the weight-streaming GEMM
+            fc_out = linear_rows(target_hidden[0], self.fc.weight, "fc").unsqueeze(0)
+        else:
+            fc_out = self.fc(target_hidden)
+        ctx = norm(self.hidden_norm, fc_out)
         position_embeddings = self.rotary_emb(hidden_states, position_ids)
         for layer in self.layers:
             hidden_states = layer.forward_static(hidden_states, ctx, position_embeddings, cache, rs, past_max, workspace)
-        return self.norm(hidden_states)
+        return norm(self.norm, hidden_states)
