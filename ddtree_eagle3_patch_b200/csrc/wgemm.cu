@@ -217,23 +217,21 @@ wgemm_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUt
         }
     }
     if (p.splits == 1 && p.gate_up) {
-        // the up rows (lanes 64..127) hand their accumulators to the gate
-        // rows through the idle ring
-        float* up = reinterpret_cast<float*>(smem);   // [TP][64]
-        if (row >= 64) {
+        // every accumulator goes through the idle ring, [TP][128], so that
+        // all four warps share the SiLU products: thread (c, h) = (row % 64,
+        // row / 64) writes column c at token rows h, h + 2, ...  The products
+        // (an accurate exp and an IEEE divide each) are a long dependent
+        // chain: unrolled by four, independent rows overlap.
+        float* gu = reinterpret_cast<float*>(smem);
 #pragma unroll
-            for (int t = 0; t < TP; ++t) up[t * 64 + row - 64] = acc[t];
-        }
+        for (int t = 0; t < TP; ++t) gu[t * BN + row] = acc[t];
         __syncthreads();
-        if (row < 64) {
-            const int col = nb * 64 + row;
-#pragma unroll
-            for (int t = 0; t < TP; ++t) {
-                if (t < p.T)
-                    p.y[(int64_t)t * p.y_stride + col] =
-                        silu_times(__float2bfloat16_rn(acc[t]), __float2bfloat16_rn(up[t * 64 + row]));
-            }
-        }
+        const int c = row & 63, h = row >> 6;
+        const int col = nb * 64 + c;
+#pragma unroll 4
+        for (int t = h; t < p.T; t += 2)
+            p.y[(int64_t)t * p.y_stride + col] =
+                silu_times(__float2bfloat16_rn(gu[t * BN + c]), __float2bfloat16_rn(gu[t * BN + 64 + c]));
     } else if (p.splits == 1) {
 #pragma unroll
         for (int t = 0; t < TP; ++t) {
@@ -257,29 +255,46 @@ wgemm_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUt
         cluster_sync();
         const int r = (int)cluster_ctarank();
         float* pair = stage + TP * BN;   // gate/up mode: the reduced [TP][128] sums
-        for (int t = r; t < p.T; t += p.splits) {
-            float part[kMaxSplits];
+        // kRows of this CTA's token rows at a time: every peer load and
+        // residual load of the group is issued before the first sum, so
+        // their latencies overlap instead of adding up row by row
+        constexpr int kRows = 4;
+        for (int t0 = r; t0 < p.T; t0 += kRows * p.splits) {
+            float part[kRows][kMaxSplits];
+            float res[kRows];
 #pragma unroll
-            for (int q = 0; q < kMaxSplits; ++q)
-                part[q] = q < p.splits ? ld_dsmem_f32(stage + t * BN + row, (uint32_t)q) : 0.f;
-            float v = 0.f;
+            for (int j = 0; j < kRows; ++j) {
+                const int t = t0 + j * p.splits;
+                const bool in = t < p.T;
 #pragma unroll
-            for (int q = 0; q < kMaxSplits; ++q) v += part[q];
-            if (p.gate_up) {
-                pair[t * BN + row] = v;
-                continue;
+                for (int q = 0; q < kMaxSplits; ++q)
+                    part[j][q] = in && q < p.splits ? ld_dsmem_f32(stage + t * BN + row, (uint32_t)q) : 0.f;
+                res[j] = in && p.residual ? __bfloat162float(p.residual[(int64_t)t * p.r_stride + n]) : 0.f;
             }
-            if (p.residual) v += __bfloat162float(p.residual[(int64_t)t * p.r_stride + n]);
-            p.y[(int64_t)t * p.y_stride + n] = __float2bfloat16_rn(v);
+#pragma unroll
+            for (int j = 0; j < kRows; ++j) {
+                const int t = t0 + j * p.splits;
+                if (t >= p.T) break;
+                float v = 0.f;
+#pragma unroll
+                for (int q = 0; q < kMaxSplits; ++q) v += part[j][q];
+                if (p.gate_up) {
+                    pair[t * BN + row] = v;
+                    continue;
+                }
+                if (p.residual) v += res[j];
+                p.y[(int64_t)t * p.y_stride + n] = __float2bfloat16_rn(v);
+            }
         }
         if (p.gate_up) {
+            // the SiLU products of this CTA's token rows, over all four warps
             __syncthreads();
-            if (row < 64) {
-                const int col = nb * 64 + row;
-                for (int t = r; t < p.T; t += p.splits)
-                    p.y[(int64_t)t * p.y_stride + col] = silu_times(__float2bfloat16_rn(pair[t * BN + row]),
-                                                                    __float2bfloat16_rn(pair[t * BN + 64 + row]));
-            }
+            const int c = row & 63, h = row >> 6;
+            const int col = nb * 64 + c;
+#pragma unroll 4
+            for (int t = r + h * p.splits; t < p.T; t += 2 * p.splits)
+                p.y[(int64_t)t * p.y_stride + col] = silu_times(__float2bfloat16_rn(pair[t * BN + c]),
+                                                                __float2bfloat16_rn(pair[t * BN + 64 + c]));
         }
         cluster_sync();
     }

@@ -118,7 +118,7 @@ def test_gather_counters_one_collective():
     assert got[0] == expect and got[1] == expect
 
 
-def _failing_worker(rank: int, world: int, port: int, mode: str, out):
+def _failing_worker(rank: int, world: int, port: int, mode: str, out, ready):
     """Rank 1 fails between steps (exits, raises, or stalls); rank 0 goes on
     to the next step's collective and must get an error within the process
     group's timeout instead of waiting for ever."""
@@ -127,6 +127,9 @@ def _failing_worker(rank: int, world: int, port: int, mode: str, out):
                        "MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port)})
     from datetime import timedelta
     from ddtree_eagle3_patch_b200 import distributed as dist
+    # both ranks have imported everything before the rendezvous starts, so
+    # the short timeout below measures the failure, not a slow import
+    ready.wait(timeout=120)
     dist.init(backend="gloo", timeout=timedelta(seconds=3))
     t0 = time.perf_counter()
     try:
@@ -153,7 +156,8 @@ def test_failed_rank_is_detected_by_the_next_collective(mode):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_failing_worker, args=(r, WORLD, port, mode, q)) for r in range(WORLD)]
+    ready = ctx.Barrier(WORLD)
+    procs = [ctx.Process(target=_failing_worker, args=(r, WORLD, port, mode, q, ready)) for r in range(WORLD)]
     for p in procs:
         p.start()
     kind, waited = q.get(timeout=90)
