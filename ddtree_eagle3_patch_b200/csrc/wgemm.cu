@@ -337,24 +337,55 @@ static int make_map_2d(CUtensorMap* m, const void* base, uint64_t cols, uint64_t
     return DDT_OK;
 }
 
-static int choose_splits(int64_t N, int64_t K, int sms) {
+// The kernel's shared-memory opt-in, once per token tile.
+template <int TP>
+static cudaError_t prepare() {
+    static std::once_flag once;
+    static cudaError_t attr = cudaSuccess;
+    std::call_once(once, [] {
+        attr = cudaFuncSetAttribute(wgemm_kernel<TP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)Cfg<TP>::kSmem);
+    });
+    return attr;
+}
+
+// CTAs of token tile TP that fit on one SM by shared memory (228 KB per SM,
+// 1 KB of it reserved per CTA).
+static int ctas_per_sm(int TP) {
+    uint32_t smem = 0;
+    switch (TP) {
+        case 16: smem = Cfg<16>::kSmem; break;
+        case 32: smem = Cfg<32>::kSmem; break;
+        case 48: smem = Cfg<48>::kSmem; break;
+        case 64: smem = Cfg<64>::kSmem; break;
+        case 80: smem = Cfg<80>::kSmem; break;
+        default: smem = Cfg<128>::kSmem; break;
+    }
+    const int n = (int)((228u * 1024u) / (smem + 1024u));
+    return n < 1 ? 1 : n;
+}
+
+// About one wave of two CTAs per SM, and at most 90 % of the CTAs that fit
+// at once: a grid of clusters that fills them (almost) exactly runs part of
+// it as a second wave.  Measured on B200 at 33 token rows (two CTAs per SM):
+// 48 row blocks x 6 splits (288 CTAs) 17.4 us, x 5 splits 10.5 us; 32 x 8
+// (256 CTAs) ran in one wave.  At 16 rows (three per SM) 48 x 6 is the best.
+static int choose_splits(int64_t N, int64_t K, int sms, int TP) {
     const int64_t nblocks = N / BN, nk = K / BK;
-    int64_t s = (2LL * (sms > 0 ? sms : 148)) / nblocks;   // about one wave of two CTAs per SM
-    if (s < 1) s = 1;
+    if (sms <= 0) sms = 148;
+    const int per_sm = ctas_per_sm(TP);
+    const int64_t wave = (int64_t)sms * (per_sm < 2 ? per_sm : 2);
+    const int64_t fit = (int64_t)sms * per_sm * 9 / 10;
+    int64_t s = (wave < fit ? wave : fit) / nblocks;
     if (s > kMaxSplits) s = kMaxSplits;
     if (s > nk / 2) s = nk / 2;                            // at least two stages per split
-    if (s < 1) s = 1;                                      // (and never more splits than stages)
-    return (int)s;
+    return s < 1 ? 1 : (int)s;
 }
 
 template <int TP>
 static int launch(const CUtensorMap& tw, const CUtensorMap& tx, const Params& p, int nblocks, cudaStream_t st) {
     using C = Cfg<TP>;
-    static std::once_flag once;
-    static cudaError_t attr = cudaSuccess;
-    std::call_once(once, [] {
-        attr = cudaFuncSetAttribute(wgemm_kernel<TP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmem);
-    });
+    const cudaError_t attr = prepare<TP>();
     if (attr != cudaSuccess) return set_error(DDT_ECUDA, "cudaFuncSetAttribute(wgemm): %s", cudaGetErrorString(attr));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)nblocks, (unsigned)p.splits);
@@ -411,14 +442,14 @@ static int wgemm_run(const void* x, int64_t x_stride, int64_t T, const void* w, 
                          ddt_wgemm_workspace_size(T, N, K));
     int dev = 0;
     cudaGetDevice(&dev);
-    int splits = choose_splits(N, K, ddt_sm_count(dev));
+    // token tile: the decode shapes (15 / 16 draft rows, 33 and 65 verify rows)
+    // pad to 16 / 48 / 80; others to the next of 16, 32, 48, 64, 80, 128
+    const int TP = T <= 16 ? 16 : T <= 32 ? 32 : T <= 48 ? 48 : T <= 64 ? 64 : T <= 80 ? 80 : 128;
+    int splits = choose_splits(N, K, ddt_sm_count(dev), TP);
     if (splits_hint > 0) {   // the caller's choice, within the cluster limit and the K stages
         splits = (int)(splits_hint < kMaxSplits ? splits_hint : kMaxSplits);
         if (splits > K / BK) splits = (int)(K / BK);
     }
-    // token tile: the decode shapes (15 / 16 draft rows, 33 and 65 verify rows)
-    // pad to 16 / 48 / 80; others to the next of 16, 32, 48, 64, 80, 128
-    const int TP = T <= 16 ? 16 : T <= 32 ? 32 : T <= 48 ? 48 : T <= 64 ? 64 : T <= 80 ? 80 : 128;
     CUtensorMap tw, tx;
     int rc = make_map_2d(&tw, w, (uint64_t)K, (uint64_t)N, (uint64_t)w_stride * 2, BN);
     if (!rc) rc = make_map_2d(&tx, x, (uint64_t)K, (uint64_t)T, (uint64_t)x_stride * 2, (uint32_t)TP);
