@@ -46,7 +46,7 @@ def test_sharding_gather_and_counters(n_prompts):
         p.start()
     results = {}
     for _ in range(WORLD):
-        rank, mine, gathered, everyone, main = q.get(timeout=120)
+        rank, mine, gathered, everyone, main = q.get(timeout=300)
         results[rank] = (mine, gathered, everyone, main)
     for p in procs:
         p.join(timeout=60)
@@ -110,7 +110,7 @@ def test_gather_counters_one_collective():
     procs = [ctx.Process(target=_counter_worker, args=(r, WORLD, port, q)) for r in range(WORLD)]
     for p in procs:
         p.start()
-    got = dict(q.get(timeout=120) for _ in range(WORLD))
+    got = dict(q.get(timeout=300) for _ in range(WORLD))
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
@@ -129,7 +129,7 @@ def _failing_worker(rank: int, world: int, port: int, mode: str, out, ready):
     from ddtree_eagle3_patch_b200 import distributed as dist
     # both ranks have imported everything before the rendezvous starts, so
     # the short timeout below measures the failure, not a slow import
-    ready.wait(timeout=120)
+    ready.wait(timeout=300)
     dist.init(backend="gloo", timeout=timedelta(seconds=3))
     t0 = time.perf_counter()
     try:
@@ -160,7 +160,7 @@ def test_failed_rank_is_detected_by_the_next_collective(mode):
     procs = [ctx.Process(target=_failing_worker, args=(r, WORLD, port, mode, q, ready)) for r in range(WORLD)]
     for p in procs:
         p.start()
-    kind, waited = q.get(timeout=90)
+    kind, waited = q.get(timeout=360)   # cold imports in a fresh container take minutes
     for p in procs:
         p.join(timeout=5)
         if p.is_alive():
