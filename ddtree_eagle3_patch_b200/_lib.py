@@ -102,6 +102,11 @@ _SIGNATURES = {
                                  _c_p, ctypes.c_size_t, _c_p]),
     "ddt_wgemm_gate_up": (ctypes.c_int, [_c_p, _c_i64, _c_i64, _c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_i64, _c_p,
                                          ctypes.c_size_t, _c_p]),
+    "ddt_wgemm_head_stats_size": (ctypes.c_size_t, [_c_i64, _c_i64]),
+    "ddt_wgemm_head": (ctypes.c_int, [_c_p, _c_i64, _c_i64, _c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_p,
+                                      ctypes.c_size_t, _c_p, ctypes.c_size_t, _c_p]),
+    "ddt_tree_build_head": (ctypes.c_int, [_c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_p, _c_i64,
+                                           ctypes.POINTER(TreeOutputs), _c_p, ctypes.c_size_t, _c_p]),
     "ddt_set_pdl": (ctypes.c_int, [ctypes.c_int]),
     "ddt_tree_accept_workspace_size": (ctypes.c_size_t, [_c_i64, _c_i64]),
     "ddt_tree_accept": (ctypes.c_int, [_c_p, ctypes.c_int, _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_p,

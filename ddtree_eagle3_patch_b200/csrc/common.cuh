@@ -56,6 +56,33 @@ __device__ __forceinline__ float unord_f32(uint32_t o) {
     uint32_t u = (o & 0x80000000u) ? (o & 0x7fffffffu) : ~o;
     return __uint_as_float(u);
 }
+// Top-k key of a logit: the ordered value, then the complement of the token
+// id, so that larger keys are larger values and, among equal values, lower
+// ids (torch.topk's order is undefined on ties; this library's is this one).
+__device__ __forceinline__ unsigned long long topk_key(float v, int64_t idx) {
+    return ((unsigned long long)ord_f32(v) << 32) | (unsigned long long)(0xffffffffu - (uint32_t)idx);
+}
+
+// Per-block statistics that the draft head's GEMM (ddt_wgemm_head) leaves
+// for the tree build (ddt_tree_build_head): for every token row t and every
+// block b of 128 vocabulary rows, the max m[t][b] of the block's bf16
+// logits (NaN if the block holds one), s[t][b] = sum of exp(x - m[t][b])
+// over them (summed in float64, stored as float32), and the block's largest
+// topk_key() key[t][b].
+constexpr int kHeadBlock = 128;
+struct HeadStatsLayout {
+    size_t m, s, keys, total;
+};
+__host__ __device__ inline HeadStatsLayout head_stats_layout(int64_t rows, int64_t nblk) {
+    HeadStatsLayout h;
+    const size_t n = (size_t)rows * (size_t)nblk;
+    h.m = 0;
+    h.s = (sizeof(float) * n + 255) & ~size_t(255);
+    h.keys = h.s + ((sizeof(float) * n + 255) & ~size_t(255));
+    h.total = h.keys + sizeof(unsigned long long) * n;
+    return h;
+}
+
 // Same for float64.
 __device__ __forceinline__ uint64_t ord_f64(double d) {
     uint64_t u = (uint64_t)__double_as_longlong(d);

@@ -30,6 +30,7 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kValsPerThread = 40;
 constexpr int kMaxChunk = kThreads * kValsPerThread;  // 20480 elements: a 151936-wide row in 8 chunks
 constexpr int kCandCap = 2048;
+constexpr int kHeadCandCap = kMaxChunk / 2;   // head-statistics mode: candidates held in the staging area
 constexpr int kMaxRows = 32;
 constexpr int kMaxBudget = 1024;
 constexpr int kMergeCap = 16384;  // chunks * topk keys held by the merging CTA
@@ -216,9 +217,7 @@ __device__ __forceinline__ unsigned long long block_kth_largest_regs(KeyAt key_a
     return t;
 }
 
-__device__ __forceinline__ unsigned long long make_key(float v, int64_t idx) {
-    return ((unsigned long long)ord_f32(v) << 32) | (unsigned long long)(0xffffffffu - (uint32_t)idx);
-}
+__device__ __forceinline__ unsigned long long make_key(float v, int64_t idx) { return topk_key(v, idx); }
 __device__ __forceinline__ int64_t key_index(unsigned long long k) {
     return (int64_t)(0xffffffffu - (uint32_t)(k & 0xffffffffull));
 }
@@ -966,7 +965,7 @@ template <typename T, bool kVec>
 __global__ void __launch_bounds__(kThreads, 1)
 tree_build_kernel(const T* __restrict__ logits, int rows, int64_t vocab, int64_t row_stride, int topk, int chunks,
                   int64_t chunk_len, int budget, const int64_t* root_token, int64_t start, ddt_tree_outputs out,
-                  unsigned char* ws) {
+                  unsigned char* ws, const unsigned char* __restrict__ hstats) {
     extern __shared__ __align__(256) unsigned char smem[];
     __shared__ SelectScratch sel;
     __shared__ unsigned long long s_offer[kWarps];
@@ -1003,6 +1002,92 @@ tree_build_kernel(const T* __restrict__ logits, int rows, int64_t vocab, int64_t
     unsigned long long* top = cand + kCandCap;
     float* cv = reinterpret_cast<float*>(top + kMaxBudget);
     const int n_valid = (int)(c1 - c0);
+    // Keys are (value order, then lower token id) and distinct.  The chunk's
+    // top kc keys go to part_keys in descending order, padded with zeros.
+    const int kc = min(topk, n_valid);
+    const int lane = tid & 31, warp = tid >> 5;
+    unsigned long long* dst = part_keys + ((int64_t)d * chunks + c) * topk;
+    auto loc_of = [&](int j) -> int { return ((j / kEpv) * kThreads + tid) * kEpv + (j % kEpv); };
+    auto key_at = [&](int j) -> unsigned long long {   // (the rare radix-select path)
+        const int loc = loc_of(j);
+        return chunk_key(cv[loc], loc, n_valid, c0);
+    };
+    float m = -INFINITY;
+    double sum_c = 0.0;
+    int cand_cap = kCandCap;
+    if (hstats) {
+        // ---- phase A from the draft head's block statistics ---------------
+        // (ddt_tree_build_head).  The chunk is a run of whole 128-row blocks.
+        // Its max and sum of exp come from the blocks' (max, sum), rescaled
+        // in float64.  Its top kc keys lie in the kc blocks with the largest
+        // block keys (a block holding a key of the top kc has a block key at
+        // least that large; the kc-th largest block key t0 is at most the
+        // kc-th largest key, since the kc best blocks hold kc keys >= t0).
+        // Those blocks are read from the logits for their keys >= t0: the
+        // candidates, few unless many values are equal.  The staging area
+        // `cv` is unused in this mode and holds them.
+        cand = reinterpret_cast<unsigned long long*>(cv);
+        cand_cap = kHeadCandCap;
+        const int nblk = (int)(vocab / kHeadBlock);
+        const HeadStatsLayout hl = head_stats_layout(rows, nblk);
+        const float* hm = reinterpret_cast<const float*>(hstats + hl.m) + (int64_t)d * nblk;
+        const float* hs = reinterpret_cast<const float*>(hstats + hl.s) + (int64_t)d * nblk;
+        const unsigned long long* hk = reinterpret_cast<const unsigned long long*>(hstats + hl.keys) + (int64_t)d * nblk;
+        const int b0 = (int)(c0 / kHeadBlock), b1 = (int)((c1 + kHeadBlock - 1) / kHeadBlock);
+        const int nb = b1 - b0;                                   // <= kMaxBudget (host)
+        unsigned long long* bkey = top;                           // the chunk's block keys
+        int* pick = reinterpret_cast<int*>(top + kMaxBudget / 2); // the blocks to read (<= kc <= 4 * kMaxBudget / 2)
+        float mloc = -INFINITY;
+        bool nan_l = false;
+        for (int b = tid; b < nb; b += kThreads) {
+            const float mb = __ldcg(hm + b0 + b);
+            nan_l |= mb != mb;
+            mloc = fmaxf(mloc, mb);
+            bkey[b] = __ldcg(hk + b0 + b);
+        }
+        if (tid == 0) {
+            s_flag = 0;
+            sel.count = 0;   // candidates
+            sel.need = 0;    // blocks picked
+        }
+        __syncthreads();
+        if (nan_l) s_flag = 1;
+        m = block_max(mloc, red_f);
+        double sl = 0.0;
+        if (m != -INFINITY && m == m) {
+            for (int b = b0 + tid; b < b1; b += kThreads) {
+                const float mb = __ldcg(hm + b);
+                if (mb != -INFINITY) sl += (double)__ldcg(hs + b) * exp((double)mb - (double)m);
+            }
+        }
+        sum_c = block_sum_d(sl, red_d);   // (its barriers order the bkey writes and sel's reset)
+        // rank of each block key by counting; the block of rank kc - 1 gives t0
+        __shared__ unsigned long long s_t0;
+        if (tid == 0) s_t0 = 0ull;
+        __syncthreads();
+        for (int b = tid; b < nb; b += kThreads) {
+            const unsigned long long kb = bkey[b];
+            int r = 0;
+            for (int q = 0; q < nb; ++q) r += bkey[q] > kb ? 1 : 0;
+            if (r < kc) pick[atomicAdd(&sel.need, 1)] = b;
+            if (r == kc - 1) s_t0 = kb;
+        }
+        __syncthreads();
+        const unsigned long long t0h = nb > kc ? s_t0 : 0ull;
+        const int npick = sel.need;
+        const T* rowh = logits + (int64_t)d * row_stride;
+        for (int j = warp; j < npick; j += kWarps) {
+            const int64_t base = (int64_t)(b0 + pick[j]) * kHeadBlock;
+            for (int i = lane; i < kHeadBlock; i += 32) {
+                const unsigned long long k = make_key(to_f32<T>(rowh[base + i]), base + i);
+                if (k >= t0h) {
+                    const int pos = atomicAdd(&sel.count, 1);
+                    if (pos < kHeadCandCap) cand[pos] = k;
+                }
+            }
+        }
+        __syncthreads();
+    } else {
 #pragma unroll
     for (int j = 0; j < kNv; ++j) {
         const int loc = (j * kThreads + tid) * kEpv;
@@ -1020,13 +1105,12 @@ tree_build_kernel(const T* __restrict__ logits, int rows, int64_t vocab, int64_t
         for (int e = 0; e < kEpv; e += 4)
             *reinterpret_cast<float4*>(cv + loc + e) = make_float4(x[e], x[e + 1], x[e + 2], x[e + 3]);
     }
-    auto loc_of = [&](int j) -> int { return ((j / kEpv) * kThreads + tid) * kEpv + (j % kEpv); };
 
     // ---- max and sum of exp (logsumexp pieces, ddtree.py:138) ----------
     // (a slot past the chunk adds exp(-inf) = +0 to the sum: no change)
     // The same pass keeps the thread's largest value and its first index
     // (values run in index order, so the lowest index among equal values).
-    float m = -INFINITY, best = -INFINITY;
+    float best = -INFINITY;
     int bloc = -1;
     bool nan_seen = false;
     DDT_FOR_VALS(x, loc, j, {
@@ -1046,17 +1130,9 @@ tree_build_kernel(const T* __restrict__ logits, int rows, int64_t vocab, int64_t
     if (m != -INFINITY && m == m) {
         DDT_FOR_VALS(x, loc, j, { sum_t += expf(x - m); })
     }
-    const double sum_c = block_sum_d((double)sum_t, red_d);
+    sum_c = block_sum_d((double)sum_t, red_d);
 
     // ---- chunk top-k candidates ----------------------------------------
-    // Keys are (value order, then lower token id) and distinct.  The chunk's
-    // top kc keys go to part_keys in descending order, padded with zeros.
-    const int kc = min(topk, n_valid);
-    const int lane = tid & 31, warp = tid >> 5;
-    auto key_at = [&](int j) -> unsigned long long {   // (the rare radix-select path)
-        const int loc = loc_of(j);
-        return chunk_key(cv[loc], loc, n_valid, c0);
-    };
     // The thread's largest key.  Without NaN it is that of its first largest
     // value (up to the order of +0 and -0, which only lowers it: the bound
     // below stays a lower bound, built from keys the thread holds).
@@ -1069,7 +1145,6 @@ tree_build_kernel(const T* __restrict__ logits, int rows, int64_t vocab, int64_t
             tmax = k > tmax ? k : tmax;
         })
     }
-    unsigned long long* dst = part_keys + ((int64_t)d * chunks + c) * topk;
     if (tid == 0) sel.count = 0;
     __syncthreads();
     // A lower bound t0 on the kc-th largest key: each warp sorts its 32
@@ -1138,6 +1213,7 @@ tree_build_kernel(const T* __restrict__ logits, int rows, int64_t vocab, int64_t
         if (pos < kCandCap) cand[pos] = chunk_key(cv[loc], loc, n_valid, c0);
     }
     __syncthreads();
+    }   // phase A from the logits
     const int ncand = sel.count;
     __syncthreads();
     if (tid == 0) sel.count = 0;
@@ -1152,7 +1228,7 @@ tree_build_kernel(const T* __restrict__ logits, int rows, int64_t vocab, int64_t
     } else {
         // radix select of the kc-th largest, the selected keys into `top`,
         // then ranked among themselves
-        if (ncand <= kCandCap) {
+        if (ncand <= cand_cap) {
             const unsigned long long t1 = block_kth_largest(cand, ncand, kc, &sel);
             for (int i = tid; i < ncand; i += kThreads) {
                 const unsigned long long k = cand[i];
@@ -1386,9 +1462,37 @@ extern "C" size_t ddt_tree_build_workspace_size(int64_t rows, int64_t vocab, int
     return ws_layout(rows, chunks_max, topk).total;
 }
 
+static int tree_build_run(const void* logits, int dtype, int64_t rows, int64_t vocab, int64_t row_stride,
+                          int64_t budget, const int64_t* root_token, int64_t start, const ddt_tree_outputs* out,
+                          void* workspace, size_t workspace_bytes, ddt_stream_t stream,
+                          const unsigned char* hstats);
+
 extern "C" int ddt_tree_build(const void* logits, int dtype, int64_t rows, int64_t vocab, int64_t row_stride,
                               int64_t budget, const int64_t* root_token, int64_t start, const ddt_tree_outputs* out,
                               void* workspace, size_t workspace_bytes, ddt_stream_t stream) {
+    return tree_build_run(logits, dtype, rows, vocab, row_stride, budget, root_token, start, out, workspace,
+                          workspace_bytes, stream, nullptr);
+}
+
+extern "C" int ddt_tree_build_head(const void* logits, int64_t rows, int64_t vocab, int64_t row_stride,
+                                   const void* head_stats, int64_t budget, const int64_t* root_token, int64_t start,
+                                   const ddt_tree_outputs* out, void* workspace, size_t workspace_bytes,
+                                   ddt_stream_t stream) {
+    if (budget > 0 && rows > 0) {
+        if (!head_stats) return set_error(DDT_EINVAL, "head_stats is null");
+        if (vocab % kHeadBlock) return set_error(DDT_EINVAL, "vocab=%lld is not a multiple of %d", (long long)vocab,
+                                                 kHeadBlock);
+        if (reinterpret_cast<uintptr_t>(head_stats) % 256)
+            return set_error(DDT_EINVAL, "head_stats must be 256-byte aligned");
+    }
+    return tree_build_run(logits, DDT_BF16, rows, vocab, row_stride, budget, root_token, start, out, workspace,
+                          workspace_bytes, stream, static_cast<const unsigned char*>(head_stats));
+}
+
+static int tree_build_run(const void* logits, int dtype, int64_t rows, int64_t vocab, int64_t row_stride,
+                          int64_t budget, const int64_t* root_token, int64_t start, const ddt_tree_outputs* out,
+                          void* workspace, size_t workspace_bytes, ddt_stream_t stream,
+                          const unsigned char* hstats) {
     int rc = validate_outputs(out, budget);
     if (rc) return rc;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
@@ -1408,6 +1512,19 @@ extern "C" int ddt_tree_build(const void* logits, int dtype, int64_t rows, int64
     const int64_t topk = budget < vocab ? budget : vocab;
     int64_t chunks, chunk_len;
     choose_chunks(rows, vocab, topk, sms, &chunks, &chunk_len);
+    if (hstats) {
+        // whole 128-row blocks per chunk (never more chunks than above, so
+        // ddt_tree_build_workspace_size covers this mode too); the topk
+        // blocks read from the logits must fit the candidate area
+        const int64_t nblk = vocab / kHeadBlock;
+        const int64_t bpc = ceil_div(nblk, chunks);
+        chunk_len = bpc * kHeadBlock;
+        chunks = ceil_div(nblk, bpc);
+        if (topk * kHeadBlock > kHeadCandCap || bpc > kMaxBudget / 2)
+            return set_error(DDT_EUNSUPPORTED, "ddt_tree_build_head: budget %lld (top-k %lld) or %lld blocks per "
+                             "chunk beyond its limits (%d, %d); use ddt_tree_build", (long long)budget,
+                             (long long)topk, (long long)bpc, kHeadCandCap / kHeadBlock, kMaxBudget / 2);
+    }
     const WsLayout L = ws_layout(rows, chunks, topk);
     if (!workspace || workspace_bytes < L.total)
         return set_error(DDT_EWORKSPACE, "tree build workspace needs %zu bytes, got %zu", L.total, workspace_bytes);
@@ -1424,7 +1541,7 @@ extern "C" int ddt_tree_build(const void* logits, int dtype, int64_t rows, int64
         if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)        \
             return check_launch("cudaFuncSetAttribute(tree_build_kernel)");                                        \
         k<<<grid, kThreads, smem, st>>>(static_cast<const T*>(logits), (int)rows, vocab, row_stride, (int)topk,    \
-                                        (int)chunks, chunk_len, (int)budget, root_token, start, *out, ws);        \
+                                        (int)chunks, chunk_len, (int)budget, root_token, start, *out, ws, hstats); \
     } while (0)
     if (dtype == DDT_F32) {
         if (vec) DDT_LAUNCH_TB(float, true); else DDT_LAUNCH_TB(float, false);

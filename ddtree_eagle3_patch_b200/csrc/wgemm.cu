@@ -73,6 +73,11 @@ struct Cfg {
 struct Params {
     int T, N, nk_total, splits;
     int gate_up;   // interleaved gate/up weight: write act(gate) * up, N / 2 columns
+    // head mode (ddt_wgemm_head): per-block statistics of the rounded
+    // outputs, laid out by head_stats_layout(T, N / 128); null otherwise
+    float* st_m;
+    float* st_s;
+    unsigned long long* st_keys;
     const __nv_bfloat16* residual;
     int64_t r_stride;
     __nv_bfloat16* y;
@@ -239,6 +244,52 @@ wgemm_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUt
                 float v = acc[t];
                 if (p.residual) v += __bfloat162float(p.residual[(int64_t)t * p.r_stride + n]);
                 p.y[(int64_t)t * p.y_stride + n] = __float2bfloat16_rn(v);
+            }
+        }
+        if (p.st_m) {
+            // Head mode: the rounded logits of this block go through the idle
+            // ring, [TP][128]; warp w then takes token rows w, w + 4, ...:
+            // the block's max, its sum of exp(x - max) (in float64, so the
+            // block's 128 terms add no rounding of their own) and its
+            // largest key.
+            float* xs = reinterpret_cast<float*>(smem);
+#pragma unroll
+            for (int t = 0; t < TP; ++t) xs[t * BN + row] = __bfloat162float(__float2bfloat16_rn(acc[t]));
+            __syncthreads();
+            const int nblk = p.N / BN;
+            for (int t = warp; t < p.T; t += kThreads / 32) {
+                float v[BN / 32];
+                unsigned long long kmax = 0ull;
+                bool nan = false;
+                float m = -INFINITY;
+#pragma unroll
+                for (int i = 0; i < BN / 32; ++i) {
+                    v[i] = xs[t * BN + lane + 32 * i];
+                    const unsigned long long k = topk_key(v[i], (int64_t)n0 + lane + 32 * i);
+                    kmax = k > kmax ? k : kmax;
+                    nan |= v[i] != v[i];
+                    m = fmaxf(m, v[i]);
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    m = fmaxf(m, __shfl_xor_sync(DDT_FULL_MASK, m, o));
+                    const unsigned long long q = __shfl_xor_sync(DDT_FULL_MASK, kmax, o);
+                    kmax = q > kmax ? q : kmax;
+                }
+                nan = __any_sync(DDT_FULL_MASK, nan);
+                double s = 0.0;
+                if (!nan && m != -INFINITY) {
+#pragma unroll
+                    for (int i = 0; i < BN / 32; ++i) s += (double)expf(v[i] - m);
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(DDT_FULL_MASK, s, o);
+                }
+                if (lane == 0) {
+                    const int64_t cell = (int64_t)t * nblk + nb;
+                    p.st_m[cell] = nan ? __int_as_float(0x7fc00000) : m;
+                    p.st_s[cell] = (float)s;
+                    p.st_keys[cell] = kmax;
+                }
             }
         }
     } else {
@@ -423,7 +474,8 @@ extern "C" size_t ddt_wgemm_workspace_size(int64_t T, int64_t N, int64_t K) {
 
 static int wgemm_run(const void* x, int64_t x_stride, int64_t T, const void* w, int64_t w_stride, int64_t N,
                      int64_t K, const void* residual, int64_t r_stride, void* y, int64_t y_stride, int gate_up,
-                     int64_t splits_hint, void* workspace, size_t workspace_bytes, ddt_stream_t stream) {
+                     int64_t splits_hint, void* workspace, size_t workspace_bytes, ddt_stream_t stream,
+                     void* stats = nullptr) {
     using namespace ddt::wgemm;
     if (!x || !w || !y) return set_error(DDT_EINVAL, "null argument");
     if (T <= 0 || T > 128) return set_error(DDT_EUNSUPPORTED, "T=%lld outside [1, 128]", (long long)T);
@@ -450,6 +502,7 @@ static int wgemm_run(const void* x, int64_t x_stride, int64_t T, const void* w, 
         splits = (int)(splits_hint < kMaxSplits ? splits_hint : kMaxSplits);
         if (splits > K / BK) splits = (int)(K / BK);
     }
+    if (stats) splits = 1;   // the statistics come from whole blocks
     CUtensorMap tw, tx;
     int rc = make_map_2d(&tw, w, (uint64_t)K, (uint64_t)N, (uint64_t)w_stride * 2, BN);
     if (!rc) rc = make_map_2d(&tx, x, (uint64_t)K, (uint64_t)T, (uint64_t)x_stride * 2, (uint32_t)TP);
@@ -461,6 +514,15 @@ static int wgemm_run(const void* x, int64_t x_stride, int64_t T, const void* w, 
     p.nk_total = (int)(K / BK);
     p.splits = splits;
     p.gate_up = gate_up;
+    p.st_m = p.st_s = nullptr;
+    p.st_keys = nullptr;
+    if (stats) {
+        const HeadStatsLayout h = head_stats_layout(T, N / BN);
+        unsigned char* sb = static_cast<unsigned char*>(stats);
+        p.st_m = reinterpret_cast<float*>(sb + h.m);
+        p.st_s = reinterpret_cast<float*>(sb + h.s);
+        p.st_keys = reinterpret_cast<unsigned long long*>(sb + h.keys);
+    }
     p.residual = static_cast<const __nv_bfloat16*>(residual);
     p.r_stride = r_stride;
     p.y = static_cast<__nv_bfloat16*>(y);
@@ -490,4 +552,19 @@ extern "C" int ddt_wgemm_gate_up(const void* x, int64_t x_stride, int64_t T, con
                                  int64_t splits_hint, void* workspace, size_t workspace_bytes, ddt_stream_t stream) {
     return wgemm_run(x, x_stride, T, w_gate_up, w_stride, N2, K, nullptr, 0, y, y_stride, 1, splits_hint, workspace,
                      workspace_bytes, stream);
+}
+
+extern "C" size_t ddt_wgemm_head_stats_size(int64_t T, int64_t N) {
+    if (T <= 0 || N <= 0) return 256;
+    return ddt::head_stats_layout(T, N / ddt::kHeadBlock).total;
+}
+
+extern "C" int ddt_wgemm_head(const void* x, int64_t x_stride, int64_t T, const void* w, int64_t w_stride, int64_t N,
+                              int64_t K, void* y, int64_t y_stride, void* stats, size_t stats_bytes, void* workspace,
+                              size_t workspace_bytes, ddt_stream_t stream) {
+    if (!stats || reinterpret_cast<uintptr_t>(stats) % 256 || stats_bytes < ddt_wgemm_head_stats_size(T, N))
+        return set_error(DDT_EWORKSPACE, "head statistics need %zu bytes (256-aligned)",
+                         ddt_wgemm_head_stats_size(T, N));
+    return wgemm_run(x, x_stride, T, w, w_stride, N, K, nullptr, 0, y, y_stride, 0, 0, workspace, workspace_bytes,
+                     stream, stats);
 }

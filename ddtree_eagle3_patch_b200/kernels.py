@@ -66,8 +66,11 @@ class DeviceTree:
 
 
 def tree_build(draft_logits: torch.Tensor, budget: int, root_token: torch.Tensor | None = None, start: int = 0,
-               out: DeviceTree | None = None) -> DeviceTree:
-    """Kernel (1) on ``draft_logits`` [rows, vocab] (fp32 / bf16 / fp16)."""
+               out: DeviceTree | None = None, head_stats: torch.Tensor | None = None) -> DeviceTree:
+    """Kernel (1) on ``draft_logits`` [rows, vocab] (fp32 / bf16 / fp16).
+    With ``head_stats`` (from ``wgemm_head`` on the same bf16 logits) it
+    reads the head's block statistics instead of scanning every logit
+    (``ddt_tree_build_head``)."""
     require_cuda(draft_logits, "draft_logits")
     if draft_logits.dim() != 2:
         raise ValueError("draft_logits must be [rows, vocab]")
@@ -85,6 +88,15 @@ def tree_build(draft_logits: torch.Tensor, budget: int, root_token: torch.Tensor
         if root_token.dtype != torch.int64:
             raise TypeError("root_token must be int64")
     o = out.c_outputs()
+    if head_stats is not None:
+        if draft_logits.dtype != torch.bfloat16:
+            raise TypeError("head statistics come with bf16 logits")
+        require_cuda(head_stats, "head_stats")
+        rc = lib.ddt_tree_build_head(ptr(draft_logits), rows, vocab, draft_logits.stride(0), ptr(head_stats),
+                                     int(budget), ptr(root_token), int(start), ctypes.byref(o), ptr(ws), ws.numel(),
+                                     stream_of(dev))
+        check(rc, "ddt_tree_build_head")
+        return out
     rc = lib.ddt_tree_build(ptr(draft_logits), dtype_code(draft_logits.dtype), rows, vocab, draft_logits.stride(0),
                             int(budget), ptr(root_token), int(start), ctypes.byref(o), ptr(ws), ws.numel(),
                             stream_of(dev))
@@ -404,6 +416,33 @@ def wgemm(x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor | None = None
                        0 if residual is None else residual.stride(0), out.data_ptr(), out.stride(0), int(splits),
                        ws.data_ptr(), ws.numel(), _lib.raw_stream(x.device.index))
     check(rc, "ddt_wgemm")
+    return out
+
+
+def head_stats_buffer(rows: int, vocab: int, device: torch.device) -> torch.Tensor:
+    """Scratch for ``wgemm_head``'s block statistics of [rows, vocab] logits."""
+    return torch.empty(_lib.load().ddt_wgemm_head_stats_size(rows, vocab), dtype=torch.uint8, device=device)
+
+
+def wgemm_head(x: torch.Tensor, w: torch.Tensor, stats: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Logits y = x @ w.T of a bias-free lm_head on the weight-streaming GEMM
+    (``ddt_wgemm_head``), with the per-block statistics that
+    ``tree_build(..., head_stats=stats)`` reads written to ``stats`` (from
+    ``head_stats_buffer``).  The logits equal ``wgemm(x, w)``'s."""
+    if not wgemm_supported(x, w):
+        raise ValueError("wgemm_head: unsupported shapes / layout (see wgemm_supported)")
+    T, K = x.shape
+    N = w.shape[0]
+    if out is None:
+        out = torch.empty((T, N), dtype=torch.bfloat16, device=x.device)
+    if out.dtype != torch.bfloat16 or out.stride(1) != 1 or tuple(out.shape) != (T, N):
+        raise ValueError("out must be [T, N] bf16 with contiguous rows")
+    lib = _lib.load()
+    ws = _wgemm_workspace(x.device)
+    rc = lib.ddt_wgemm_head(x.data_ptr(), x.stride(0), T, w.data_ptr(), w.stride(0), N, K, out.data_ptr(),
+                            out.stride(0), stats.data_ptr(), stats.numel(), ws.data_ptr(), ws.numel(),
+                            _lib.raw_stream(x.device.index))
+    check(rc, "ddt_wgemm_head")
     return out
 
 

@@ -96,6 +96,20 @@ DDT_API int ddt_tree_build(const void* logits, int dtype, int64_t rows, int64_t 
                    int64_t budget, const int64_t* root_token /* device scalar, nullable */, int64_t start,
                    const ddt_tree_outputs* out, void* workspace, size_t workspace_bytes, ddt_stream_t stream);
 
+/* ddt_tree_build over bf16 logits written by ddt_wgemm_head, from its block
+ * statistics `head_stats` (same rows and vocab): the row maxima and sums of
+ * exp come from the blocks' pieces, and the top-k from the logits of only
+ * the top-k blocks by their largest key.  Same outputs and workspace as
+ * ddt_tree_build: the same top ids; lp within 2 ulp of the float64
+ * log-softmax (another summation order than ddt_tree_build's, so the two
+ * may differ in the last bits), the tree the expansion of those.  vocab a
+ * multiple of 128, top-k (min(budget, vocab)) at most 80;
+ * DDT_EUNSUPPORTED beyond. */
+DDT_API int ddt_tree_build_head(const void* logits, int64_t rows, int64_t vocab, int64_t row_stride,
+                                const void* head_stats, int64_t budget, const int64_t* root_token, int64_t start,
+                                const ddt_tree_outputs* out, void* workspace, size_t workspace_bytes,
+                                ddt_stream_t stream);
+
 /* ddt_tree_build for callers that cannot allocate device memory.
  * This entry point has no counterpart in the reference.  Some callers of this
  * library cannot call cudaMalloc: a host application whose device memory is
@@ -367,6 +381,18 @@ DDT_API int ddt_wgemm(const void* x, int64_t x_stride, int64_t T, const void* w,
 DDT_API int ddt_wgemm_gate_up(const void* x, int64_t x_stride, int64_t T, const void* w_gate_up, int64_t w_stride,
                               int64_t N2, int64_t K, void* y, int64_t y_stride, int64_t splits, void* workspace,
                               size_t workspace_bytes, ddt_stream_t stream);
+/* The draft's lm_head fused with the first step of the tree build
+ * (ddtree.py:476-485 computes the draft logits, :136-139 their top-k and
+ * log-softmax): ddt_wgemm's y = x w^T (bf16, no residual, no K split),
+ * plus, for every token row t and every block of 128 rows of w (128 vocabulary
+ * entries), the block's max logit, its sum of exp(logit - max) and its
+ * largest (logit, then lower id) key, written to `stats`
+ * (ddt_wgemm_head_stats_size bytes, 256-aligned).  ddt_tree_build_head reads
+ * them instead of scanning the whole logits.  N a multiple of 128. */
+DDT_API size_t ddt_wgemm_head_stats_size(int64_t T, int64_t N);
+DDT_API int ddt_wgemm_head(const void* x, int64_t x_stride, int64_t T, const void* w, int64_t w_stride, int64_t N,
+                           int64_t K, void* y, int64_t y_stride, void* stats, size_t stats_bytes, void* workspace,
+                           size_t workspace_bytes, ddt_stream_t stream);
 
 /* ---------------------------------------------------------------------------
  * EAGLE3 path acceptance.  Replaces evaluate_eagle3_posterior

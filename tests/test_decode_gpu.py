@@ -203,7 +203,7 @@ def test_bf16_decode_identical_across_launch_forms(monkeypatch):
     ids = random_prompt(40, vocab=1024, seed=2, exclude=drf.mask_token_id).to(DEV)
 
     def run(**env):
-        for k in ("DDTREE_PDL", "DDTREE_EAGER", "DDTREE_WGEMM"):
+        for k in ("DDTREE_PDL", "DDTREE_EAGER", "DDTREE_WGEMM", "DDTREE_HEAD_TOPK"):
             monkeypatch.delenv(k, raising=False)
         for k, v in env.items():
             monkeypatch.setenv(k, v)
@@ -212,7 +212,8 @@ def test_bf16_decode_identical_across_launch_forms(monkeypatch):
 
     base = run()
     assert base.graph_rounds > 0
-    for env in ({"DDTREE_PDL": "0"}, {"DDTREE_EAGER": "1"}):
+    # (DDTREE_HEAD_TOPK=1: the draft head fused with the tree build's top-k)
+    for env in ({"DDTREE_PDL": "0"}, {"DDTREE_EAGER": "1"}, {"DDTREE_HEAD_TOPK": "1"}):
         other = run(**env)
         assert other.output_ids.tolist() == base.output_ids.tolist(), env
         assert other.acceptance_lengths == base.acceptance_lengths, env
