@@ -35,6 +35,11 @@
 // up row and the epilogue writes act(gate) * up: the [T, 2I] intermediate is
 // never stored and no separate elementwise kernel runs.
 //
+// Head mode (ddt_wgemm_head, the draft's lm_head): besides the logits, the
+// epilogue leaves per token row and per block of 128 vocabulary rows the
+// block's max, its sum of exp(x - max) and its largest top-k key, which the
+// tree build (ddt_tree_build_head) reads instead of scanning every logit.
+//
 // Launched as a programmatic dependent (ddt_set_pdl), the kernel signals its
 // own dependents at once and its producer puts the first ring stages' weight
 // loads in flight before griddepcontrol.wait: the weights do not depend on
