@@ -17,12 +17,13 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank: int, world: int, port: int, n_prompts: int, out):
+def _worker(rank: int, world: int, port: int, n_prompts: int, out, ready):
     os.environ.update({"RANK": str(rank), "WORLD_SIZE": str(world), "LOCAL_RANK": str(rank),
                        "LOCAL_WORLD_SIZE": str(world), "MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port)})
     from datetime import timedelta
     from ddtree_eagle3_patch_b200 import distributed as dist
-    dist.init(backend="gloo", timeout=timedelta(seconds=60))
+    ready.wait(timeout=300)   # both ranks imported: the rendezvous does not wait on a cold import
+    dist.init(backend="gloo", timeout=timedelta(seconds=300))
     try:
         mine = list(dist.shard_indices(n_prompts))
         # per-prompt "results": accepted lengths derived from the prompt index
@@ -41,7 +42,8 @@ def test_sharding_gather_and_counters(n_prompts):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, WORLD, port, n_prompts, q)) for r in range(WORLD)]
+    ready = ctx.Barrier(WORLD)
+    procs = [ctx.Process(target=_worker, args=(r, WORLD, port, n_prompts, q, ready)) for r in range(WORLD)]
     for p in procs:
         p.start()
     results = {}
@@ -87,12 +89,13 @@ def test_single_process_fallbacks(monkeypatch):
         dist.shard_indices(5, rank_=2, size_=2)
 
 
-def _counter_worker(rank: int, world: int, port: int, out):
+def _counter_worker(rank: int, world: int, port: int, out, ready):
     os.environ.update({"RANK": str(rank), "WORLD_SIZE": str(world), "LOCAL_RANK": str(rank),
                        "MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port)})
     from datetime import timedelta
     from ddtree_eagle3_patch_b200 import distributed as dist
-    dist.init(backend="gloo", timeout=timedelta(seconds=60))
+    ready.wait(timeout=300)   # both ranks imported: the rendezvous does not wait on a cold import
+    dist.init(backend="gloo", timeout=timedelta(seconds=300))
     try:
         # tokens, rounds, seconds: one fixed-size vector per rank
         m = dist.gather_counters([100.0 * (rank + 1), 10.0 + rank, 0.5 * (rank + 1)])
@@ -107,7 +110,8 @@ def test_gather_counters_one_collective():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_counter_worker, args=(r, WORLD, port, q)) for r in range(WORLD)]
+    ready = ctx.Barrier(WORLD)
+    procs = [ctx.Process(target=_counter_worker, args=(r, WORLD, port, q, ready)) for r in range(WORLD)]
     for p in procs:
         p.start()
     got = dict(q.get(timeout=300) for _ in range(WORLD))
@@ -130,7 +134,12 @@ def _failing_worker(rank: int, world: int, port: int, mode: str, out, ready):
     # both ranks have imported everything before the rendezvous starts, so
     # the short timeout below measures the failure, not a slow import
     ready.wait(timeout=300)
-    dist.init(backend="gloo", timeout=timedelta(seconds=3))
+    try:
+        dist.init(backend="gloo", timeout=timedelta(seconds=3))
+    except Exception:                            # noqa: BLE001 - a loaded host missed the short rendezvous
+        if rank == 0:
+            out.put(("set-up failed", 0.0))
+        os._exit(0)
     t0 = time.perf_counter()
     try:
         dist.gather_counters([1.0, 2.0])        # step 1 on both ranks
@@ -154,17 +163,22 @@ def _failing_worker(rank: int, world: int, port: int, mode: str, out, ready):
 @pytest.mark.parametrize("mode", ["exit", "raise", "stall"])
 def test_failed_rank_is_detected_by_the_next_collective(mode):
     ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _free_port()
-    ready = ctx.Barrier(WORLD)
-    procs = [ctx.Process(target=_failing_worker, args=(r, WORLD, port, mode, q, ready)) for r in range(WORLD)]
-    for p in procs:
-        p.start()
-    kind, waited = q.get(timeout=360)   # cold imports in a fresh container take minutes
-    for p in procs:
-        p.join(timeout=5)
-        if p.is_alive():
-            p.kill()
+    # the group's short timeout also bounds its set-up: on a loaded host a
+    # missed rendezvous is reported as such and the scenario starts over
+    for _attempt in range(3):
+        q = ctx.Queue()
+        port = _free_port()
+        ready = ctx.Barrier(WORLD)
+        procs = [ctx.Process(target=_failing_worker, args=(r, WORLD, port, mode, q, ready)) for r in range(WORLD)]
+        for p in procs:
+            p.start()
+        kind, waited = q.get(timeout=360)   # cold imports in a fresh container take minutes
+        for p in procs:
             p.join(timeout=5)
-    assert kind != "no error"
+            if p.is_alive():
+                p.kill()
+                p.join(timeout=5)
+        if kind != "set-up failed":
+            break
+    assert kind not in ("no error", "set-up failed")
     assert waited < 30.0, waited
